@@ -1,0 +1,390 @@
+"""MatMulNBits INT4 decode benchmark on B200 (one JSON line on rank 0).
+
+Workload: the 7B-shaped decode GEMV sweep at M=1, block_size 128,
+fp32 A ~ N(0,1), packed uint4 zero points, fp32 scales U[0.001, 0.01], shapes (K, N) =
+(4096, 4096), (4096, 1024), (4096, 14336), (14336, 4096), (4096, 32000). One step = one
+MatMulNBits op per shape (5 ops, 144 216 064 algorithmic bytes: weights + scales + zero
+points as the reference stores them). Value = algorithmic GB/s over all ranks.
+
+* value     inputs resident in HBM; each step is one CUDA-graph replay of the 5 launches;
+            4 weight replicas rotate so the 577 MB working set exceeds the 126 MB L2.
+* e2e       the same ops through the C-ABI host-buffer entry (msq_matmul_host): pinned host
+            A copied in and Y copied out inside the timed region, synchronous per op.
+* roofline  the decode GEMV kernel: algorithmic bytes / its CUDA-event launch duration vs
+            the measured HBM copy bandwidth (MEASURED_PEAKS.json).
+* cpu_baseline  the reference's own ms_qgemm_nbits (oracle/_ref, built from the reference
+            sources) on this host's cores over whole sweeps for ~10 s.
+
+--impl reference times that reference CPU kernel as the arm itself (rank 0 only).
+Multi-GPU (torchrun): every rank runs its own copy of the sweep (weak scaling, no
+collective); timing is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+SWEEP = [(4096, 4096), (4096, 1024), (4096, 14336), (14336, 4096), (4096, 32000)]  # (K, N)
+BS = 128
+SCALE_LO, SCALE_HI = 0.001, 0.01
+REPLICAS = 4
+METRIC = "MatMulNBits INT4 M=1 HBM GB/s"
+WORKLOAD = ("7B decode GEMV sweep (BASELINE configs[1]) at M=1: (K,N) = (4096,4096), (4096,1024), "
+            "(4096,14336), (14336,4096), (4096,32000); bits=4, block_size=128, packed zero points, fp32 A and "
+            "scales")
+FALLBACK_HBM_GBS = 6650.0
+# dram bytes per algorithmic byte of the decode GEMV, from the ncu capture summarised in
+# profiles/gemv_q4_decode_7b.md (None until a capture exists).
+NCU_DRAM_PER_ALG_BYTE = None
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def make_cases(seed0: int = 0):
+    from modelsharp_b200 import synth
+    return [synth.make_case(seed0 + i, 1, N, K, 4, BS, "packed", a_dist="normal",
+                            scale_lo=SCALE_LO, scale_hi=SCALE_HI) for i, (K, N) in enumerate(SWEEP)]
+
+
+def step_bytes() -> int:
+    from modelsharp_b200 import synth
+    return sum(synth.algorithmic_bytes(N, K, 4, BS, "packed") for K, N in SWEEP)
+
+
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+# ---------------------------------------------------------------- clocks (NVML, in-process)
+class ClockSampler:
+    """Samples SM clock and throttle reasons every ~2 ms on a background thread."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, index: int):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._h = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # no NVML: report nothing rather than guess
+            log(f"clock sampling unavailable: {e}")
+
+    def _sample(self):
+        nv = self._nv
+        self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+        r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+        for bit, name in self.REASONS.items():
+            if r & bit and name != "gpu_idle":
+                self.reasons.add(name)
+
+    def _run(self):
+        while not self._stop.is_set():
+            self._sample()
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self._h is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._h is not None:
+            self._stop.set()
+            self._t.join()
+            self._sample()
+
+    def summary(self):
+        if not self.samples:
+            return None
+        return {"sm_mhz": float(statistics.median(self.samples)), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------- CPU reference timing
+def time_reference_sweep(cases, budget_s: float, min_reps: int = 2):
+    """Whole sweeps of the reference's ms_qgemm_nbits on all host cores; returns (median s, reps, kind)."""
+    from oracle import oracle
+    if oracle.reference_available():
+        fn, kind = oracle.reference_native, "reference"
+    else:
+        fn, kind = oracle.managed, "port"
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < min_reps or time.perf_counter() < t_end:
+        t0 = time.perf_counter()
+        for c in cases:
+            fn(c)
+        times.append(time.perf_counter() - t0)
+        if len(times) >= 1000:
+            break
+    return statistics.median(times), len(times), kind
+
+
+def run_reference_arm(args, rank: int, world: int):
+    if rank != 0:
+        return
+    cases = make_cases()
+    nbytes = step_bytes()
+    from oracle import oracle
+    kind = "reference" if oracle.reference_available() else "port"
+    fn = oracle.reference_native if kind == "reference" else oracle.managed
+    for _ in range(max(args.warmup, 1)):
+        for c in cases:
+            fn(c)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for c in cases:
+            fn(c)
+    dt = time.perf_counter() - t0
+    value = nbytes * args.steps / dt / 1e9
+    cores = os.cpu_count()
+    out = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "bytes_per_step": nbytes},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": kind,
+                         "sample": f"{args.steps} whole sweeps of ms_qgemm_nbits, OpenMP over all {cores} host "
+                                   "threads (native/src/qgemm.cpp built from the reference sources)"
+                         if kind == "reference" else f"{args.steps} whole sweeps of the C restatement"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+
+
+# ---------------------------------------------------------------- GPU arm
+def run_ours(args, rank: int, world: int, local_rank: int):
+    import torch
+    import torch.distributed as dist
+
+    from modelsharp_b200 import QuantizedWeights
+    from modelsharp_b200 import _native as N
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    lib = N.lib()
+    nbytes = step_bytes()
+    cases = make_cases()
+
+    # Device-resident weights: REPLICAS independent packs of each shape.
+    stream = torch.cuda.Stream(dev)
+    reps = []
+    for r in range(REPLICAS):
+        reps.append([QuantizedWeights(c["b"], c["scales"], c["zp"], c["N"], c["K"], 4, BS, device=dev)
+                     for c in cases])
+    a_dev = [torch.from_numpy(c["a"]).to(dev) for c in cases]
+    y_dev = [torch.empty(1, c["N"], device=dev) for c in cases]
+    torch.cuda.synchronize(dev)
+    sptr = stream.cuda_stream
+
+    def launch_step(r: int):
+        for w, a, y, c in zip(reps[r], a_dev, y_dev, cases):
+            rc = lib.msq_matmul(None, sptr, w.handle, a.data_ptr(), N.DT_F32, 1, y.data_ptr(), c["N"])
+            if rc:
+                N.check(rc)
+
+    # Warm-up (also sets kernel attributes before capture), then one graph per replica.
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            launch_step(i % REPLICAS)
+    stream.synchronize()
+    path = N.last_path()
+    graphs = []
+    launches_before = N.launch_count()
+    for r in range(REPLICAS):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            launch_step(r)
+        graphs.append(g)
+    launches_per_step = (N.launch_count() - launches_before) // REPLICAS
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            graphs[i % REPLICAS].replay()
+    stream.synchronize()
+
+    # Parity spot check of this exact data (not timed).
+    y_chk = [y.cpu().numpy() for y in y_dev]
+
+    # ---- timed region: K graph replays
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        ev0.record(stream)
+        with torch.cuda.stream(stream):
+            for i in range(args.steps):
+                graphs[i % REPLICAS].replay()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * nbytes * args.steps / (ms * 1e-3) / 1e9
+
+    # ---- roofline: per-launch CUDA events on the launching stream, same kernels
+    per_shape = []
+    tot_bytes, tot_ms = 0, 0.0
+    from modelsharp_b200 import synth
+    with torch.cuda.stream(stream):
+        for si, c in enumerate(cases):
+            b = synth.algorithmic_bytes(c["N"], c["K"], 4, BS, "packed")
+            evs = []
+            for it in range(4 * REPLICAS):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                w = reps[it % REPLICAS][si]
+                e0.record(stream)
+                lib.msq_matmul(None, sptr, w.handle, a_dev[si].data_ptr(), N.DT_F32, 1, y_dev[si].data_ptr(), c["N"])
+                e1.record(stream)
+                evs.append((e0, e1))
+            stream.synchronize()
+            d = [e0.elapsed_time(e1) for e0, e1 in evs[REPLICAS:]]
+            avg = sum(d) / len(d)
+            per_shape.append({"K": c["K"], "N": c["N"], "bytes": b, "us": avg * 1e3, "GB/s": b / (avg * 1e-3) / 1e9})
+            tot_bytes += b
+            tot_ms += avg
+    peak, peak_kind = peaks()
+    achieved = tot_bytes / (tot_ms * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": (NCU_DRAM_PER_ALG_BYTE * tot_bytes / len(cases)) if NCU_DRAM_PER_ALG_BYTE else None,
+                "peak_source": f"{peak_kind} HBM copy bandwidth", "kernel": path,
+                "bytes_per_launch": tot_bytes / len(cases), "per_shape": per_shape}
+
+    # ---- e2e: host buffers through the C ABI, copies inside the timed region
+    a_host = [torch.from_numpy(c["a"]).pin_memory() for c in cases]
+    y_host = [torch.empty(1, c["N"]).pin_memory() for c in cases]
+    h2d = sum(a.numel() * 4 for a in a_host)
+    d2h = sum(y.numel() * 4 for y in y_host)
+    e2e_steps = max(1, min(args.steps, 2000))
+
+    def e2e_step(r: int):
+        for w, a, y in zip(reps[r], a_host, y_host):
+            rc = lib.msq_matmul_host(None, sptr, w.handle, a.data_ptr(), N.DT_F32, 1, y.data_ptr())
+            if rc:
+                N.check(rc)
+
+    for i in range(max(args.warmup, 3)):
+        e2e_step(i % REPLICAS)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(e2e_steps):
+        e2e_step(i % REPLICAS)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * nbytes * e2e_steps / (e2e_ms * 1e-3) / 1e9
+    e2e_ok = all(np.array_equal(y.numpy(), yc) for y, yc in zip(y_host, y_chk))
+
+    # ---- parity spot check + CPU baseline (rank 0, N = 1)
+    cpu = None
+    parity = None
+    if rank == 0:
+        from oracle import oracle
+        parity = max(oracle.rel_l2(y, oracle.managed(c)) for y, c in zip(y_chk, cases))
+        if world == 1:
+            med, reps_done, kind = time_reference_sweep(cases, budget_s=args.cpu_seconds)
+            cores = os.cpu_count()
+            cpu = {"value": nbytes / med / 1e9, "unit": "GB/s", "cores": cores, "kind": kind,
+                   "sample": f"{reps_done} whole sweeps (5 ops, {nbytes} B each), median, OpenMP over all "
+                             f"{cores} host threads"}
+
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "bytes_per_step": nbytes, "weights": "u4 (int4 codes)",
+                       "l2": f"inputs larger than L2: {REPLICAS} weight replicas rotate, "
+                             f"{REPLICAS * nbytes / 1e6:.0f} MB working set vs 126 MB L2",
+                       "launch": "one CUDA graph replay per step", "parity_rel_l2": parity,
+                       "parallelism": f"replicas{world}"},
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "steps": e2e_steps, "entry": "msq_matmul_host", "matches_device_run": e2e_ok},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(out), flush=True)
+    for g in graphs:
+        del g
+    for rr in reps:
+        for w in rr:
+            w.free()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,140 @@
+/*
+ * ms_cuda_nbits.h -- C ABI of the B200 (sm_100a) MatMulNBits backend, libms_cuda_nbits.so.
+ *
+ * Operator: com.microsoft.MatMulNBits, Y[M,N] = A[M,K] . dequant(B)^T with
+ *   W[n,k] = (q[n,k] - zp[n, k/bs]) * scale[n, k/bs]
+ * in the layouts of ModelSharp's reference kernel
+ * (src/ModelSharp/Cpu/Kernels/Quantize/MatMulNBitsKernel.cs:21-42):
+ *   B       uint8 [N, ceil(K/bs), ceil(bs*bits/8)], low nibble = even k
+ *   scales  [N * ceil(K/bs)], float32 / float16 / bfloat16 (widened exactly)
+ *   zp      absent (2^(bits-1)), uint8 packed n-bit with row stride
+ *           ceil(ceil(K/bs)*bits/8), or float32 [N * ceil(K/bs)]
+ *
+ * Conventions follow native/ms_kernels.h:10-13 (row-major, caller-owned pointers,
+ * outputs fully overwritten) and the context-aware CUDA entry of
+ * native/src/cublas_gemm.cu:624-681 (an int status; an optional CUcontext that is
+ * pushed for the call; an optional CUstream; enqueue-only device entries).
+ * Every entry returns MSQ_OK (0) or a negative MSQ_E_* code and never aborts the
+ * process; msq_last_error() then holds the message, worded as the reference's
+ * ModelSharpException for validation failures (MatMulNBitsKernel.cs:87-161).
+ *
+ * Pointers named d_* are device pointers of the current (or given) context; others
+ * are host pointers. cu_ctx may be NULL (use the calling thread's current context,
+ * or the primary context of the current device); stream may be NULL (legacy default).
+ */
+#pragma once
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes --------------------------------------------------------------- */
+#define MSQ_OK              0
+#define MSQ_E_INVALID      -1  /* shape / attribute / argument validation failed     */
+#define MSQ_E_UNSUPPORTED  -2  /* valid for the op but not implemented (g_idx perm)   */
+#define MSQ_E_CUDA         -3  /* CUDA runtime or driver error                        */
+#define MSQ_E_NO_DEVICE    -4  /* no compute-capability 10.x device visible           */
+#define MSQ_E_OOM          -5  /* device allocation failed                            */
+
+/* ---- element types (ModelSharp ElementType, src/ModelSharp/Tensors/ElementType.cs:4-15) */
+#define MSQ_DT_ABSENT  -1
+#define MSQ_DT_F32      1
+#define MSQ_DT_F64      2
+#define MSQ_DT_F16      3
+#define MSQ_DT_I32      4
+#define MSQ_DT_I64      5
+#define MSQ_DT_I8       6
+#define MSQ_DT_U8       7
+#define MSQ_DT_BOOL     8
+#define MSQ_DT_BF16    16  /* not an ElementType: the loader widens bf16 (OnnxModelLoader.cs:410) */
+
+/* ---- kernel path selection (msq_matmul_ex) -------------------------------------- */
+#define MSQ_PATH_AUTO     0  /* M<=16 -> decode GEMV, M>=17 -> tcgen05 GEMM, else generic */
+#define MSQ_PATH_GENERIC  1  /* any bits / block size / zero-point form, reference layout  */
+#define MSQ_PATH_GEMV     2  /* bits=4, block_size a power of two >= 32                   */
+#define MSQ_PATH_GEMM     3  /* bits=4, block_size a power of two >= 32, tcgen05 + TMEM   */
+
+/* ---- msq_pack flags ----------------------------------------------------------------- */
+#define MSQ_PACK_DEFAULT       0
+#define MSQ_PACK_GENERIC_ONLY  1  /* keep only the reference layout (exercise the generic kernel) */
+
+/* ---- capability / info (ms_kernels.h:23-25, NativeCuda.cs:204-206) ------------------ */
+const char* msq_build_info(void);      /* nvcc version, target arch, build date            */
+int         msq_available(void);       /* 1 if a CC 10.x device is visible and usable      */
+const char* msq_last_error(void);      /* message of this thread's last failing call       */
+int64_t     msq_launch_count(void);    /* kernels launched by this library (process-wide)  */
+const char* msq_last_path(void);       /* kernel path of this thread's last matmul         */
+
+/* ---- validation only: no device work (MatMulNBitsKernel.cs:82-164) ------------------
+ * Checks the attributes N, K, bits, block_size, the element counts of B / scales /
+ * zero_points, the zero-point dtype, an optional g_idx (identity only), and A's shape
+ * (a_dims[a_rank], last dim == K). On success writes M = product of A's leading dims.
+ * zp_dtype is MSQ_DT_ABSENT when the input is missing.                                 */
+int msq_check_node(int N, int K, int bits, int block_size,
+                   int64_t b_len, int64_t scales_len,
+                   int zp_dtype, int64_t zp_len,
+                   const int64_t* g_idx, int64_t g_idx_len,
+                   const int64_t* a_dims, int a_rank,
+                   int64_t* M_out);
+
+/* ---- device-resident weights (IlgpuEngine.cs:2218-2229 residency, repacked) ----------
+ * Repacks the reference-layout B / scales / zero_points (device pointers) into the
+ * kernel layout, keeping rows [n_begin, n_end) of the N weight rows (0, N for all; a
+ * sub-range is the column shard of an N-split). The source buffers may be freed after
+ * the stream has passed this call.                                                      */
+typedef struct msq_weights_s* msq_weights_t;
+
+int msq_pack(void* cu_ctx, void* stream,
+             const uint8_t* d_b, int64_t b_len,
+             const void* d_scales, int scales_dtype, int64_t scales_len,
+             const void* d_zp, int zp_dtype, int64_t zp_len,
+             int N, int K, int bits, int block_size,
+             int n_begin, int n_end, int flags,
+             msq_weights_t* out);
+
+/* Same from host memory: uploads, repacks and synchronizes the stream. */
+int msq_pack_host(void* cu_ctx, void* stream,
+                  const uint8_t* b, int64_t b_len,
+                  const void* scales, int scales_dtype, int64_t scales_len,
+                  const void* zp, int zp_dtype, int64_t zp_len,
+                  int N, int K, int bits, int block_size,
+                  int n_begin, int n_end, int flags,
+                  msq_weights_t* out);
+
+/* Rows, K, bits, block size and device bytes held by a handle (any pointer may be NULL). */
+int msq_weights_query(msq_weights_t w, int* n_rows, int* K, int* bits, int* block_size,
+                      int64_t* device_bytes);
+
+/* Frees the handle's device memory (after the work queued on it has completed). */
+int msq_free(msq_weights_t w);
+
+/* ---- compute (GpuKernels.cs:578-626 launched at IlgpuEngine.cs:2231) -----------------
+ * Y[m, j] = sum_k A[m, k] * W[n_begin + j, k] for m < M, j < n_rows; Y row stride ldy
+ * (>= n_rows, in floats) so a column shard can write straight into a wider Y. A is
+ * row-major [M, K], float32 / float16 / bfloat16. Enqueued on `stream`; the caller
+ * synchronizes.                                                                         */
+int msq_matmul(void* cu_ctx, void* stream, msq_weights_t w,
+               const void* d_a, int a_dtype, int64_t M,
+               float* d_y, int64_t ldy);
+
+/* msq_matmul with an explicit kernel path (MSQ_PATH_*). */
+int msq_matmul_ex(void* cu_ctx, void* stream, msq_weights_t w,
+                  const void* d_a, int a_dtype, int64_t M,
+                  float* d_y, int64_t ldy, int path);
+
+/* Host-buffer form (NativeQuant.TryMatMulNBits, NativeQuant.cs:78-115): copies A in,
+ * runs, copies Y [M, n_rows] out and synchronizes the stream.                          */
+int msq_matmul_host(void* cu_ctx, void* stream, msq_weights_t w,
+                    const void* a, int a_dtype, int64_t M, float* y);
+
+/* ---- one-shot drop-in for ms_qgemm_nbits (native/ms_kernels.h:42-44) -----------------
+ * Host pointers, fp32 A / scales, packed or NULL zero points; uploads, runs on the
+ * current device and downloads per call. Returns a status where the original is void. */
+int msq_qgemm_nbits(const float* a, const uint8_t* bq, const float* scales,
+                    const uint8_t* zero_points, float* y,
+                    int M, int N, int K, int bits, int block_size);
+
+#ifdef __cplusplus
+}
+#endif

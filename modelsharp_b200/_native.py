@@ -1,0 +1,104 @@
+"""ctypes binding of libms_cuda_nbits.so (include/ms_cuda_nbits.h).
+
+Library resolution mirrors the reference's DllImport resolver
+(src/ModelSharp/Native/NativeGemm.cs:235-253, NativeCuda.cs:182-200): an explicit path in
+MODELSHARP_CUDA_NBITS_LIB first, then the in-tree build next to this file. There is no
+fallback: a missing library raises, because this op has no CPU or library path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+from .errors import ModelSharpException
+
+MSQ_OK = 0
+MSQ_E_INVALID = -1
+MSQ_E_UNSUPPORTED = -2
+MSQ_E_CUDA = -3
+MSQ_E_NO_DEVICE = -4
+MSQ_E_OOM = -5
+
+# ElementType codes (src/ModelSharp/Tensors/ElementType.cs:4-15) plus bf16.
+DT_ABSENT, DT_F32, DT_F64, DT_F16, DT_I32, DT_I64, DT_I8, DT_U8, DT_BOOL, DT_BF16 = -1, 1, 2, 3, 4, 5, 6, 7, 8, 16
+
+PATH_AUTO, PATH_GENERIC, PATH_GEMV, PATH_GEMM = 0, 1, 2, 3
+PACK_DEFAULT, PACK_GENERIC_ONLY = 0, 1
+
+LIB_NAME = "libms_cuda_nbits.so"
+HEADER = Path(__file__).resolve().parent.parent / "include" / "ms_cuda_nbits.h"
+
+_vp = C.c_void_p
+_i64 = C.c_int64
+_i32 = C.c_int
+
+# name -> (restype, argtypes); every function the header declares.
+SIGNATURES: dict[str, tuple] = {
+    "msq_build_info": (C.c_char_p, []),
+    "msq_available": (_i32, []),
+    "msq_last_error": (C.c_char_p, []),
+    "msq_launch_count": (_i64, []),
+    "msq_last_path": (C.c_char_p, []),
+    "msq_check_node": (_i32, [_i32, _i32, _i32, _i32, _i64, _i64, _i32, _i64, _vp, _i64, _vp, _i32, _vp]),
+    "msq_pack": (_i32, [_vp, _vp, _vp, _i64, _vp, _i32, _i64, _vp, _i32, _i64, _i32, _i32, _i32, _i32,
+                        _i32, _i32, _i32, _vp]),
+    "msq_pack_host": (_i32, [_vp, _vp, _vp, _i64, _vp, _i32, _i64, _vp, _i32, _i64, _i32, _i32, _i32, _i32,
+                             _i32, _i32, _i32, _vp]),
+    "msq_weights_query": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp]),
+    "msq_free": (_i32, [_vp]),
+    "msq_matmul": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp, _i64]),
+    "msq_matmul_ex": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp, _i64, _i32]),
+    "msq_matmul_host": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp]),
+    "msq_qgemm_nbits": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32]),
+}
+
+_lib: C.CDLL | None = None
+
+
+def library_path() -> Path:
+    env = os.environ.get("MODELSHARP_CUDA_NBITS_LIB")
+    if env:
+        return Path(env)
+    return Path(__file__).resolve().parent / LIB_NAME
+
+
+def lib() -> C.CDLL:
+    """The loaded library; raises ModelSharpException when it is missing."""
+    global _lib
+    if _lib is None:
+        p = library_path()
+        if not p.exists():
+            raise ModelSharpException(
+                f"{LIB_NAME} not found at {p}; build it with `python -m modelsharp_b200.build` "
+                "(MatMulNBits has no CPU fallback on this backend).")
+        L = C.CDLL(str(p))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return (lib().msq_last_error() or b"").decode("utf-8", "replace")
+
+
+def check(rc: int, what: str = "") -> None:
+    """Raises ModelSharpException with the library's message for a non-zero status."""
+    if rc != MSQ_OK:
+        msg = last_error() or f"{what} failed with status {rc}"
+        raise ModelSharpException(msg, status=rc)
+
+
+def launch_count() -> int:
+    return int(lib().msq_launch_count())
+
+
+def last_path() -> str:
+    return (lib().msq_last_path() or b"").decode()
+
+
+def available() -> bool:
+    return bool(lib().msq_available())

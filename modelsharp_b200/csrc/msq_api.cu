@@ -1,0 +1,462 @@
+// C ABI of libms_cuda_nbits.so (declared in include/ms_cuda_nbits.h).
+//
+// Host-side runtime around the kernels: argument validation with the reference's
+// messages (MatMulNBitsKernel.cs:82-164), device-resident weight handles (the
+// residency role of IlgpuEngine.cs:2218-2229 / 3392-3429), kernel-path dispatch, the
+// host-buffer and one-shot forms, context push/pop for caller-supplied driver contexts
+// (the pattern of native/src/cublas_gemm.cu:505-528), and diagnostics counters
+// (NativeCuda.cs:147-150).
+#include "msq_internal.cuh"
+
+#include <cuda.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+namespace msq {
+namespace {
+
+thread_local std::string t_last_error;
+thread_local const char* t_last_path = "";
+std::atomic<int64_t> g_launches{0};
+
+using PFN_push = CUresult (*)(CUcontext);
+using PFN_pop = CUresult (*)(CUcontext*);
+PFN_push g_push = nullptr;
+PFN_pop g_pop = nullptr;
+std::once_flag g_driver_once;
+
+void load_driver_entries() {
+  std::call_once(g_driver_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxPushCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_push = reinterpret_cast<PFN_push>(fn);
+    fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxPopCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_pop = reinterpret_cast<PFN_pop>(fn);
+  });
+}
+
+// Pushes a caller-supplied driver context for the duration of one C-ABI call.
+struct CtxGuard {
+  bool pushed = false;
+  int rc = MSQ_OK;
+  explicit CtxGuard(void* ctx) {
+    if (!ctx) return;
+    load_driver_entries();
+    if (!g_push || !g_pop) {
+      rc = fail(MSQ_E_CUDA, "cannot resolve cuCtxPushCurrent/cuCtxPopCurrent");
+      return;
+    }
+    if (g_push(static_cast<CUcontext>(ctx)) != CUDA_SUCCESS) {
+      rc = fail(MSQ_E_CUDA, "cuCtxPushCurrent failed");
+      return;
+    }
+    pushed = true;
+  }
+  ~CtxGuard() {
+    if (pushed) {
+      CUcontext c;
+      g_pop(&c);
+    }
+  }
+};
+
+const char* dtype_name(int dt) {
+  switch (dt) {
+    case MSQ_DT_F32: return "Float32";
+    case MSQ_DT_F64: return "Float64";
+    case MSQ_DT_F16: return "Float16";
+    case MSQ_DT_I32: return "Int32";
+    case MSQ_DT_I64: return "Int64";
+    case MSQ_DT_I8: return "Int8";
+    case MSQ_DT_U8: return "UInt8";
+    case MSQ_DT_BOOL: return "Boolean";
+    case MSQ_DT_BF16: return "BFloat16";
+    default: return "Unknown";
+  }
+}
+
+bool is_float_act(int dt) { return dt == MSQ_DT_F32 || dt == MSQ_DT_F16 || dt == MSQ_DT_BF16; }
+
+bool pow2(int v) { return v > 0 && (v & (v - 1)) == 0; }
+
+// Static shape checks shared by msq_check_node and msq_pack (MatMulNBitsKernel.cs:87-145).
+int check_weights(int N, int K, int bits, int bs, int64_t b_len, int64_t scales_len, int scales_dtype,
+                  int zp_dtype, int64_t zp_len) {
+  if (N <= 0 || K <= 0)
+    return fail(MSQ_E_INVALID, "MatMulNBits requires positive N and K attributes (got N=%d, K=%d).", N, K);
+  if (bits != 4 && bits != 8)
+    return fail(MSQ_E_INVALID, "MatMulNBits supports bits=4 or bits=8; got %d.", bits);
+  if (bs <= 0) return fail(MSQ_E_INVALID, "MatMulNBits requires a positive block_size; got %d.", bs);
+  const int64_t nb = ((int64_t)K + bs - 1) / bs;
+  const int64_t blob = ((int64_t)bs * bits + 7) / 8;
+  const int64_t expected_b = (int64_t)N * nb * blob;
+  if (b_len != expected_b)
+    return fail(MSQ_E_INVALID,
+                "MatMulNBits B has %lld elements; expected %lld (N=%d \xC3\x97 n_blocks_per_row=%lld "
+                "\xC3\x97 blob_size=%lld).",
+                (long long)b_len, (long long)expected_b, N, (long long)nb, (long long)blob);
+  if (!is_float_act(scales_dtype))
+    return fail(MSQ_E_INVALID, "MatMulNBits scales must be Float32 or Float16; got %s.", dtype_name(scales_dtype));
+  const int64_t expected_scales = (int64_t)N * nb;
+  if (scales_len != expected_scales)
+    return fail(MSQ_E_INVALID,
+                "MatMulNBits scales has %lld elements; expected %lld (N=%d \xC3\x97 n_blocks_per_row=%lld).",
+                (long long)scales_len, (long long)expected_scales, N, (long long)nb);
+  const int64_t zp_row = (nb * bits + 7) / 8;
+  if (zp_dtype == MSQ_DT_ABSENT) return MSQ_OK;
+  if (zp_dtype == MSQ_DT_F32) {
+    if (zp_len != expected_scales)
+      return fail(MSQ_E_INVALID, "MatMulNBits float zero_points has %lld elements; expected %lld.",
+                  (long long)zp_len, (long long)expected_scales);
+  } else if (zp_dtype == MSQ_DT_U8) {
+    const int64_t expected_zp = (int64_t)N * zp_row;
+    if (zp_len != expected_zp)
+      return fail(MSQ_E_INVALID, "MatMulNBits packed zero_points has %lld bytes; expected %lld (N=%d \xC3\x97 %lld).",
+                  (long long)zp_len, (long long)expected_zp, N, (long long)zp_row);
+  } else {
+    return fail(MSQ_E_INVALID, "MatMulNBits zero_points must be Float32 or UInt8; got %s.", dtype_name(zp_dtype));
+  }
+  return MSQ_OK;
+}
+
+int current_device(int* dev) {
+  cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  return MSQ_OK;
+}
+
+template <typename T>
+int dev_alloc(T** p, size_t n, int64_t* total) {
+  *p = nullptr;
+  if (n == 0) return MSQ_OK;
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), n * sizeof(T));
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(MSQ_E_OOM, "device allocation of %zu bytes failed: %s", n * sizeof(T), cudaGetErrorString(e));
+  }
+  *total += (int64_t)(n * sizeof(T));
+  return MSQ_OK;
+}
+
+void free_weights(Weights* w) {
+  if (!w) return;
+  release_gemm_state(*w);
+  void* ptrs[] = {w->nib, w->sc, w->sc16, w->zp4, w->zpf, w->b_ref, w->sc_ref, w->zp_ref_u8, w->zp_ref_f32};
+  for (void* p : ptrs)
+    if (p) cudaFree(p);
+  delete w;
+}
+
+int pack_impl(cudaStream_t st, const uint8_t* d_b, int64_t b_len, const void* d_scales, int scales_dtype,
+              int64_t scales_len, const void* d_zp, int zp_dtype, int64_t zp_len, int N, int K, int bits,
+              int bs, int n_begin, int n_end, int flags, msq_weights_t* out) {
+  if (!out) return fail(MSQ_E_INVALID, "msq_pack: out handle pointer is NULL");
+  *out = nullptr;
+  int rc = check_weights(N, K, bits, bs, b_len, scales_len, scales_dtype, zp_dtype, zp_len);
+  if (rc != MSQ_OK) return rc;
+  if (n_begin < 0 || n_end > N || n_begin >= n_end)
+    return fail(MSQ_E_INVALID, "msq_pack: row range [%d, %d) is not inside [0, %d)", n_begin, n_end, N);
+  if (!d_b || !d_scales || (zp_dtype != MSQ_DT_ABSENT && !d_zp))
+    return fail(MSQ_E_INVALID, "msq_pack: NULL device pointer");
+
+  Weights* w = new Weights();
+  rc = current_device(&w->device);
+  if (rc != MSQ_OK) {
+    delete w;
+    return rc;
+  }
+  w->n_rows = n_end - n_begin;
+  w->K = K;
+  w->bits = bits;
+  w->block_size = bs;
+  w->nb = (K + bs - 1) / bs;
+  w->blob = (bs * bits + 7) / 8;
+  w->zp_row_bytes = (w->nb * bits + 7) / 8;
+  w->zp_kind = zp_dtype == MSQ_DT_U8 ? ZP_PACKED : zp_dtype == MSQ_DT_F32 ? ZP_F32 : ZP_NONE;
+  w->fast4 = bits == 4 && bs >= 32 && pow2(bs) && !(flags & MSQ_PACK_GENERIC_ONLY);
+
+  const size_t rows = (size_t)w->n_rows;
+  if (w->fast4) {
+    w->KP = (K + 127) / 128 * 128;
+    w->nib_pitch = w->KP / 2;
+    w->sc_pitch = (w->nb + 3) / 4 * 4;
+    w->zp_pitch = (w->zp_row_bytes + 15) / 16 * 16;
+    rc = dev_alloc(&w->nib, rows * (size_t)w->nib_pitch, &w->device_bytes);
+    if (rc == MSQ_OK) rc = dev_alloc(&w->sc, rows * (size_t)w->sc_pitch, &w->device_bytes);
+    if (rc == MSQ_OK) rc = dev_alloc(&w->sc16, rows * (size_t)w->sc_pitch, &w->device_bytes);
+    if (rc == MSQ_OK && w->zp_kind == ZP_PACKED) rc = dev_alloc(&w->zp4, rows * (size_t)w->zp_pitch, &w->device_bytes);
+    if (rc == MSQ_OK && w->zp_kind == ZP_F32) rc = dev_alloc(&w->zpf, rows * (size_t)w->sc_pitch, &w->device_bytes);
+    if (rc == MSQ_OK) rc = repack_fast4(st, *w, d_b, n_begin, d_scales, scales_dtype, d_zp);
+  } else {
+    rc = dev_alloc(&w->b_ref, rows * (size_t)w->nb * w->blob, &w->device_bytes);
+    if (rc == MSQ_OK) rc = dev_alloc(&w->sc_ref, rows * (size_t)w->nb, &w->device_bytes);
+    if (rc == MSQ_OK && w->zp_kind == ZP_PACKED)
+      rc = dev_alloc(&w->zp_ref_u8, rows * (size_t)w->zp_row_bytes, &w->device_bytes);
+    if (rc == MSQ_OK && w->zp_kind == ZP_F32) rc = dev_alloc(&w->zp_ref_f32, rows * (size_t)w->nb, &w->device_bytes);
+    if (rc == MSQ_OK) rc = repack_reference(st, *w, d_b, n_begin, d_scales, scales_dtype, d_zp);
+  }
+  if (rc != MSQ_OK) {
+    cudaStreamSynchronize(st);
+    free_weights(w);
+    return rc;
+  }
+  *out = reinterpret_cast<msq_weights_t>(w);
+  return MSQ_OK;
+}
+
+int matmul_impl(cudaStream_t st, Weights* w, const void* d_a, int a_dtype, int64_t M, float* d_y, int64_t ldy,
+                int path) {
+  if (!w) return fail(MSQ_E_INVALID, "msq_matmul: NULL weights handle");
+  if (!is_float_act(a_dtype))
+    return fail(MSQ_E_INVALID, "MatMulNBits A must be Float32 or Float16; got %s.", dtype_name(a_dtype));
+  if (M < 0) return fail(MSQ_E_INVALID, "msq_matmul: negative M (%lld)", (long long)M);
+  if (ldy < w->n_rows) return fail(MSQ_E_INVALID, "msq_matmul: ldy %lld < rows %d", (long long)ldy, w->n_rows);
+  if (M == 0) {
+    note_path("empty");
+    return MSQ_OK;
+  }
+  if (!d_a || !d_y) return fail(MSQ_E_INVALID, "msq_matmul: NULL device pointer");
+  int dev;
+  int rc = current_device(&dev);
+  if (rc != MSQ_OK) return rc;
+  if (dev != w->device)
+    return fail(MSQ_E_INVALID, "weights handle lives on device %d but the current device is %d", w->device, dev);
+  if (path == MSQ_PATH_AUTO) {
+    if (!w->fast4) path = MSQ_PATH_GENERIC;
+    else path = MSQ_PATH_GEMV;
+  }
+  switch (path) {
+    case MSQ_PATH_GENERIC: return run_generic(st, *w, d_a, a_dtype, M, d_y, ldy);
+    case MSQ_PATH_GEMV: return run_gemv(st, *w, d_a, a_dtype, M, d_y, ldy);
+    case MSQ_PATH_GEMM: return run_gemm(st, *w, d_a, a_dtype, M, d_y, ldy);
+    default: return fail(MSQ_E_INVALID, "msq_matmul_ex: unknown path %d", path);
+  }
+}
+
+size_t act_elem_size(int dt) { return dt == MSQ_DT_F32 ? 4 : 2; }
+
+}  // namespace
+
+int fail(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(e == cudaErrorMemoryAllocation ? MSQ_E_OOM : MSQ_E_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e),
+              cudaGetErrorName(e));
+}
+
+void note_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+void note_path(const char* name) { t_last_path = name; }
+
+int num_sms(int device) {
+  static int cache[64] = {0};
+  if (device >= 0 && device < 64 && cache[device]) return cache[device];
+  int v = 148;
+  cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device);
+  if (device >= 0 && device < 64) cache[device] = v;
+  return v;
+}
+
+}  // namespace msq
+
+using namespace msq;
+
+extern "C" {
+
+const char* msq_build_info(void) {
+  static std::string s = [] {
+    char buf[256];
+    snprintf(buf, sizeof buf, "libms_cuda_nbits (nvcc %d.%d, sm_100a, built %s %s)", __CUDACC_VER_MAJOR__,
+             __CUDACC_VER_MINOR__, __DATE__, __TIME__);
+    return std::string(buf);
+  }();
+  return s.c_str();
+}
+
+int msq_available(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    return 0;
+  }
+  int dev = 0, major = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return 0;
+  return major == 10 ? 1 : 0;
+}
+
+const char* msq_last_error(void) { return t_last_error.c_str(); }
+int64_t msq_launch_count(void) { return g_launches.load(); }
+const char* msq_last_path(void) { return t_last_path; }
+
+int msq_check_node(int N, int K, int bits, int block_size, int64_t b_len, int64_t scales_len, int zp_dtype,
+                   int64_t zp_len, const int64_t* g_idx, int64_t g_idx_len, const int64_t* a_dims, int a_rank,
+                   int64_t* M_out) {
+  int rc = check_weights(N, K, bits, block_size, b_len, scales_len, MSQ_DT_F32, zp_dtype, zp_len);
+  if (rc != MSQ_OK) return rc;
+  if (g_idx && g_idx_len > 0) {
+    for (int64_t k = 0; k < g_idx_len; ++k)
+      if (g_idx[k] != k / block_size)
+        return fail(MSQ_E_UNSUPPORTED, "MatMulNBits g_idx with a non-trivial block permutation is not supported.");
+  }
+  if (a_rank <= 0 || !a_dims || a_dims[a_rank - 1] != K) {
+    std::string dims;
+    for (int i = 0; i < a_rank && a_dims; ++i) {
+      if (i) dims += ",";
+      dims += std::to_string((long long)a_dims[i]);
+    }
+    return fail(MSQ_E_INVALID, "MatMulNBits A inner dimension must equal K=%d; got shape [%s].", K, dims.c_str());
+  }
+  int64_t M = 1;
+  for (int i = 0; i < a_rank - 1; ++i) M *= a_dims[i];
+  if (M_out) *M_out = M;
+  return MSQ_OK;
+}
+
+int msq_pack(void* cu_ctx, void* stream, const uint8_t* d_b, int64_t b_len, const void* d_scales, int scales_dtype,
+             int64_t scales_len, const void* d_zp, int zp_dtype, int64_t zp_len, int N, int K, int bits,
+             int block_size, int n_begin, int n_end, int flags, msq_weights_t* out) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  return pack_impl(static_cast<cudaStream_t>(stream), d_b, b_len, d_scales, scales_dtype, scales_len, d_zp,
+                   zp_dtype, zp_len, N, K, bits, block_size, n_begin, n_end, flags, out);
+}
+
+int msq_pack_host(void* cu_ctx, void* stream, const uint8_t* b, int64_t b_len, const void* scales,
+                  int scales_dtype, int64_t scales_len, const void* zp, int zp_dtype, int64_t zp_len, int N,
+                  int K, int bits, int block_size, int n_begin, int n_end, int flags, msq_weights_t* out) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  if (out) *out = nullptr;
+  int rc = check_weights(N, K, bits, block_size, b_len, scales_len, scales_dtype, zp_dtype, zp_len);
+  if (rc != MSQ_OK) return rc;
+  if (!b || !scales || (zp_dtype != MSQ_DT_ABSENT && !zp)) return fail(MSQ_E_INVALID, "msq_pack_host: NULL pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t sbytes = (size_t)scales_len * (scales_dtype == MSQ_DT_F32 ? 4 : 2);
+  const size_t zbytes = zp_dtype == MSQ_DT_ABSENT ? 0 : (size_t)zp_len * (zp_dtype == MSQ_DT_F32 ? 4 : 1);
+  uint8_t* db = nullptr;
+  void *ds = nullptr, *dz = nullptr;
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&db), (size_t)b_len);
+  if (e == cudaSuccess) e = cudaMalloc(&ds, sbytes);
+  if (e == cudaSuccess && zbytes) e = cudaMalloc(&dz, zbytes);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(db, b, (size_t)b_len, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(ds, scales, sbytes, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess && zbytes) e = cudaMemcpyAsync(dz, zp, zbytes, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess)
+    rc = pack_impl(st, db, b_len, ds, scales_dtype, scales_len, dz, zp_dtype, zp_len, N, K, bits, block_size,
+                   n_begin, n_end, flags, out);
+  else
+    rc = cuda_fail(e, "msq_pack_host upload");
+  cudaError_t se = cudaStreamSynchronize(st);
+  cudaFree(db);
+  cudaFree(ds);
+  if (dz) cudaFree(dz);
+  if (rc == MSQ_OK && se != cudaSuccess) {
+    msq_free(out ? *out : nullptr);
+    if (out) *out = nullptr;
+    return cuda_fail(se, "msq_pack_host synchronize");
+  }
+  return rc;
+}
+
+int msq_weights_query(msq_weights_t h, int* n_rows, int* K, int* bits, int* block_size, int64_t* device_bytes) {
+  Weights* w = reinterpret_cast<Weights*>(h);
+  if (!w) return fail(MSQ_E_INVALID, "msq_weights_query: NULL handle");
+  if (n_rows) *n_rows = w->n_rows;
+  if (K) *K = w->K;
+  if (bits) *bits = w->bits;
+  if (block_size) *block_size = w->block_size;
+  if (device_bytes) *device_bytes = w->device_bytes;
+  return MSQ_OK;
+}
+
+int msq_free(msq_weights_t h) {
+  free_weights(reinterpret_cast<Weights*>(h));
+  return MSQ_OK;
+}
+
+int msq_matmul(void* cu_ctx, void* stream, msq_weights_t w, const void* d_a, int a_dtype, int64_t M, float* d_y,
+               int64_t ldy) {
+  return msq_matmul_ex(cu_ctx, stream, w, d_a, a_dtype, M, d_y, ldy, MSQ_PATH_AUTO);
+}
+
+int msq_matmul_ex(void* cu_ctx, void* stream, msq_weights_t w, const void* d_a, int a_dtype, int64_t M, float* d_y,
+                  int64_t ldy, int path) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  return matmul_impl(static_cast<cudaStream_t>(stream), reinterpret_cast<Weights*>(w), d_a, a_dtype, M, d_y, ldy,
+                     path);
+}
+
+int msq_matmul_host(void* cu_ctx, void* stream, msq_weights_t h, const void* a, int a_dtype, int64_t M, float* y) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  Weights* w = reinterpret_cast<Weights*>(h);
+  if (!w) return fail(MSQ_E_INVALID, "msq_matmul_host: NULL weights handle");
+  if (!is_float_act(a_dtype))
+    return fail(MSQ_E_INVALID, "MatMulNBits A must be Float32 or Float16; got %s.", dtype_name(a_dtype));
+  if (M <= 0) return M == 0 ? MSQ_OK : fail(MSQ_E_INVALID, "msq_matmul_host: negative M");
+  if (!a || !y) return fail(MSQ_E_INVALID, "msq_matmul_host: NULL host pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t abytes = (size_t)M * w->K * act_elem_size(a_dtype);
+  const size_t ybytes = (size_t)M * w->n_rows * sizeof(float);
+  void* da = nullptr;
+  float* dy = nullptr;
+  cudaError_t e = cudaMallocAsync(&da, abytes, st);
+  if (e == cudaSuccess) e = cudaMallocAsync(reinterpret_cast<void**>(&dy), ybytes, st);
+  if (e != cudaSuccess) {
+    if (da) cudaFreeAsync(da, st);
+    return cuda_fail(e, "msq_matmul_host allocation");
+  }
+  int rc = MSQ_OK;
+  e = cudaMemcpyAsync(da, a, abytes, cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) rc = cuda_fail(e, "msq_matmul_host upload");
+  if (rc == MSQ_OK) rc = matmul_impl(st, w, da, a_dtype, M, dy, w->n_rows, MSQ_PATH_AUTO);
+  if (rc == MSQ_OK) {
+    e = cudaMemcpyAsync(y, dy, ybytes, cudaMemcpyDeviceToHost, st);
+    if (e != cudaSuccess) rc = cuda_fail(e, "msq_matmul_host download");
+  }
+  cudaFreeAsync(da, st);
+  cudaFreeAsync(dy, st);
+  e = cudaStreamSynchronize(st);
+  if (rc == MSQ_OK && e != cudaSuccess) rc = cuda_fail(e, "msq_matmul_host synchronize");
+  return rc;
+}
+
+int msq_qgemm_nbits(const float* a, const uint8_t* bq, const float* scales, const uint8_t* zero_points, float* y,
+                    int M, int N, int K, int bits, int block_size) {
+  if (N <= 0 || K <= 0 || block_size <= 0 || (bits != 4 && bits != 8) || M < 0)
+    return check_weights(N, K, bits, block_size, 0, 0, MSQ_DT_F32, MSQ_DT_ABSENT, 0) != MSQ_OK
+               ? MSQ_E_INVALID
+               : fail(MSQ_E_INVALID, "msq_qgemm_nbits: negative M");
+  const int64_t nb = ((int64_t)K + block_size - 1) / block_size;
+  const int64_t blob = ((int64_t)block_size * bits + 7) / 8;
+  const int64_t zp_row = (nb * bits + 7) / 8;
+  msq_weights_t w = nullptr;
+  int rc = msq_pack_host(nullptr, nullptr, bq, (int64_t)N * nb * blob, scales, MSQ_DT_F32, (int64_t)N * nb,
+                         zero_points, zero_points ? MSQ_DT_U8 : MSQ_DT_ABSENT, zero_points ? (int64_t)N * zp_row : 0,
+                         N, K, bits, block_size, 0, N, MSQ_PACK_DEFAULT, &w);
+  if (rc != MSQ_OK) return rc;
+  rc = msq_matmul_host(nullptr, nullptr, w, a, MSQ_DT_F32, M, y);
+  msq_free(w);
+  return rc;
+}
+
+}  // extern "C"

@@ -1,0 +1,85 @@
+// Internal declarations shared by the translation units of libms_cuda_nbits.so.
+// Nothing here is part of the C ABI (include/ms_cuda_nbits.h is).
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include "../../include/ms_cuda_nbits.h"
+
+namespace msq {
+
+enum ZpKind : int { ZP_NONE = 0, ZP_PACKED = 1, ZP_F32 = 2 };
+
+// Device-resident weights of rows [n_begin, n_end) of one MatMulNBits initializer.
+//
+// "fast4" handles (bits = 4, block_size a power of two >= 32) hold the kernel layout:
+//   nib   uint8 [n_rows][KP/2]  KP = K rounded up to 128; each 32-bit word carries the
+//                               8 codes of k = 8w..8w+7 in nibble slots ordered
+//                               k-offsets {0,2,4,6,1,3,5,7} (pairs (k, k+1) sit 16 bits
+//                               apart, so one mask yields both halves of a half2)
+//   sc    float [n_rows][sc_pitch]   exact fp32 scales, pitch nb rounded up to 4
+//   sc16  half  [n_rows][sc_pitch]   the same scales rounded to fp16 (GEMM operand path)
+//   zp4   uint8 [n_rows][zp_pitch]   packed zero points as the reference packs them
+//   zpf   float [n_rows][sc_pitch]   float zero points
+// Other handles keep the reference layout (b_ref, sc_ref, zp_ref_*) for the generic
+// kernel.
+struct Weights {
+  int device = -1;
+  int n_rows = 0, K = 0, bits = 4, block_size = 0, nb = 0, blob = 0, zp_row_bytes = 0;
+  int zp_kind = ZP_NONE;
+  bool fast4 = false;
+  int KP = 0;
+  uint8_t* nib = nullptr;
+  int64_t nib_pitch = 0;
+  float* sc = nullptr;
+  __half* sc16 = nullptr;
+  int64_t sc_pitch = 0;
+  uint8_t* zp4 = nullptr;
+  int64_t zp_pitch = 0;
+  float* zpf = nullptr;
+  uint8_t* b_ref = nullptr;
+  float* sc_ref = nullptr;
+  uint8_t* zp_ref_u8 = nullptr;
+  float* zp_ref_f32 = nullptr;
+  int64_t device_bytes = 0;
+  void* gemm_state = nullptr;
+};
+
+// ---- error and diagnostics plumbing (msq_api.cu) ----
+int fail(int code, const char* fmt, ...);
+int cuda_fail(cudaError_t e, const char* what);
+void note_launch(int n = 1);
+void note_path(const char* name);
+int num_sms(int device);
+
+#define MSQ_CUDA_TRY(expr, what)                         \
+  do {                                                   \
+    cudaError_t _e = (expr);                             \
+    if (_e != cudaSuccess) return ::msq::cuda_fail(_e, what); \
+  } while (0)
+
+// ---- repack (msq_repack.cu) ----
+int repack_fast4(cudaStream_t st, Weights& w, const uint8_t* d_b, int n_begin,
+                 const void* d_scales, int scales_dtype, const void* d_zp);
+int repack_reference(cudaStream_t st, Weights& w, const uint8_t* d_b, int n_begin,
+                     const void* d_scales, int scales_dtype, const void* d_zp);
+
+// ---- kernels ----
+int run_generic(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M,
+                float* d_y, int64_t ldy);
+int run_gemv(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M,
+             float* d_y, int64_t ldy);
+int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t M,
+             float* d_y, int64_t ldy);
+void release_gemm_state(Weights& w);
+
+// Loads element idx of an activation tensor of dtype dt (f32 / f16 / bf16) as fp32.
+__device__ __forceinline__ float load_act(const void* a, int dt, int64_t idx) {
+  if (dt == MSQ_DT_F32) return static_cast<const float*>(a)[idx];
+  if (dt == MSQ_DT_F16) return __half2float(static_cast<const __half*>(a)[idx]);
+  return __bfloat162float(static_cast<const __nv_bfloat16*>(a)[idx]);
+}
+
+}  // namespace msq
