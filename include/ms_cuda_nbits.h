@@ -36,6 +36,7 @@ extern "C" {
 #define MSQ_E_CUDA         -3  /* CUDA runtime or driver error                        */
 #define MSQ_E_NO_DEVICE    -4  /* no compute-capability 10.x device visible           */
 #define MSQ_E_OOM          -5  /* device allocation failed                            */
+#define MSQ_E_TIMEOUT      -6  /* a kernel's bounded wait gave up (see msq_device_status) */
 
 /* ---- element types (ModelSharp ElementType, src/ModelSharp/Tensors/ElementType.cs:4-15) */
 #define MSQ_DT_ABSENT  -1
@@ -127,6 +128,12 @@ int msq_matmul_ex(void* cu_ctx, void* stream, msq_weights_t w,
  * runs, copies Y [M, n_rows] out and synchronizes the stream.                          */
 int msq_matmul_host(void* cu_ctx, void* stream, msq_weights_t w,
                     const void* a, int a_dtype, int64_t M, float* y);
+
+/* Synchronizes `stream` and reports whether any kernel of this library on the current
+ * device gave up a bounded wait (a pipeline stage that never arrived) since the last call:
+ * MSQ_OK, or MSQ_E_TIMEOUT with the kernel and stage in msq_last_error(). Clears the flags.
+ * No counterpart in the reference (its kernels have no device-side waits).              */
+int msq_device_status(void* cu_ctx, void* stream);
 
 /* ---- one-shot drop-in for ms_qgemm_nbits (native/ms_kernels.h:42-44) -----------------
  * Host pointers, fp32 A / scales, packed or NULL zero points; uploads, runs on the

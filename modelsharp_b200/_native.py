@@ -19,6 +19,7 @@ MSQ_E_UNSUPPORTED = -2
 MSQ_E_CUDA = -3
 MSQ_E_NO_DEVICE = -4
 MSQ_E_OOM = -5
+MSQ_E_TIMEOUT = -6
 
 # ElementType codes (src/ModelSharp/Tensors/ElementType.cs:4-15) plus bf16.
 DT_ABSENT, DT_F32, DT_F64, DT_F16, DT_I32, DT_I64, DT_I8, DT_U8, DT_BOOL, DT_BF16 = -1, 1, 2, 3, 4, 5, 6, 7, 8, 16
@@ -50,6 +51,7 @@ SIGNATURES: dict[str, tuple] = {
     "msq_matmul": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp, _i64]),
     "msq_matmul_ex": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp, _i64, _i32]),
     "msq_matmul_host": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp]),
+    "msq_device_status": (_i32, [_vp, _vp]),
     "msq_qgemm_nbits": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32]),
 }
 

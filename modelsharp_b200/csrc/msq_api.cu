@@ -151,7 +151,7 @@ int dev_alloc(T** p, size_t n, int64_t* total) {
 void free_weights(Weights* w) {
   if (!w) return;
   release_gemm_state(*w);
-  void* ptrs[] = {w->nib, w->sc, w->sc16, w->zp4, w->zpf, w->b_ref, w->sc_ref, w->zp_ref_u8, w->zp_ref_f32};
+  void* ptrs[] = {w->nib, w->sc, w->sc16, w->zp4, w->zpf, w->strm, w->b_ref, w->sc_ref, w->zp_ref_u8, w->zp_ref_f32};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   delete w;
@@ -189,7 +189,7 @@ int pack_impl(cudaStream_t st, const uint8_t* d_b, int64_t b_len, const void* d_
   if (w->fast4) {
     w->KP = (K + 127) / 128 * 128;
     w->nib_pitch = w->KP / 2;
-    w->sc_pitch = (w->nb + 3) / 4 * 4;
+    w->sc_pitch = (w->nb + 7) / 8 * 8;
     w->zp_pitch = (w->zp_row_bytes + 15) / 16 * 16;
     rc = dev_alloc(&w->nib, rows * (size_t)w->nib_pitch, &w->device_bytes);
     if (rc == MSQ_OK) rc = dev_alloc(&w->sc, rows * (size_t)w->sc_pitch, &w->device_bytes);
@@ -197,6 +197,10 @@ int pack_impl(cudaStream_t st, const uint8_t* d_b, int64_t b_len, const void* d_
     if (rc == MSQ_OK && w->zp_kind == ZP_PACKED) rc = dev_alloc(&w->zp4, rows * (size_t)w->zp_pitch, &w->device_bytes);
     if (rc == MSQ_OK && w->zp_kind == ZP_F32) rc = dev_alloc(&w->zpf, rows * (size_t)w->sc_pitch, &w->device_bytes);
     if (rc == MSQ_OK) rc = repack_fast4(st, *w, d_b, n_begin, d_scales, scales_dtype, d_zp);
+    plan_stream(*w, num_sms(w->device));
+    if (rc == MSQ_OK)
+      rc = dev_alloc(&w->strm, (size_t)w->nblk * w->ntiles * w->rb * w->rec_bytes, &w->device_bytes);
+    if (rc == MSQ_OK) rc = repack_stream(st, *w, d_b, n_begin, d_scales, scales_dtype, d_zp);
   } else {
     rc = dev_alloc(&w->b_ref, rows * (size_t)w->nb * w->blob, &w->device_bytes);
     if (rc == MSQ_OK) rc = dev_alloc(&w->sc_ref, rows * (size_t)w->nb, &w->device_bytes);
@@ -438,6 +442,21 @@ int msq_matmul_host(void* cu_ctx, void* stream, msq_weights_t h, const void* a, 
   e = cudaStreamSynchronize(st);
   if (rc == MSQ_OK && e != cudaSuccess) rc = cuda_fail(e, "msq_matmul_host synchronize");
   return rc;
+}
+
+int msq_device_status(void* cu_ctx, void* stream) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int fv = 0, fm = 0;
+  int rc = read_gemv_errors(st, &fv);
+  if (rc == MSQ_OK) rc = read_gemm_errors(st, &fm);
+  if (rc != MSQ_OK) return rc;
+  static const char* what[] = {"", "waiting for a stage to arrive", "waiting for a free stage",
+                               "waiting for the tensor core", "draining in-flight copies"};
+  if (fv) return fail(MSQ_E_TIMEOUT, "decode GEMV kernel gave up %s", what[fv > 0 && fv < 5 ? fv : 0]);
+  if (fm) return fail(MSQ_E_TIMEOUT, "GEMM kernel gave up %s", what[fm > 0 && fm < 5 ? fm : 0]);
+  return MSQ_OK;
 }
 
 int msq_qgemm_nbits(const float* a, const uint8_t* bq, const float* scales, const uint8_t* zero_points, float* y,

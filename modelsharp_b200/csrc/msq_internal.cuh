@@ -19,10 +19,16 @@ enum ZpKind : int { ZP_NONE = 0, ZP_PACKED = 1, ZP_F32 = 2 };
 //                               8 codes of k = 8w..8w+7 in nibble slots ordered
 //                               k-offsets {0,2,4,6,1,3,5,7} (pairs (k, k+1) sit 16 bits
 //                               apart, so one mask yields both halves of a half2)
-//   sc    float [n_rows][sc_pitch]   exact fp32 scales, pitch nb rounded up to 4
+//   sc    float [n_rows][sc_pitch]   exact fp32 scales, pitch nb rounded up to 8
 //   sc16  half  [n_rows][sc_pitch]   the same scales rounded to fp16 (GEMM operand path)
 //   zp4   uint8 [n_rows][zp_pitch]   packed zero points as the reference packs them
 //   zpf   float [n_rows][sc_pitch]   float zero points
+//   strm  the decode-GEMV stream: records of (row, k-tile) laid out
+//         [row block][k-tile][row in block][record], a record being the tile's nibble words
+//         (same slot order), then its fp32 scales, then its zero points (packed nibbles or
+//         fp32), padded to an odd number of 16-byte chunks. One row block x one k-tile is
+//         one contiguous bulk copy; the odd chunk stride keeps lane-per-row shared-memory
+//         reads free of bank conflicts.
 // Other handles keep the reference layout (b_ref, sc_ref, zp_ref_*) for the generic
 // kernel.
 struct Weights {
@@ -39,6 +45,14 @@ struct Weights {
   uint8_t* zp4 = nullptr;
   int64_t zp_pitch = 0;
   float* zpf = nullptr;
+  uint8_t* strm = nullptr;
+  int rb = 0;         // rows per row block
+  int kt = 0;         // k per tile (multiple of max(block_size, 64))
+  int ntiles = 0;     // k-tiles per row
+  int nblk = 0;       // row blocks
+  int rec_bytes = 0;  // bytes per (row, tile) record
+  int rec_sc = 0;     // byte offset of the scales in a record
+  int rec_zp = 0;     // byte offset of the zero points in a record
   uint8_t* b_ref = nullptr;
   float* sc_ref = nullptr;
   uint8_t* zp_ref_u8 = nullptr;
@@ -63,6 +77,11 @@ int num_sms(int device);
 // ---- repack (msq_repack.cu) ----
 int repack_fast4(cudaStream_t st, Weights& w, const uint8_t* d_b, int n_begin,
                  const void* d_scales, int scales_dtype, const void* d_zp);
+int repack_stream(cudaStream_t st, Weights& w, const uint8_t* d_b, int n_begin,
+                  const void* d_scales, int scales_dtype, const void* d_zp);
+void plan_stream(Weights& w, int sms);
+int read_gemv_errors(cudaStream_t st, int* flags);
+int read_gemm_errors(cudaStream_t st, int* flags);
 int repack_reference(cudaStream_t st, Weights& w, const uint8_t* d_b, int n_begin,
                      const void* d_scales, int scales_dtype, const void* d_zp);
 

@@ -196,3 +196,20 @@ def test_registry_replaces_by_op_type(cuda_device):
     r = KernelRegistry.create_default()
     ok, k = r.try_get("MatMulNBits")
     assert ok and k.op_type == "MatMulNBits" and r.count == 1
+
+
+def test_no_kernel_gave_up_a_wait(cuda_device):
+    """Every bounded wait in the pipelined kernels completed during the parity runs above."""
+    c = cases.baseline_case(1)
+    run(c, cuda_device)
+    rc = N.lib().msq_device_status(None, None)
+    assert rc == N.MSQ_OK, N.last_error()
+
+
+@pytest.mark.parametrize("N_", [1, 7, 33, 150, 1000, 5000])
+def test_stream_row_blocks_any_height(cuda_device, N_):
+    """The row-block height adapts to N (1..32 rows per block); partial last blocks and
+    single-row handles must produce every row exactly once."""
+    c = synth.make_case(14, 1, N_, 2048, 4, 128, "packed")
+    y = run(c, cuda_device, N.PATH_GEMV)
+    assert oracle.rel_l2(y, oracle.managed(c)) <= TOL_FP32
