@@ -197,9 +197,9 @@ int pack_impl(cudaStream_t st, const uint8_t* d_b, int64_t b_len, const void* d_
     if (rc == MSQ_OK && w->zp_kind == ZP_PACKED) rc = dev_alloc(&w->zp4, rows * (size_t)w->zp_pitch, &w->device_bytes);
     if (rc == MSQ_OK && w->zp_kind == ZP_F32) rc = dev_alloc(&w->zpf, rows * (size_t)w->sc_pitch, &w->device_bytes);
     if (rc == MSQ_OK) rc = repack_fast4(st, *w, d_b, n_begin, d_scales, scales_dtype, d_zp);
-    plan_stream(*w, num_sms(w->device));
+    plan_stream(*w);
     if (rc == MSQ_OK)
-      rc = dev_alloc(&w->strm, (size_t)w->nblk * w->ntiles * w->rb * w->rec_bytes, &w->device_bytes);
+      rc = dev_alloc(&w->strm, (size_t)w->nblk * w->ntiles * w->stage_bytes, &w->device_bytes);
     if (rc == MSQ_OK) rc = repack_stream(st, *w, d_b, n_begin, d_scales, scales_dtype, d_zp);
   } else {
     rc = dev_alloc(&w->b_ref, rows * (size_t)w->nb * w->blob, &w->device_bytes);
@@ -237,6 +237,7 @@ int matmul_impl(cudaStream_t st, Weights* w, const void* d_a, int a_dtype, int64
     return fail(MSQ_E_INVALID, "weights handle lives on device %d but the current device is %d", w->device, dev);
   if (path == MSQ_PATH_AUTO) {
     if (!w->fast4) path = MSQ_PATH_GENERIC;
+    else if (M >= 17 && w->K >= 64) path = MSQ_PATH_GEMM;
     else path = MSQ_PATH_GEMV;
   }
   switch (path) {
@@ -449,7 +450,7 @@ int msq_device_status(void* cu_ctx, void* stream) {
   if (g.rc != MSQ_OK) return g.rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int fv = 0, fm = 0;
-  int rc = read_gemv_errors(st, &fv);
+  int rc = read_gemv_mma_errors(st, &fv);
   if (rc == MSQ_OK) rc = read_gemm_errors(st, &fm);
   if (rc != MSQ_OK) return rc;
   static const char* what[] = {"", "waiting for a stage to arrive", "waiting for a free stage",

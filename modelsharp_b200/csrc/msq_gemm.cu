@@ -1,18 +1,456 @@
-// Prefill GEMM (tcgen05) for MatMulNBits -- placeholder until the tensor-core kernel lands.
+// Prefill GEMM for MatMulNBits on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
+//
+//   Y[m, n] = sum_k A[m, k] * W[n, k],  W[n, k] = fp16((q[n,k] - zp[n,b]) * s[n,b])
+//
+// One CTA computes a BM x BN tile of Y (BM = 128 activation rows = TMEM lanes, BN = 128 or
+// 256 weight rows = TMEM columns) over k-stages of 64:
+//   warp 8      TMA producer: the fp16 activation tile (128 x 64, 128-byte swizzle) and the
+//               packed int4 weight tile (BN rows x 32 bytes) of each stage, no multicast;
+//   warps 0..7  dequantise the packed tile into fp16 (q - zp) * s, written straight into the
+//               K-major 128-byte-swizzled layout the tensor core reads, then release the stage;
+//   warp 9      allocates TMEM and, from one lane, issues 4 x tcgen05.mma (M=128, N=BN, K=16)
+//               per stage with the fp32 accumulator in TMEM, committing each stage back to
+//               the producer;
+//   warps 0..7  finally read the accumulator with tcgen05.ld and store fp32 Y.
+// The dequantised operand is exact up to one fp16 rounding of (q - zp) * s; products and
+// sums are fp32 in the tensor core (parity bar: rel-L2 <= 5e-3 against the fp32 reference).
+// fp32 / bf16 activations are converted to fp16 into a stream-ordered scratch buffer first.
 #include "msq_internal.cuh"
+#include "msq_ptx.cuh"
+
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
 
 namespace msq {
+namespace {
 
-int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t M, float* d_y, int64_t ldy) {
-  (void)st; (void)w; (void)d_a; (void)a_dtype; (void)M; (void)d_y; (void)ldy;
-  return fail(MSQ_E_UNSUPPORTED, "tcgen05 GEMM path not built yet");
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kDeqWarps = 8;
+constexpr int kThreads = (kDeqWarps + 2) * 32;  // + TMA warp + MMA warp
+constexpr int kTmaWarp = kDeqWarps;
+constexpr int kMmaWarp = kDeqWarps + 1;
+
+__device__ int g_gemm_err;
+
+template <int BN>
+struct Plan {
+  static constexpr int kStages = BN == 256 ? 3 : 4;
+  static constexpr int kABytes = BM * BK * 2;         // 16 KB
+  static constexpr int kBBytes = BN * BK * 2;         // dequantised fp16 weights
+  static constexpr int kPBytes = BN * BK / 2;         // packed int4 weights
+  static constexpr int kOffA = 0;
+  static constexpr int kOffB = kOffA + kStages * kABytes;
+  static constexpr int kOffP = kOffB + kStages * kBBytes;
+  static constexpr int kOffBar = kOffP + kStages * kPBytes;
+  static constexpr int kBarBytes = (3 * kStages + 1) * 8 + 16;
+  static constexpr int kSmem = kOffBar + kBarBytes + 1024;  // + alignment slack
+};
+
+struct GemmArgs {
+  float* y;
+  int64_t ldy;
+  int M, n_rows, K, ksteps;
+  const float* unused;
+  const __half* sc16;
+  int64_t sc_pitch;
+  const uint8_t* zp4;
+  int64_t zp_pitch;
+  const float* zpf;
+  int bs_shift;
+  int vec_store;
+};
+
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-void release_gemm_state(Weights& w) { w.gemm_state = nullptr; }
+__device__ __forceinline__ bool wait_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code) {
+  if (*abort_flag) return false;
+  if (ptx::mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = ptx::globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 0) {
+      if (*abort_flag) return false;
+      if (ptx::globaltimer() - t0 > ptx::kWaitBudgetNs) {
+        *abort_flag = 1;
+        atomicCAS(&g_gemm_err, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
+// (1024 + q) as fp16 pairs from a nibble pair mask, then exact (q - zp) and one rounding * s.
+__device__ __forceinline__ uint32_t deq_pair(uint32_t bits, __half2 zc, __half2 s2) {
+  const uint32_t h = (bits & 0x000F000Fu) | 0x64006400u;
+  const __half2 v = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&h), zc), s2);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+__device__ __forceinline__ uint32_t deq_pair_f32(uint32_t bits, float z, float s) {
+  const float lo = ((float)(bits & 0xF) - z) * s;
+  const float hi = ((float)((bits >> 16) & 0xF) - z) * s;
+  const __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+template <int BN, int ZPK>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmP,
+                   const GemmArgs p) {
+  using PL = Plan<BN>;
+  constexpr int S = PL::kStages;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + PL::kOffBar);
+  uint64_t* wready = full + S;
+  uint64_t* empty = wready + S;
+  uint64_t* accum = empty + S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&wready[s], kDeqWarps);
+      ptx::mbar_init(&empty[s], 1);
+    }
+    ptx::mbar_init(accum, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == kMmaWarp) {
+    ptx::tmem_alloc(tmem_slot, BN);
+    ptx::tmem_relinquish();
+  }
+  if (warp == kTmaWarp && lane == 0) {
+    ptx::prefetch_tmap(&tmA);
+    ptx::prefetch_tmap(&tmP);
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == kTmaWarp) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int kt = 0; kt < p.ksteps; ++kt) {
+        const int s = kt % S;
+        const uint32_t u = kt / S;
+        if (kt >= S && !wait_abort(&empty[s], (u - 1) & 1, abort_flag, ptx::kErrTimeoutEmpty)) break;
+        ptx::mbar_arrive_expect_tx(&full[s], PL::kABytes + PL::kPBytes);
+        ptx::tma_load_2d(smem + PL::kOffA + s * PL::kABytes, &tmA, &full[s], kt * BK, m0);
+        ptx::tma_load_2d(smem + PL::kOffP + s * PL::kPBytes, &tmP, &full[s], kt * (BK / 2), n0);
+        ++issued;
+      }
+      for (int s = 0; s < S && s < issued; ++s) {  // drain copies in flight
+        const int last = s + (issued - 1 - s) / S * S;
+        const unsigned long long t0 = ptx::globaltimer();
+        while (!ptx::mbar_try_wait(&full[s], (last / S) & 1)) {
+          if (ptx::globaltimer() - t0 > ptx::kWaitBudgetNs) {
+            atomicCAS(&g_gemm_err, 0, ptx::kErrTimeoutDrain);
+            break;
+          }
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+      bool ok = true;
+      for (int kt = 0; kt < p.ksteps && ok; ++kt) {
+        const int s = kt % S;
+        const uint32_t u = kt / S;
+        ok = wait_abort(&full[s], u & 1, abort_flag, ptx::kErrTimeoutFull) &&
+             wait_abort(&wready[s], u & 1, abort_flag, ptx::kErrTimeoutFull);
+        if (!ok) break;
+        ptx::tc_fence_after();
+        const uint64_t ad = sw128_desc(ptx::smem_u32(smem + PL::kOffA + s * PL::kABytes));
+        const uint64_t bd = sw128_desc(ptx::smem_u32(smem + PL::kOffB + s * PL::kBBytes));
+#pragma unroll
+        for (int j = 0; j < BK / 16; ++j)
+          ptx::mma_f16(tmem, ad + 2 * j, bd + 2 * j, idesc, (kt | j) != 0);
+        ptx::mma_commit(&empty[s]);
+      }
+      ptx::mma_commit(accum);
+      // the accumulator (and every MMA reading shared memory) must be done before exit
+      const unsigned long long t0 = ptx::globaltimer();
+      while (!ptx::mbar_try_wait(accum, 0)) {
+        if (ptx::globaltimer() - t0 > ptx::kWaitBudgetNs) {
+          atomicCAS(&g_gemm_err, 0, ptx::kErrTimeoutMma);
+          break;
+        }
+      }
+    }
+  } else {
+    // ---------------- dequantisation warps 0..7
+    const int tid = threadIdx.x;                 // 0..255
+    for (int kt = 0; kt < p.ksteps; ++kt) {
+      const int s = kt % S;
+      const uint32_t u = kt / S;
+      const bool ok = wait_abort(&full[s], u & 1, abort_flag, ptx::kErrTimeoutFull);
+      if (ok) {
+        const uint8_t* ptile = smem + PL::kOffP + s * PL::kPBytes;
+        uint8_t* btile = smem + PL::kOffB + s * PL::kBBytes;
+        for (int r = tid; r < BN; r += kDeqWarps * 32) {
+          const int n = n0 + r;
+          const bool valid = n < p.n_rows;
+          const uint4 w0 = *reinterpret_cast<const uint4*>(ptile + r * 32);
+          const uint4 w1 = *reinterpret_cast<const uint4*>(ptile + r * 32 + 16);
+          const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+          // the stage's block(s): one block for bs >= 64, two (words 0-3 / 4-7) for bs = 32
+          const int blk0 = (kt * BK) >> p.bs_shift;
+          const int blk1 = (kt * BK + 32) >> p.bs_shift;
+          float s0 = 0.f, s1 = 0.f, z0 = 8.f, z1 = 8.f;
+          if (valid) {
+            s0 = __half2float(p.sc16[(int64_t)n * p.sc_pitch + blk0]);
+            s1 = __half2float(p.sc16[(int64_t)n * p.sc_pitch + blk1]);
+            if (ZPK == ZP_PACKED) {
+              const uint8_t* zr = p.zp4 + (int64_t)n * p.zp_pitch;
+              z0 = (float)((zr[blk0 >> 1] >> ((blk0 & 1) * 4)) & 0xF);
+              z1 = (float)((zr[blk1 >> 1] >> ((blk1 & 1) * 4)) & 0xF);
+            } else if (ZPK == ZP_F32) {
+              z0 = p.zpf[(int64_t)n * p.sc_pitch + blk0];
+              z1 = p.zpf[(int64_t)n * p.sc_pitch + blk1];
+            }
+          }
+          uint8_t* brow = btile + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+          for (int wi = 0; wi < 8; ++wi) {
+            const uint32_t x = words[wi];
+            const float sf = wi < 4 ? s0 : s1;
+            const float zf = wi < 4 ? z0 : z1;
+            uint4 o;
+            if (ZPK == ZP_F32) {
+              o.x = deq_pair_f32(x, zf, sf);
+              o.y = deq_pair_f32(x >> 4, zf, sf);
+              o.z = deq_pair_f32(x >> 8, zf, sf);
+              o.w = deq_pair_f32(x >> 12, zf, sf);
+            } else {
+              const __half2 zc = __float2half2_rn(1024.f + zf);
+              const __half2 s2 = __float2half2_rn(sf);
+              o.x = deq_pair(x, zc, s2);
+              o.y = deq_pair(x >> 4, zc, s2);
+              o.z = deq_pair(x >> 8, zc, s2);
+              o.w = deq_pair(x >> 12, zc, s2);
+            }
+            *reinterpret_cast<uint4*>(brow + ((wi ^ (r & 7)) << 4)) = o;
+          }
+        }
+      }
+      ptx::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&wready[s]);
+    }
+
+    // ---------------- epilogue: TMEM -> registers -> Y
+    // warp-uniform: tcgen05.ld below is a .sync.aligned warp instruction
+    const bool ok = __all_sync(0xffffffffu, wait_abort(accum, 0, abort_flag, ptx::kErrTimeoutMma));
+    ptx::tc_fence_after();
+    if (ok) {
+      const int q = warp & 3;                 // TMEM lane quarter of this warp
+      const int half = warp >> 2;             // column half
+      const int m = m0 + q * 32 + lane;
+      constexpr int kCols = BN / 2;
+#pragma unroll 1
+      for (int c = 0; c < kCols; c += 32) {
+        const int col = half * kCols + c;
+        uint32_t v[32];
+        ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)col, v);
+        ptx::tmem_ld_wait();
+        if (m < p.M) {
+          float* yrow = p.y + (int64_t)m * p.ldy + n0 + col;
+          if (p.vec_store && n0 + col + 32 <= p.n_rows) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4*>(yrow + j) = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                                                                 __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n0 + col + j < p.n_rows) yrow[j] = __uint_as_float(v[j]);
+          }
+        }
+      }
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, BN);
+  }
+}
+
+// fp32 / bf16 / unaligned fp16 activations -> fp16 [M][lda] (k < K only).
+__global__ void to_half_kernel(const void* __restrict__ a, int dt, int64_t M, int K, __half* __restrict__ out,
+                               int64_t lda) {
+  const int64_t total = M * (int64_t)K;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / K, k = i - m * K;
+    out[m * lda + k] = __float2half_rn(load_act(a, dt, i));
+  }
+}
+
+// ---------------------------------------------------------------- host side
+using PFN_encode = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+PFN_encode g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int encoder(PFN_encode* out) {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_encode>(fn);
+  });
+  if (!g_encode) return fail(MSQ_E_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  *out = g_encode;
+  return MSQ_OK;
+}
+
+int make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, void* base, uint64_t inner, uint64_t outer,
+                uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+  PFN_encode enc;
+  int rc = encoder(&enc);
+  if (rc != MSQ_OK) return rc;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dt, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MSQ_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return MSQ_OK;
+}
+
+struct GemmState {
+  CUtensorMap tmP128, tmP256;
+};
+
+template <int BN, int ZPK>
+int launch(cudaStream_t st, const CUtensorMap& tmA, const CUtensorMap& tmP, const GemmArgs& a, dim3 grid) {
+  auto kern = gemm_tc_kernel<BN, ZPK>;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    MSQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Plan<BN>::kSmem),
+                 "gemm smem attribute");
+    configured[dev] = true;
+  }
+  kern<<<grid, kThreads, Plan<BN>::kSmem, st>>>(tmA, tmP, a);
+  note_launch();
+  MSQ_CUDA_TRY(cudaGetLastError(), "gemm launch");
+  return MSQ_OK;
+}
+
+template <int BN>
+int launch_zp(cudaStream_t st, int zp_kind, const CUtensorMap& tmA, const CUtensorMap& tmP, const GemmArgs& a,
+              dim3 grid) {
+  switch (zp_kind) {
+    case ZP_PACKED: return launch<BN, ZP_PACKED>(st, tmA, tmP, a, grid);
+    case ZP_F32: return launch<BN, ZP_F32>(st, tmA, tmP, a, grid);
+    default: return launch<BN, ZP_NONE>(st, tmA, tmP, a, grid);
+  }
+}
+
+}  // namespace
+
+int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t M, float* d_y, int64_t ldy) {
+  if (!w.fast4) return fail(MSQ_E_UNSUPPORTED, "GEMM path needs bits=4 and a power-of-two block_size >= 32");
+  if (M <= 0) return MSQ_OK;
+  if (M > 0x7fffffff) return fail(MSQ_E_INVALID, "GEMM: M too large");
+  GemmState* gs = static_cast<GemmState*>(w.gemm_state);
+  if (!gs) {
+    gs = new GemmState();
+    int rc = make_map_2d(&gs->tmP128, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.nib, (uint64_t)w.nib_pitch,
+                         (uint64_t)w.n_rows, (uint64_t)w.nib_pitch, BK / 2, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc == MSQ_OK)
+      rc = make_map_2d(&gs->tmP256, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.nib, (uint64_t)w.nib_pitch,
+                       (uint64_t)w.n_rows, (uint64_t)w.nib_pitch, BK / 2, 256, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc != MSQ_OK) {
+      delete gs;
+      return rc;
+    }
+    w.gemm_state = gs;
+  }
+  // fp16 activations with 16-byte rows feed TMA directly; anything else goes through scratch
+  const void* a16 = d_a;
+  int64_t lda = w.K;
+  void* scratch = nullptr;
+  if (a_dtype != MSQ_DT_F16 || (w.K % 8) != 0 || (reinterpret_cast<uintptr_t>(d_a) & 15) != 0) {
+    lda = (w.K + 7) / 8 * 8;
+    MSQ_CUDA_TRY(cudaMallocAsync(&scratch, sizeof(__half) * (size_t)M * lda, st), "GEMM activation scratch");
+    to_half_kernel<<<num_sms(w.device) * 4, 256, 0, st>>>(d_a, a_dtype, M, w.K, static_cast<__half*>(scratch), lda);
+    note_launch();
+    a16 = scratch;
+  }
+  CUtensorMap tmA;
+  int rc = make_map_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, const_cast<void*>(a16), (uint64_t)w.K, (uint64_t)M,
+                       (uint64_t)lda * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc == MSQ_OK) {
+    GemmArgs g{};
+    g.y = d_y;
+    g.ldy = ldy;
+    g.M = (int)M;
+    g.n_rows = w.n_rows;
+    g.K = w.K;
+    g.ksteps = (w.K + BK - 1) / BK;
+    g.sc16 = w.sc16;
+    g.sc_pitch = w.sc_pitch;
+    g.zp4 = w.zp4;
+    g.zp_pitch = w.zp_pitch;
+    g.zpf = w.zpf;
+    int sh = 0;
+    while ((1 << sh) < w.block_size) ++sh;
+    g.bs_shift = sh;
+    g.vec_store = (ldy % 4 == 0) && ((reinterpret_cast<uintptr_t>(d_y) & 15) == 0);
+    const int64_t mt = (M + BM - 1) / BM;
+    const int64_t tiles256 = (w.n_rows + 255) / 256 * mt;
+    const bool big = tiles256 >= 2 * num_sms(w.device);
+    if (big) {
+      rc = launch_zp<256>(st, w.zp_kind, tmA, gs->tmP256, g, dim3((w.n_rows + 255) / 256, (unsigned)mt));
+    } else {
+      rc = launch_zp<128>(st, w.zp_kind, tmA, gs->tmP128, g, dim3((w.n_rows + 127) / 128, (unsigned)mt));
+    }
+    if (rc == MSQ_OK) note_path(big ? "gemm_tc_n256" : "gemm_tc_n128");
+  }
+  if (scratch) cudaFreeAsync(scratch, st);
+  return rc;
+}
+
+void release_gemm_state(Weights& w) {
+  delete static_cast<GemmState*>(w.gemm_state);
+  w.gemm_state = nullptr;
+}
 
 int read_gemm_errors(cudaStream_t st, int* flags) {
-  (void)st;
-  *flags = 0;
+  int v = 0;
+  MSQ_CUDA_TRY(cudaMemcpyFromSymbolAsync(&v, g_gemm_err, sizeof(int), 0, cudaMemcpyDeviceToHost, st),
+               "read gemm error word");
+  MSQ_CUDA_TRY(cudaStreamSynchronize(st), "synchronize");
+  if (v) {
+    const int zero = 0;
+    MSQ_CUDA_TRY(cudaMemcpyToSymbolAsync(g_gemm_err, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st),
+                 "clear gemm error word");
+    MSQ_CUDA_TRY(cudaStreamSynchronize(st), "synchronize");
+  }
+  *flags = v;
   return MSQ_OK;
 }
 

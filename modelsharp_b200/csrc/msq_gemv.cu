@@ -23,7 +23,6 @@
 // segments; a work item is (group of R rows, lane-chunk phase) and is reduced across the
 // warp with shuffles into per-phase shared slots, summed in a fixed order at the end.
 #include "msq_internal.cuh"
-#include "msq_ptx.cuh"
 
 #include <algorithm>
 
@@ -262,317 +261,6 @@ int launch_zp(cudaStream_t st, int zp_kind, GemvArgs a, int grid, size_t smem) {
 inline int rows_per_warp(int mr) { return mr <= 2 ? 4 : (mr == 4 ? 2 : 1); }
 
 
-// ============================================================================================
-// Streamed decode GEMV (the default for bits = 4): a producer warp moves one row block x one
-// k-tile of the interleaved record stream per stage (a single contiguous cp.async.bulk) into
-// an up-to-8-deep shared-memory ring; 16 consumer warps decode it with one lane per weight
-// row, so the activation chunk every lane needs is the same shared-memory word (broadcast)
-// and the per-row sums never cross lanes until the end of the row block. Each consumer warp
-// owns a fixed 1/16 of every tile's chunks; the 16 partial sums of a row are added in a
-// fixed order at the end of its row block.
-// ============================================================================================
-constexpr int kSConsumers = 16;
-constexpr int kSThreads = (kSConsumers + 1) * 32;
-constexpr int kSMaxStages = 8;
-constexpr int kSSmemMax = 227 * 1024;
-
-__device__ int g_gemv_err;  // device error word of the streamed kernel (bounded waits)
-
-struct StreamArgs {
-  const uint8_t* strm;
-  const void* a;
-  int a_dtype;
-  int64_t M, m0;
-  float* y;
-  int64_t ldy;
-  int n_rows, K, kpad, kt, ntiles, rb, nblk, rec_bytes, rec_sc, rec_zp, bs_shift, nst, stage_bytes;
-};
-
-// Waits on an mbarrier unless the CTA has aborted; a timeout aborts the CTA.
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                              int code) {
-  if (*abort_flag) return false;
-  if (ptx::mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = ptx::globaltimer();
-  for (uint32_t i = 1;; ++i) {
-    if (ptx::mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0) {
-      if (*abort_flag) return false;
-      if (ptx::globaltimer() - t0 > ptx::kWaitBudgetNs) {
-        *abort_flag = 1;
-        atomicCAS(&g_gemv_err, 0, code);
-        return false;
-      }
-    }
-  }
-}
-
-// Loads A[row][k0 .. k0+7] as fp32 (zeros past K).
-__device__ __forceinline__ void load8(const StreamArgs& p, int64_t row, int k0, float (&v)[8]) {
-  const int64_t base = row * (int64_t)p.K + k0;
-  if (k0 + 8 <= p.K && (p.K & 7) == 0) {
-    if (p.a_dtype == MSQ_DT_F32) {
-      const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(p.a) + base);
-      float4 x = q[0], y = q[1];
-      v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w; v[4] = y.x; v[5] = y.y; v[6] = y.z; v[7] = y.w;
-    } else {
-      uint4 raw = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.a) + base);
-      const uint32_t r[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if (p.a_dtype == MSQ_DT_F16) {
-          float2 f = __half22float2(*reinterpret_cast<const __half2*>(&r[j]));
-          v[2 * j] = f.x; v[2 * j + 1] = f.y;
-        } else {
-          float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r[j]));
-          v[2 * j] = f.x; v[2 * j + 1] = f.y;
-        }
-      }
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = k0 + j < p.K ? load_act(p.a, p.a_dtype, base + j) : 0.f;
-  }
-}
-
-template <int MR>
-__device__ __forceinline__ void stage_activations(const StreamArgs& p, float* As, float* Ss) {
-  const int ngroups = p.kpad / 8;
-  const int total = MR * ngroups;
-  const int64_t mvalid = p.M - p.m0;
-  for (int idx = threadIdx.x; idx < total; idx += kSConsumers * 32) {
-    const int m = idx / ngroups, g = idx - m * ngroups;
-    float v[8];
-    if (m < mvalid) {
-      load8(p, p.m0 + m, g * 8, v);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = 0.f;
-    }
-    float4* dst = reinterpret_cast<float4*>(As + (int64_t)m * p.kpad + g * 8);
-    dst[0] = make_float4(v[0], v[2] * 0x1p-4f, v[4] * 0x1p-8f, v[6] * 0x1p-12f);
-    dst[1] = make_float4(v[1] * 0x1p-16f, v[3] * 0x1p-8f, v[5] * 0x1p-12f, v[7] * 0x1p-16f);
-    float s8 = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
-    const unsigned mask = __activemask();
-    s8 += __shfl_xor_sync(mask, s8, 1);
-    s8 += __shfl_xor_sync(mask, s8, 2);
-    if ((g & 3) == 0) Ss[m * (p.kpad / 32) + (g >> 2)] = s8;
-  }
-}
-
-template <int MR, int ZPK>
-__global__ void __launch_bounds__(kSThreads, 1) gemv_stream_kernel(const StreamArgs p) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  float* As = reinterpret_cast<float*>(smem);
-  float* Ss = As + MR * p.kpad;
-  float* red = Ss + MR * (p.kpad / 32);
-  uint64_t* full = reinterpret_cast<uint64_t*>(red + kSConsumers * 32 * MR);
-  uint64_t* empty = full + kSMaxStages;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kSMaxStages);
-  // bulk-copy destinations must be 16-byte aligned; round the ring's base up to 128 bytes
-  uint8_t* stages = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(empty + kSMaxStages) + 16 + 127) & ~static_cast<uintptr_t>(127));
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < p.nst; ++s) {
-      ptx::mbar_init(&full[s], 1);
-      ptx::mbar_init(&empty[s], kSConsumers);
-    }
-    *abort_flag = 0;
-    ptx::fence_mbar_init();
-  }
-  __syncthreads();
-
-  if (warp == kSConsumers) {
-    // ---------------- producer: one elected lane issues the bulk copies
-    if (lane == 0) {
-      int issued = 0;
-      bool ok = true;
-      for (int b = blockIdx.x; b < p.nblk && ok; b += gridDim.x)
-        for (int t = 0; t < p.ntiles && ok; ++t) {
-          const int s = issued % p.nst;
-          const uint32_t u = issued / p.nst;
-          if (issued >= p.nst) ok = wait_or_abort(&empty[s], (u - 1) & 1, abort_flag, ptx::kErrTimeoutEmpty);
-          if (!ok) break;
-          ptx::mbar_arrive_expect_tx(&full[s], p.stage_bytes);
-          ptx::bulk_g2s(stages + (size_t)s * p.stage_bytes,
-                        p.strm + ((int64_t)b * p.ntiles + t) * (int64_t)p.stage_bytes, p.stage_bytes, &full[s]);
-          ++issued;
-        }
-      // Drain: the last copy issued into each slot must land before this CTA may exit.
-      for (int s = 0; s < p.nst && s < issued; ++s) {
-        const int last = s + (issued - 1 - s) / p.nst * p.nst;
-        const uint32_t u = last / p.nst;
-        const unsigned long long t0 = ptx::globaltimer();
-        while (!ptx::mbar_try_wait(&full[s], u & 1)) {
-          if (ptx::globaltimer() - t0 > ptx::kWaitBudgetNs) {
-            atomicCAS(&g_gemv_err, 0, ptx::kErrTimeoutDrain);
-            break;
-          }
-        }
-      }
-    }
-    return;
-  }
-
-  // ---------------- consumers
-  stage_activations<MR>(p, As, Ss);
-  ptx::named_bar_sync(1, kSConsumers * 32);
-
-  const int CT = p.kt / 32;
-  const int sw = p.kpad / 32;
-  const int64_t mvalid = p.M - p.m0;
-  int it = 0;
-  for (int b = blockIdx.x; b < p.nblk; b += gridDim.x) {
-    float yacc[MR];
-#pragma unroll
-    for (int m = 0; m < MR; ++m) yacc[m] = 0.f;
-    for (int t = 0; t < p.ntiles; ++t, ++it) {
-      const int s = it % p.nst;
-      const uint32_t u = it / p.nst;
-      const bool ok = wait_or_abort(&full[s], u & 1, abort_flag, ptx::kErrTimeoutFull);
-      if (ok && lane < p.rb) {
-        const uint8_t* rec = stages + (size_t)s * p.stage_bytes + lane * p.rec_bytes;
-#pragma unroll 2
-        for (int c = warp; c < CT; c += kSConsumers) {
-          const uint4 wv = *reinterpret_cast<const uint4*>(rec + c * 16);
-          const int bl = (c * 32) >> p.bs_shift;
-          const float sc = *reinterpret_cast<const float*>(rec + p.rec_sc + 4 * bl);
-          float z;
-          if (ZPK == ZP_PACKED) {
-            z = (float)((rec[p.rec_zp + (bl >> 1)] >> ((bl & 1) * 4)) & 0xF);
-          } else if (ZPK == ZP_F32) {
-            z = *reinterpret_cast<const float*>(rec + p.rec_zp + 4 * bl);
-          } else {
-            z = 8.0f;
-          }
-          const int g = t * CT + c;
-          const float4* a4 = reinterpret_cast<const float4*>(As) + g * 8;
-          float2 acc[MR];
-#pragma unroll
-          for (int m = 0; m < MR; ++m) acc[m] = make_float2(0.f, 0.f);
-#pragma unroll
-          for (int wd = 0; wd < 4; ++wd) {
-            const uint32_t x = wd == 0 ? wv.x : wd == 1 ? wv.y : wd == 2 ? wv.z : wv.w;
-            float2 d[4];
-            decode_word(x, d);
-#pragma unroll
-            for (int m = 0; m < MR; ++m) {
-              const float4 lo = a4[(int64_t)m * (p.kpad / 4) + 2 * wd];
-              const float4 hi = a4[(int64_t)m * (p.kpad / 4) + 2 * wd + 1];
-              acc[m] = __ffma2_rn(make_float2(lo.x, lo.y), d[0], acc[m]);
-              acc[m] = __ffma2_rn(make_float2(lo.z, lo.w), d[1], acc[m]);
-              acc[m] = __ffma2_rn(make_float2(hi.x, hi.y), d[2], acc[m]);
-              acc[m] = __ffma2_rn(make_float2(hi.z, hi.w), d[3], acc[m]);
-            }
-          }
-#pragma unroll
-          for (int m = 0; m < MR; ++m) {
-            const float P = acc[m].x + acc[m].y;
-            yacc[m] = fmaf(sc, fmaf(-z, Ss[m * sw + g], P), yacc[m]);
-          }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&empty[s]);
-    }
-    // fixed-order cross-warp reduction of the row block
-#pragma unroll
-    for (int m = 0; m < MR; ++m) red[(warp * 32 + lane) * MR + m] = yacc[m];
-    ptx::named_bar_sync(1, kSConsumers * 32);
-    if ((int)threadIdx.x < p.rb * MR) {
-      const int rr = threadIdx.x % p.rb, m = threadIdx.x / p.rb;
-      const int64_t row = (int64_t)b * p.rb + rr;
-      float v = 0.f;
-      for (int w = 0; w < kSConsumers; ++w) v += red[(w * 32 + rr) * MR + m];
-      if (row < p.n_rows && m < mvalid) p.y[(p.m0 + m) * p.ldy + row] = v;
-    }
-    ptx::named_bar_sync(1, kSConsumers * 32);
-  }
-}
-
-template <int MR, int ZPK>
-int launch_stream(cudaStream_t st, const StreamArgs& a, int grid, size_t smem) {
-  auto kern = gemv_stream_kernel<MR, ZPK>;
-  static bool configured[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !configured[dev]) {
-    MSQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSSmemMax),
-                 "stream gemv smem attribute");
-    configured[dev] = true;
-  }
-  kern<<<grid, kSThreads, smem, st>>>(a);
-  note_launch();
-  MSQ_CUDA_TRY(cudaGetLastError(), "stream gemv launch");
-  return MSQ_OK;
-}
-
-template <int MR>
-int launch_stream_zp(cudaStream_t st, int zp_kind, const StreamArgs& a, int grid, size_t smem) {
-  switch (zp_kind) {
-    case ZP_PACKED: return launch_stream<MR, ZP_PACKED>(st, a, grid, smem);
-    case ZP_F32: return launch_stream<MR, ZP_F32>(st, a, grid, smem);
-    default: return launch_stream<MR, ZP_NONE>(st, a, grid, smem);
-  }
-}
-
-// Shared-memory plan of the streamed kernel; returns 0 when it does not fit.
-size_t stream_smem(const Weights& w, int mr, int* nst) {
-  const size_t kpad = (size_t)w.ntiles * w.kt;
-  const size_t fixed = sizeof(float) * (mr * kpad + mr * kpad / 32 + (size_t)kSConsumers * 32 * mr) +
-                       2 * kSMaxStages * sizeof(uint64_t) + 16 + 128;
-  const size_t stage = (size_t)w.rb * w.rec_bytes;
-  if (fixed + 2 * stage > (size_t)kSSmemMax) return 0;
-  int n = (int)((kSSmemMax - fixed) / stage);
-  if (n > kSMaxStages) n = kSMaxStages;
-  *nst = n;
-  return fixed + (size_t)n * stage;
-}
-
-int run_gemv_stream(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M, float* d_y,
-                    int64_t ldy, int mr) {
-  int nst = 0;
-  const size_t smem = stream_smem(w, mr, &nst);
-  if (!smem || !w.strm) return MSQ_E_UNSUPPORTED;
-  StreamArgs a{};
-  a.strm = w.strm;
-  a.a = d_a;
-  a.a_dtype = a_dtype;
-  a.M = M;
-  a.y = d_y;
-  a.ldy = ldy;
-  a.n_rows = w.n_rows;
-  a.K = w.K;
-  a.kt = w.kt;
-  a.ntiles = w.ntiles;
-  a.kpad = w.ntiles * w.kt;
-  a.rb = w.rb;
-  a.nblk = w.nblk;
-  a.rec_bytes = w.rec_bytes;
-  a.rec_sc = w.rec_sc;
-  a.rec_zp = w.rec_zp;
-  int sh = 0;
-  while ((1 << sh) < w.block_size) ++sh;
-  a.bs_shift = sh;
-  a.nst = nst;
-  a.stage_bytes = w.rb * w.rec_bytes;
-  const int grid = std::min(w.nblk, num_sms(w.device));
-  for (int64_t m0 = 0; m0 < M; m0 += mr) {
-    a.m0 = m0;
-    int rc;
-    switch (mr) {
-      case 1: rc = launch_stream_zp<1>(st, w.zp_kind, a, grid, smem); break;
-      case 2: rc = launch_stream_zp<2>(st, w.zp_kind, a, grid, smem); break;
-      case 4: rc = launch_stream_zp<4>(st, w.zp_kind, a, grid, smem); break;
-      default: rc = launch_stream_zp<8>(st, w.zp_kind, a, grid, smem); break;
-    }
-    if (rc != MSQ_OK) return rc;
-  }
-  return MSQ_OK;
-}
-
 }  // namespace
 
 int run_gemv(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M,
@@ -582,13 +270,10 @@ int run_gemv(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, in
   const int sms = num_sms(w.device);
   const int mr = M == 1 ? 1 : M == 2 ? 2 : M <= 4 ? 4 : 8;
   {
-    const int rc = run_gemv_stream(st, w, d_a, a_dtype, M, d_y, ldy, mr);
-    if (rc != MSQ_E_UNSUPPORTED) {
-      if (rc == MSQ_OK) note_path(mr == 1 ? "gemv_stream_m1" : mr == 2 ? "gemv_stream_m2" : mr == 4 ? "gemv_stream_m4" : "gemv_stream_m8");
-      return rc;
-    }
+    const int rc = run_gemv_mma(st, w, d_a, a_dtype, M, d_y, ldy);
+    if (rc != MSQ_E_UNSUPPORTED) return rc;
   }
-  // Too large for the streamed kernel's shared memory: K-segmented kernel below.
+  // Block sizes the tensor-core kernel does not take: the K-segmented CUDA-core kernel below.
   const int R = rows_per_warp(mr);
 
   GemvArgs a{};
@@ -638,21 +323,6 @@ int run_gemv(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, in
     if (rc != MSQ_OK) return rc;
   }
   note_path(mr == 1 ? "gemv_seg_m1" : mr == 2 ? "gemv_seg_m2" : mr == 4 ? "gemv_seg_m4" : "gemv_seg_m8");
-  return MSQ_OK;
-}
-
-int read_gemv_errors(cudaStream_t st, int* flags) {
-  int v = 0;
-  MSQ_CUDA_TRY(cudaMemcpyFromSymbolAsync(&v, g_gemv_err, sizeof(int), 0, cudaMemcpyDeviceToHost, st),
-               "read gemv error word");
-  MSQ_CUDA_TRY(cudaStreamSynchronize(st), "synchronize");
-  if (v) {
-    const int zero = 0;
-    MSQ_CUDA_TRY(cudaMemcpyToSymbolAsync(g_gemv_err, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st),
-                 "clear gemv error word");
-    MSQ_CUDA_TRY(cudaStreamSynchronize(st), "synchronize");
-  }
-  *flags = v;
   return MSQ_OK;
 }
 

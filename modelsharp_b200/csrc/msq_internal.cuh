@@ -23,12 +23,13 @@ enum ZpKind : int { ZP_NONE = 0, ZP_PACKED = 1, ZP_F32 = 2 };
 //   sc16  half  [n_rows][sc_pitch]   the same scales rounded to fp16 (GEMM operand path)
 //   zp4   uint8 [n_rows][zp_pitch]   packed zero points as the reference packs them
 //   zpf   float [n_rows][sc_pitch]   float zero points
-//   strm  the decode-GEMV stream: records of (row, k-tile) laid out
-//         [row block][k-tile][row in block][record], a record being the tile's nibble words
-//         (same slot order), then its fp32 scales, then its zero points (packed nibbles or
-//         fp32), padded to an odd number of 16-byte chunks. One row block x one k-tile is
-//         one contiguous bulk copy; the odd chunk stride keeps lane-per-row shared-memory
-//         reads free of bank conflicts.
+//   strm  the decode-GEMV stream, one contiguous stage per (row block, k-tile), stages laid
+//         out [row block][k-tile]. A row block is G groups of 16 rows; a k-tile is nwk warp
+//         slices of ks k. Inside a stage: the nibbles as [group][slice][64-k chunk][lane][16 B]
+//         where lane (r = lane/4, t = lane%4) holds, per 16-k step, one word with the codes of
+//         rows r and r+8 at k = 2t, 2t+1, 2t+8, 2t+9 (the mma.m16n8k16 A-fragment order), then
+//         the fp32 scales [group][slice][block][16 rows], then the zero points
+//         [group][slice][block][16 rows] (packed nibbles or fp32).
 // Other handles keep the reference layout (b_ref, sc_ref, zp_ref_*) for the generic
 // kernel.
 struct Weights {
@@ -46,13 +47,16 @@ struct Weights {
   int64_t zp_pitch = 0;
   float* zpf = nullptr;
   uint8_t* strm = nullptr;
-  int rb = 0;         // rows per row block
-  int kt = 0;         // k per tile (multiple of max(block_size, 64))
-  int ntiles = 0;     // k-tiles per row
-  int nblk = 0;       // row blocks
-  int rec_bytes = 0;  // bytes per (row, tile) record
-  int rec_sc = 0;     // byte offset of the scales in a record
-  int rec_zp = 0;     // byte offset of the zero points in a record
+  int ks = 0;           // k per warp slice (multiple of max(block_size, 64))
+  int nwk = 0;          // warp slices per k-tile (<= 16)
+  int groups = 0;       // 16-row groups per row block
+  int kt = 0;           // k per tile = nwk * ks
+  int ntiles = 0;       // k-tiles per row
+  int rb = 0;           // rows per row block = 16 * groups
+  int nblk = 0;         // row blocks
+  int stage_bytes = 0;  // bytes per (row block, k-tile) stage
+  int off_sc = 0;       // byte offset of the scales in a stage
+  int off_zp = 0;       // byte offset of the zero points in a stage
   uint8_t* b_ref = nullptr;
   float* sc_ref = nullptr;
   uint8_t* zp_ref_u8 = nullptr;
@@ -79,8 +83,8 @@ int repack_fast4(cudaStream_t st, Weights& w, const uint8_t* d_b, int n_begin,
                  const void* d_scales, int scales_dtype, const void* d_zp);
 int repack_stream(cudaStream_t st, Weights& w, const uint8_t* d_b, int n_begin,
                   const void* d_scales, int scales_dtype, const void* d_zp);
-void plan_stream(Weights& w, int sms);
-int read_gemv_errors(cudaStream_t st, int* flags);
+void plan_stream(Weights& w);
+int read_gemv_mma_errors(cudaStream_t st, int* flags);
 int read_gemm_errors(cudaStream_t st, int* flags);
 int repack_reference(cudaStream_t st, Weights& w, const uint8_t* d_b, int n_begin,
                      const void* d_scales, int scales_dtype, const void* d_zp);
@@ -90,6 +94,8 @@ int run_generic(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype,
                 float* d_y, int64_t ldy);
 int run_gemv(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M,
              float* d_y, int64_t ldy);
+int run_gemv_mma(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M,
+                 float* d_y, int64_t ldy);
 int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t M,
              float* d_y, int64_t ldy);
 void release_gemm_state(Weights& w);

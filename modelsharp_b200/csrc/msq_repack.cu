@@ -79,48 +79,82 @@ __global__ void widen_kernel(const void* __restrict__ s, int sdt, int64_t off, i
   if (idx < n) out[idx] = load_scale(s, sdt, off + idx);
 }
 
-// One thread per 32-bit word of the decode stream ([block][tile][row][record]).
+// One thread per 32-bit word of the decode stream (layout in msq_internal.cuh).
 __global__ void repack_stream_kernel(const uint8_t* __restrict__ b, const void* __restrict__ scales, int sdt,
                                      const void* __restrict__ zp, int zp_kind, int64_t row0, int n_rows, int K,
-                                     int bs, int nb, int blob, int zp_row_bytes, int rb, int kt, int ntiles,
-                                     int rec_words, int sc_word, int zp_word, uint32_t* __restrict__ out,
-                                     int64_t total_words) {
-  int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+                                     int bs, int nb, int blob, int zp_row_bytes, int ks, int nwk, int groups,
+                                     int kt, int ntiles, int stage_words, int off_sc_w, int off_zp_w,
+                                     uint32_t* __restrict__ out, int64_t total_words) {
+  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (idx >= total_words) return;
-  const int64_t rec = idx / rec_words;
-  const int wi = (int)(idx - rec * rec_words);
-  const int rr = (int)(rec % rb);
-  const int64_t bt = rec / rb;
-  const int t = (int)(bt % ntiles);
-  const int64_t blk = bt / ntiles;
-  const int64_t r = blk * rb + rr;
-  const int nbt = kt / bs;
+  const int64_t stage = idx / stage_words;
+  const int wi = (int)(idx - stage * stage_words);
+  const int tile = (int)(stage % ntiles);
+  const int64_t blk = stage / ntiles;
+  const int nbs = ks / bs;
+  const int chunks = ks / 64;
   uint32_t val = 0;
-  if (r < n_rows) {
-    const int64_t n = row0 + r;
-    if (wi < kt / 8) {
-      const uint8_t* brow = b + n * (int64_t)nb * blob;
+  if (wi < off_sc_w) {
+    // nibble words: [group][slice][chunk][lane][4 words]
+    int r = wi;
+    const int step = r & 3; r >>= 2;
+    const int lane = r & 31; r >>= 5;
+    const int chunk = r % chunks; r /= chunks;
+    const int slice = r % nwk;
+    const int g = r / nwk;
+    const int64_t row0r = blk * 16 * groups + g * 16 + (lane >> 2);
+    const int t = lane & 3;
+    const int64_t kb = (int64_t)tile * kt + (int64_t)slice * ks + chunk * 64 + step * 16 + 2 * t;
+    // slot j -> (row offset, k offset): 0:(0,0) 1:(0,8) 2:(8,0) 3:(8,8) 4:(0,1) 5:(0,9) 6:(8,1) 7:(8,9)
+    const int rofs[8] = {0, 0, 8, 8, 0, 0, 8, 8};
+    const int kofs[8] = {0, 8, 0, 8, 1, 9, 1, 9};
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int64_t k = (int64_t)t * kt + 8 * wi + kSlotK[j];
-        if (k < K) {
-          const int64_t bk = k / bs, i = k - bk * bs;
-          val |= (uint32_t)((brow[bk * blob + (i >> 1)] >> ((i & 1) * 4)) & 0xF) << (4 * j);
+    for (int j = 0; j < 8; ++j) {
+      const int64_t rr = row0r + rofs[j];
+      const int64_t k = kb + kofs[j];
+      if (rr < n_rows && k < K) {
+        const int64_t bk = k / bs, i = k - bk * bs;
+        const uint8_t byte = b[((row0 + rr) * nb + bk) * (int64_t)blob + (i >> 1)];
+        val |= (uint32_t)((byte >> ((i & 1) * 4)) & 0xF) << (4 * j);
+      }
+    }
+  } else if (wi < off_zp_w) {
+    // fp32 scales: [group][slice][block][16 rows]
+    int r = wi - off_sc_w;
+    const int row = r & 15; r >>= 4;
+    const int j = r % nbs; r /= nbs;
+    const int slice = r % nwk;
+    const int g = r / nwk;
+    const int64_t rr = blk * 16 * groups + g * 16 + row;
+    const int64_t bl = ((int64_t)tile * kt + (int64_t)slice * ks) / bs + j;
+    if (rr < n_rows && bl < nb) val = __float_as_uint(load_scale(scales, sdt, (row0 + rr) * nb + bl));
+  } else if (zp_kind == ZP_PACKED) {
+    // packed: [group][slice][block][2 words of 8 nibbles, nibble = row]
+    int r = wi - off_zp_w;
+    const int half = r & 1; r >>= 1;
+    if (r < groups * nwk * nbs) {
+      const int j = r % nbs; r /= nbs;
+      const int slice = r % nwk;
+      const int g = r / nwk;
+      const int64_t bl = ((int64_t)tile * kt + (int64_t)slice * ks) / bs + j;
+      for (int q = 0; q < 8; ++q) {
+        const int64_t rr = blk * 16 * groups + g * 16 + half * 8 + q;
+        if (rr < n_rows && bl < nb) {
+          const uint8_t zb = static_cast<const uint8_t*>(zp)[(row0 + rr) * zp_row_bytes + (bl >> 1)];
+          val |= (uint32_t)((zb >> ((bl & 1) * 4)) & 0xF) << (4 * q);
         }
       }
-    } else if (wi >= sc_word && wi < sc_word + nbt) {
-      const int64_t bl = (int64_t)t * nbt + (wi - sc_word);
-      if (bl < nb) val = __float_as_uint(load_scale(scales, sdt, n * nb + bl));
-    } else if (zp_kind == ZP_PACKED && wi >= zp_word && wi < zp_word + (nbt + 7) / 8) {
-      const int j0 = 8 * (wi - zp_word);
-      const uint8_t* zrow = static_cast<const uint8_t*>(zp) + n * zp_row_bytes;
-      for (int j = 0; j < 8 && j0 + j < nbt; ++j) {
-        const int64_t bl = (int64_t)t * nbt + j0 + j;
-        if (bl < nb) val |= (uint32_t)((zrow[bl >> 1] >> ((bl & 1) * 4)) & 0xF) << (4 * j);
-      }
-    } else if (zp_kind == ZP_F32 && wi >= zp_word && wi < zp_word + nbt) {
-      const int64_t bl = (int64_t)t * nbt + (wi - zp_word);
-      if (bl < nb) val = __float_as_uint(static_cast<const float*>(zp)[n * nb + bl]);
+    }
+  } else if (zp_kind == ZP_F32) {
+    int r = wi - off_zp_w;
+    if (r < groups * nwk * nbs * 16) {
+      const int row = r & 15; r >>= 4;
+      const int j = r % nbs; r /= nbs;
+      const int slice = r % nwk;
+      const int g = r / nwk;
+      const int64_t rr = blk * 16 * groups + g * 16 + row;
+      const int64_t bl = ((int64_t)tile * kt + (int64_t)slice * ks) / bs + j;
+      if (rr < n_rows && bl < nb) val = __float_as_uint(static_cast<const float*>(zp)[(row0 + rr) * nb + bl]);
     }
   }
   out[idx] = val;
@@ -159,49 +193,41 @@ int repack_fast4(cudaStream_t st, Weights& w, const uint8_t* d_b, int n_begin,
   return MSQ_OK;
 }
 
-// Chooses the decode-stream geometry: k-tiles of ~1024 (a multiple of max(bs, 64)), and a
-// row-block height <= 32 that spreads the row blocks evenly over the SMs.
-void plan_stream(Weights& w, int sms) {
+// Decode-stream geometry: warp slices of ks k (a multiple of max(block_size, 64); 128 when
+// K is long enough to fill 16 slices of 128), nwk <= 16 slices per k-tile, and as many
+// 16-row groups per row block as leave the 16 consumer warps busy.
+void plan_stream(Weights& w) {
   const int K = w.K, bs = w.block_size;
   const int unit = bs > 64 ? bs : 64;
-  const int t0 = (K + 1023) / 1024;
-  int kt = (K + t0 - 1) / t0;
-  kt = (kt + unit - 1) / unit * unit;
-  w.kt = kt;
-  w.ntiles = (K + kt - 1) / kt;
-  const int nbt = kt / bs;
-  int zb = w.zp_kind == ZP_PACKED ? (nbt + 7) / 8 * 4 : w.zp_kind == ZP_F32 ? 4 * nbt : 0;
-  int rec = kt / 2 + 4 * nbt + zb;
-  rec = (rec + 15) / 16 * 16;
-  if ((rec / 16) % 2 == 0) rec += 16;
-  w.rec_bytes = rec;
-  w.rec_sc = kt / 2;
-  w.rec_zp = kt / 2 + 4 * nbt;
-  // row-block height: each CTA walks its row blocks in turn, so the kernel time goes as
-  // (row blocks per CTA) x (rows per block); minimise that, preferring taller blocks on ties.
-  const int n = w.n_rows;
-  int best_rb = 1;
-  int64_t best = -1;
-  for (int rb = 32; rb >= 1; --rb) {
-    const int64_t nblk = (n + rb - 1) / rb;
-    const int64_t cost = (nblk + sms - 1) / sms * rb;
-    if (best < 0 || cost < best) {
-      best = cost;
-      best_rb = rb;
-    }
-  }
-  w.rb = best_rb;
-  w.nblk = (n + best_rb - 1) / best_rb;
+  int ks = unit;
+  if (unit <= 128 && K >= 16 * 128) ks = 128;
+  int nwk = (K + ks - 1) / ks;
+  if (nwk > 16) nwk = 16;
+  w.ks = ks;
+  w.nwk = nwk;
+  w.groups = 16 / nwk;
+  w.kt = nwk * ks;
+  w.ntiles = (K + w.kt - 1) / w.kt;
+  w.rb = 16 * w.groups;
+  w.nblk = (w.n_rows + w.rb - 1) / w.rb;
+  const int nbs = ks / bs;
+  const int units = w.groups * nwk * nbs;
+  const int nib = w.rb * w.kt / 2;
+  const int sc = units * 16 * 4;
+  const int zpb = w.zp_kind == ZP_PACKED ? units * 8 : w.zp_kind == ZP_F32 ? units * 64 : 0;
+  w.off_sc = nib;
+  w.off_zp = nib + sc;
+  w.stage_bytes = (nib + sc + zpb + 15) / 16 * 16;
 }
 
 int repack_stream(cudaStream_t st, Weights& w, const uint8_t* d_b, int n_begin, const void* d_scales,
                   int scales_dtype, const void* d_zp) {
   const int T = 256;
-  const int rec_words = w.rec_bytes / 4;
-  const int64_t total = (int64_t)w.nblk * w.ntiles * w.rb * rec_words;
+  const int stage_words = w.stage_bytes / 4;
+  const int64_t total = (int64_t)w.nblk * w.ntiles * stage_words;
   repack_stream_kernel<<<grid_for(total, T), T, 0, st>>>(
       d_b, d_scales, scales_dtype, d_zp, w.zp_kind, n_begin, w.n_rows, w.K, w.block_size, w.nb, w.blob,
-      w.zp_row_bytes, w.rb, w.kt, w.ntiles, rec_words, w.rec_sc / 4, w.rec_zp / 4,
+      w.zp_row_bytes, w.ks, w.nwk, w.groups, w.kt, w.ntiles, stage_words, w.off_sc / 4, w.off_zp / 4,
       reinterpret_cast<uint32_t*>(w.strm), total);
   note_launch();
   MSQ_CUDA_TRY(cudaGetLastError(), "stream repack launch");

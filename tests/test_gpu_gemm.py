@@ -1,0 +1,88 @@
+"""tcgen05 prefill GEMM against the parity checker (needs a B200).
+
+Bar: rel-L2 <= 5e-3 against the fp32 reference (the weights enter the tensor core as fp16
+(q - zp) * s). Large M is checked on sampled rows of A (rows are independent).
+"""
+import numpy as np
+import pytest
+import torch
+
+from modelsharp_b200 import QuantizedWeights, synth
+from modelsharp_b200 import _native as N
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+TOL_TC = 5e-3
+
+
+def gemm(c, dev, a=None, path=N.PATH_GEMM):
+    w = QuantizedWeights(c["b"], c["scales"], c["zp"], c["N"], c["K"], 4, c["block_size"], device=dev)
+    a_t = torch.from_numpy(np.ascontiguousarray(c["a"] if a is None else a)).to(dev)
+    y = w.matmul(a_t, path=path)
+    torch.cuda.synchronize(dev)
+    assert N.lib().msq_device_status(None, None) == N.MSQ_OK, N.last_error()
+    return y.cpu().numpy()
+
+
+def sampled_ref(c, rows):
+    return np.concatenate([oracle.managed(c, rows=r) for r in rows], axis=0)
+
+
+@pytest.mark.parametrize("M,N_,K,bs,zp", [
+    (17, 256, 256, 32, "packed"),      # smallest GEMM M, one partial row tile
+    (64, 1000, 4160, 128, "packed"),   # ragged N tile and ragged last k-stage
+    (128, 512, 1024, 32, "none"),
+    (200, 384, 2048, 64, "float"),
+    (300, 4096, 4096, 128, "packed"),  # BN=256 tiles
+])
+def test_gemm_parity_fp32_activations(cuda_device, M, N_, K, bs, zp):
+    c = synth.make_case(31, M, N_, K, 4, bs, zp, scale_lo=0.001, scale_hi=0.01)
+    y = gemm(c, cuda_device)
+    assert N.last_path().startswith("gemm_tc")
+    assert oracle.rel_l2(y, oracle.managed(c)) <= TOL_TC
+
+
+@pytest.mark.parametrize("M", [512, 2048])
+def test_gemm_prefill_config_fp16(cuda_device, M):
+    """K=4096, N=14336, bs=32, zero points, fp16 A and fp16 scales."""
+    c = synth.make_case(3, M, 14336, 4096, 4, 32, "packed", a_dtype="f16", scale_dtype="f16",
+                        scale_lo=0.001, scale_hi=0.01)
+    y = gemm(c, cuda_device)
+    rows = [slice(0, 48), slice(M // 2, M // 2 + 16), slice(M - 64, M)]
+    ref = sampled_ref(c, rows)
+    got = np.concatenate([y[r] for r in rows], axis=0)
+    assert oracle.rel_l2(got, ref) <= TOL_TC
+
+
+def test_gemm_auto_routes_prefill(cuda_device):
+    c = synth.make_case(32, 40, 640, 1024, 4, 128, "packed")
+    w = QuantizedWeights(c["b"], c["scales"], c["zp"], 640, 1024, 4, 128, device=cuda_device)
+    y = w.matmul(torch.from_numpy(c["a"]).to(cuda_device))
+    torch.cuda.synchronize()
+    assert N.last_path().startswith("gemm_tc")
+    assert oracle.rel_l2(y.cpu().numpy(), oracle.managed(c)) <= TOL_TC
+
+
+def test_gemm_writes_only_its_shard(cuda_device):
+    c = synth.make_case(33, 130, 300, 512, 4, 32, "packed")
+    w = QuantizedWeights(c["b"], c["scales"], c["zp"], 300, 512, 4, 32, rows=(100, 300), device=cuda_device)
+    y = torch.full((130, 320), float("nan"), device=cuda_device)
+    w.matmul(torch.from_numpy(c["a"]).to(cuda_device), out=y[:, 100:300], ldy=320, path=N.PATH_GEMM)
+    torch.cuda.synchronize()
+    out = y.cpu().numpy()
+    assert np.isnan(out[:, :100]).all() and np.isnan(out[:, 300:]).all()
+    assert oracle.rel_l2(out[:, 100:300], oracle.managed(c)[:, 100:300]) <= TOL_TC
+
+
+def test_gemm_bf16_and_unaligned_half(cuda_device):
+    c = synth.make_case(34, 70, 256, 1000, 4, 32, "packed")  # K % 8 != 0 -> scratch copy
+    a16 = torch.from_numpy(c["a"]).to(torch.float16)
+    ref = oracle.managed(dict(c, a=a16.float().numpy()))
+    w = QuantizedWeights(c["b"], c["scales"], c["zp"], 256, 1000, 4, 32, device=cuda_device)
+    y = w.matmul(a16.to(cuda_device), path=N.PATH_GEMM).cpu().numpy()
+    assert oracle.rel_l2(y, ref) <= TOL_TC
+    ab = torch.from_numpy(c["a"]).to(torch.bfloat16)
+    refb = oracle.managed(dict(c, a=ab.float().numpy()))
+    yb = w.matmul(ab.to(cuda_device), path=N.PATH_GEMM).cpu().numpy()
+    assert oracle.rel_l2(yb, refb) <= TOL_TC
