@@ -268,6 +268,37 @@ int cuda_fail(cudaError_t e, const char* what) {
 }
 
 void note_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+namespace {
+std::mutex g_pool_mu;
+cudaMemPool_t g_pools[64] = {};
+}  // namespace
+
+int scratch_alloc(void** p, size_t bytes, cudaStream_t st) {
+  int dev = 0;
+  MSQ_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+  cudaMemPool_t pool = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_pool_mu);
+    if (dev >= 0 && dev < 64) pool = g_pools[dev];
+    if (!pool) {
+      cudaMemPoolProps props = {};
+      props.allocType = cudaMemAllocationTypePinned;
+      props.location.type = cudaMemLocationTypeDevice;
+      props.location.id = dev;
+      MSQ_CUDA_TRY(cudaMemPoolCreate(&pool, &props), "cudaMemPoolCreate");
+      uint64_t keep = ~0ull;
+      MSQ_CUDA_TRY(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep), "pool attribute");
+      if (dev >= 0 && dev < 64) g_pools[dev] = pool;
+    }
+  }
+  MSQ_CUDA_TRY(cudaMallocFromPoolAsync(p, bytes, pool, st), "scratch allocation");
+  return MSQ_OK;
+}
+
+void scratch_free(void* p, cudaStream_t st) {
+  if (p) cudaFreeAsync(p, st);
+}
 void note_path(const char* name) { t_last_path = name; }
 
 int num_sms(int device) {
@@ -423,13 +454,15 @@ int msq_matmul_host(void* cu_ctx, void* stream, msq_weights_t h, const void* a, 
   const size_t abytes = (size_t)M * w->K * act_elem_size(a_dtype);
   const size_t ybytes = (size_t)M * w->n_rows * sizeof(float);
   void* da = nullptr;
-  float* dy = nullptr;
-  cudaError_t e = cudaMallocAsync(&da, abytes, st);
-  if (e == cudaSuccess) e = cudaMallocAsync(reinterpret_cast<void**>(&dy), ybytes, st);
-  if (e != cudaSuccess) {
-    if (da) cudaFreeAsync(da, st);
-    return cuda_fail(e, "msq_matmul_host allocation");
+  void* dyv = nullptr;
+  int arc = scratch_alloc(&da, abytes, st);
+  if (arc == MSQ_OK) arc = scratch_alloc(&dyv, ybytes, st);
+  if (arc != MSQ_OK) {
+    scratch_free(da, st);
+    return arc;
   }
+  float* dy = static_cast<float*>(dyv);
+  cudaError_t e;
   int rc = MSQ_OK;
   e = cudaMemcpyAsync(da, a, abytes, cudaMemcpyHostToDevice, st);
   if (e != cudaSuccess) rc = cuda_fail(e, "msq_matmul_host upload");
@@ -438,8 +471,8 @@ int msq_matmul_host(void* cu_ctx, void* stream, msq_weights_t h, const void* a, 
     e = cudaMemcpyAsync(y, dy, ybytes, cudaMemcpyDeviceToHost, st);
     if (e != cudaSuccess) rc = cuda_fail(e, "msq_matmul_host download");
   }
-  cudaFreeAsync(da, st);
-  cudaFreeAsync(dy, st);
+  scratch_free(da, st);
+  scratch_free(dy, st);
   e = cudaStreamSynchronize(st);
   if (rc == MSQ_OK && e != cudaSuccess) rc = cuda_fail(e, "msq_matmul_host synchronize");
   return rc;

@@ -73,8 +73,8 @@ __device__ __forceinline__ bool wait_abort(uint64_t* bar, uint32_t parity, volat
   if (ptx::mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = ptx::globaltimer();
   for (uint32_t i = 1;; ++i) {
-    if (ptx::mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0) {
+    if (ptx::mbar_try_wait_sleep(bar, parity)) return true;
+    if ((i & 7u) == 0) {
       if (*abort_flag) return false;
       if (ptx::globaltimer() - t0 > ptx::kWaitBudgetNs) {
         *abort_flag = 1;
@@ -395,7 +395,8 @@ int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t 
   void* scratch = nullptr;
   if (a_dtype != MSQ_DT_F16 || (w.K % 8) != 0 || (reinterpret_cast<uintptr_t>(d_a) & 15) != 0) {
     lda = (w.K + 7) / 8 * 8;
-    MSQ_CUDA_TRY(cudaMallocAsync(&scratch, sizeof(__half) * (size_t)M * lda, st), "GEMM activation scratch");
+    const int arc = scratch_alloc(&scratch, sizeof(__half) * (size_t)M * lda, st);
+    if (arc != MSQ_OK) return arc;
     to_half_kernel<<<num_sms(w.device) * 4, 256, 0, st>>>(d_a, a_dtype, M, w.K, static_cast<__half*>(scratch), lda);
     note_launch();
     a16 = scratch;
@@ -430,7 +431,7 @@ int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t 
     }
     if (rc == MSQ_OK) note_path(big ? "gemm_tc_n256" : "gemm_tc_n128");
   }
-  if (scratch) cudaFreeAsync(scratch, st);
+  scratch_free(scratch, st);
   return rc;
 }
 

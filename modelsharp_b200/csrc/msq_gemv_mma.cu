@@ -1,24 +1,25 @@
-// Decode GEMV for MatMulNBits on the tensor cores (bits = 4, block_size 32 / 64 / 128, M <= 4
-// per pass). Memory-bound: one producer warp streams the repacked weight stages
-// (cp.async.bulk, up to 8 in flight); 16 consumer warps turn each lane's 32-bit nibble word
-// straight into the A fragment of mma.m16n8k16 (rows r and r+8, four k each) and multiply it
-// against the activations held as B fragments.
+// Decode GEMV for MatMulNBits on the tensor cores with exact integer arithmetic
+// (bits = 4, block_size 32 / 64 / 128, M <= 4 per pass).
+//
+// Memory-bound: one producer warp streams the repacked weight stages (16 weight rows x one
+// k-tile, 17-35 KB, one cp.async.bulk each) through a small shared-memory ring; the 16
+// consumer warps split every stage by 64/128-k units and run mma.m16n8k32 (u8 x s8 -> s32).
 //
 // Exactness. The reference computes sum_k a[m,k] * ((q - zp) * s) in fp32
-// (MatMulNBitsKernel.cs:236-261). Here, per quantisation block b:
-//     y[m,n] += s[n,b] * ( sum_{k in b} q[n,k] * a'[m,k]  -  zp[n,b] * S_b[m] ) * 2^-sigma_m
-// with a' = a * 2^sigma_m (a power-of-two row scale putting max|a'| just under 2^14) and
-// S_b = sum_{k in b} a'. The tensor core sees q exactly (fp16 1024+q minus 1024) and a' as
-// two fp16 columns hi = fp16(a'), lo = fp16(a' - hi), so a' is carried to ~2^-22 and every
-// product is exact in the fp32 accumulator; scale and zero point are applied in fp32. The
-// parity bar against the fp32 reference is rel-L2 <= 1e-5.
+// (MatMulNBitsKernel.cs:236-261). Here each quantisation block b of each row of A becomes a
+// 24-bit fixed-point integer vector a_int = rint(a * 2^sigma_b) (max|a * 2^sigma_b| < 2^22,
+// sigma_b chosen per block from the block's own maximum), split into three balanced int8
+// digits a_int = d0 + 256 d1 + 65536 d2 that form B columns. The tensor core returns
+// D_i = sum_{k in b} q[n,k] * d_i[k] exactly in s32, and
+//     y[m,n] += s[n,b] * 2^-sigma_b * ( D_0 + 256 D_1 + 65536 D_2  -  zp[n,b] * S_b )
+// with S_b = sum_{k in b} a_int exact in s32. Only the rounding of a to 2^-24 of its block
+// maximum and the fp32 block combination round; parity is checked at rel-L2 <= 1e-5 against
+// the fp32 reference. Block-local scales need no row-wide reduction, so the activation
+// preparation is one pass of loads and warp shuffles.
 //
-// Decode: one word holds, in nibble slots 0..7, the codes of (row r, k 2t), (r, 2t+8),
-// (r+8, 2t), (r+8, 2t+8), (r, 2t+1), (r, 2t+9), (r+8, 2t+1), (r+8, 2t+9). The half2 pairs
-// of the A fragment come out of (x & 0x000F000F) | 0x64006400 (k 2t, 2t+1 of row r) and of
-// (x & 0x00F000F0) | 0x64006400 (k 2t+8, 2t+9, i.e. 16 q), then the same on x >> 8 for row
-// r+8; activations at k%16 >= 8 are staged pre-divided by 16 to match. Per 8 weights:
-// 1 shift, 4 LOP3, 4 HSUB2 and one HMMA.
+// Decode: a lane's 32-bit word holds, byte j, the codes of (row r, k 4t+j) (low nibble)
+// and (row r+8, k 4t+j) (high nibble), so (x & 0x0F0F0F0F) and ((x >> 4) & 0x0F0F0F0F) are
+// directly the u8 A-fragment registers of rows r and r+8: three integer ops per 8 weights.
 #include "msq_internal.cuh"
 #include "msq_ptx.cuh"
 
@@ -29,9 +30,9 @@ namespace {
 
 constexpr int kConsumers = 16;
 constexpr int kThreads = (kConsumers + 1) * 32;
-constexpr int kMaxStages = 8;
+constexpr int kMaxSlots = 8;
 constexpr int kSmemMax = 227 * 1024;
-constexpr int kMaxM = 4;  // B columns: (hi, lo) x 4 rows of A = one n8 tile
+constexpr int kMaxM = 4;  // B columns: 4 per A row (3 digits + 1 zero) -> two n8 tiles for 4 rows
 
 __device__ int g_mma_err;
 
@@ -43,9 +44,11 @@ struct Args {
   int mc;  // A rows in this pass (<= 4)
   float* y;
   int64_t ldy;
-  int n_rows, K, bs, ks, nwk, groups, kt, ntiles, rb, nblk, stage_bytes, off_sc, off_zp, zp_kind;
-  int nst, seg_tiles, rows_cta;
-  int off_ahl, off_s, off_ysum, off_bar, off_ring;  // shared-memory offsets (bytes)
+  int n_rows, K, kt, ntiles, nblk, stage_bytes, off_sc, off_zp, zp_kind;
+  int nslots, rows_cta;
+  int kp;     // ntiles * kt: K padded to whole tiles
+  int a_vec;  // rows of A may be read 4 elements at a time
+  int off_dig, off_s, off_ysum, off_bar, off_ring;  // shared-memory offsets (bytes)
 };
 
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code) {
@@ -53,8 +56,8 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
   if (ptx::mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = ptx::globaltimer();
   for (uint32_t i = 1;; ++i) {
-    if (ptx::mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0) {
+    if (ptx::mbar_try_wait_sleep(bar, parity)) return true;
+    if ((i & 7u) == 0) {
       if (*abort_flag) return false;
       if (ptx::globaltimer() - t0 > ptx::kWaitBudgetNs) {
         *abort_flag = 1;
@@ -65,41 +68,88 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
   }
 }
 
-__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
+__device__ __forceinline__ void imma(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                     uint32_t b1) {
   asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
       "{%0, %1, %2, %3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// (1024 + q) pairs -> q pairs, exact in fp16.
-__device__ __forceinline__ uint32_t q_pair(uint32_t masked) {
-  const uint32_t h = masked | 0x64006400u;
-  const uint32_t k1024 = 0x64006400u;
-  __half2 v = __hsub2(*reinterpret_cast<const __half2*>(&h), *reinterpret_cast<const __half2*>(&k1024));
-  return *reinterpret_cast<const uint32_t*>(&v);
+// A[m0 + m][k .. k+3] as fp32, zeros past K.
+__device__ __forceinline__ float4 load4(const Args& p, int m, int k) {
+  const int64_t base = (p.m0 + m) * (int64_t)p.K + k;
+  if (p.a_vec && k + 4 <= p.K) {
+    if (p.a_dtype == MSQ_DT_F32) return *reinterpret_cast<const float4*>(static_cast<const float*>(p.a) + base);
+    const uint2 r = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.a) + base);
+    float2 lo, hi;
+    if (p.a_dtype == MSQ_DT_F16) {
+      lo = __half22float2(*reinterpret_cast<const __half2*>(&r.x));
+      hi = __half22float2(*reinterpret_cast<const __half2*>(&r.y));
+    } else {
+      lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.x));
+      hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.y));
+    }
+    return make_float4(lo.x, lo.y, hi.x, hi.y);
+  }
+  float v[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) v[j] = k + j < p.K ? load_act(p.a, p.a_dtype, base + j) : 0.f;
+  return make_float4(v[0], v[1], v[2], v[3]);
 }
 
-template <int KSTEPS, int BSTEPS>
+// rint(x * 2^sigma) as a 24-bit integer.
+__device__ __forceinline__ int fixed24(float x, float sc) { return __float2int_rn(x * sc); }
+
+// Writes the three balanced int8 digits of 4 consecutive k of row m (columns 4m..4m+2; the
+// fourth column of each row stays zero) and returns their exact integer sum.
+__device__ __forceinline__ int store_digits(int8_t* dig, int kp, int m, int k, float4 v, float sc) {
+  const int a[4] = {fixed24(v.x, sc), fixed24(v.y, sc), fixed24(v.z, sc), fixed24(v.w, sc)};
+  uint32_t w0 = 0, w1 = 0, w2 = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int d0 = ((a[j] + 128) & 255) - 128;
+    const int r1 = (a[j] - d0) >> 8;
+    const int d1 = ((r1 + 128) & 255) - 128;
+    const int d2 = (r1 - d1) >> 8;
+    w0 |= (uint32_t)(d0 & 255) << (8 * j);
+    w1 |= (uint32_t)(d1 & 255) << (8 * j);
+    w2 |= (uint32_t)(d2 & 255) << (8 * j);
+  }
+  *reinterpret_cast<uint32_t*>(dig + (4 * m + 0) * kp + k) = w0;
+  *reinterpret_cast<uint32_t*>(dig + (4 * m + 1) * kp + k) = w1;
+  *reinterpret_cast<uint32_t*>(dig + (4 * m + 2) * kp + k) = w2;
+  *reinterpret_cast<uint32_t*>(dig + (4 * m + 3) * kp + k) = 0u;
+  return (a[0] + a[1]) + (a[2] + a[3]);
+}
+
+// BS = quantisation block size (32 / 64 / 128); NT = n8 tiles of B (1: M <= 2, 2: M <= 4).
+// A "unit" is max(BS, 64) k: one or two 64-k chunks (a uint4 of code words per lane each).
+template <int BS, int NT>
 __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
-  constexpr int NBS = KSTEPS / BSTEPS;  // quantisation blocks per warp slice
+  constexpr int UNIT = BS > 64 ? BS : 64;
+  constexpr int CH = UNIT / 64;     // 64-k chunks per unit
+  constexpr int UB = UNIT / BS;     // blocks per unit
+  constexpr int STEPS = UNIT / 32;  // k32 mma steps per unit
+  constexpr int BSTEPS = BS / 32;   // k32 steps per block
+  constexpr int UPW = 2;            // units per warp per tile (kt <= 32 units)
   extern __shared__ __align__(16) uint8_t smem[];
-  float* sig = reinterpret_cast<float*>(smem);               // [0..3] 2^sigma, [4..7] 2^-sigma, [8..] scratch
-  __half* ahl = reinterpret_cast<__half*>(smem + p.off_ahl);  // [2*mc][segk]
-  float* sblk = reinterpret_cast<float*>(smem + p.off_s);     // [mc][segk/bs]
-  float* ysum = reinterpret_cast<float*>(smem + p.off_ysum);  // [nwk][rows_cta][mc]
+  int8_t* dig = reinterpret_cast<int8_t*>(smem + p.off_dig);  // [4*mc][kp] digits
+  int* sblk = reinterpret_cast<int*>(smem + p.off_s);         // [mc][kp/BS] exact block sums of a_int
+  float* sinv = reinterpret_cast<float*>(sblk + p.mc * (p.kp / BS));  // [mc][kp/BS] 2^-sigma_b
+  float* ysum = reinterpret_cast<float*>(smem + p.off_ysum);  // [16 warps][rows_cta][mc][2]
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bar);
-  uint64_t* empty = full + kMaxStages;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kMaxStages);
+  uint64_t* empty = full + kMaxSlots;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kMaxSlots);
   uint8_t* ring = smem + p.off_ring;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int grid = gridDim.x;
   const int nb_cta = (p.nblk - (int)blockIdx.x + grid - 1) / grid;  // row blocks of this CTA
+  const int T = p.ntiles;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < p.nst; ++s) {
+    for (int s = 0; s < p.nslots; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], kConsumers);
     }
@@ -109,26 +159,31 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
   __syncthreads();
 
   if (warp == kConsumers) {
-    // ---------------- producer
+    // ---------------- producer: stages in (tile, row block) order
     if (lane == 0) {
-      int issued = 0;
+      int issued = 0, s = 0;
+      uint32_t wrap = 0;
       bool ok = true;
-      for (int t = 0; t < p.ntiles && ok; ++t)
-        for (int i = 0; i < nb_cta && ok; ++i) {
+      for (int t = 0; t < T && ok; ++t)
+        for (int i = 0; i < nb_cta; ++i) {
+          if (issued >= p.nslots && !wait_or_abort(&empty[s], wrap ^ 1u, abort_flag, ptx::kErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
           const int b = blockIdx.x + i * grid;
-          const int s = issued % p.nst;
-          const uint32_t u = issued / p.nst;
-          if (issued >= p.nst) ok = wait_or_abort(&empty[s], (u - 1) & 1, abort_flag, ptx::kErrTimeoutEmpty);
-          if (!ok) break;
           ptx::mbar_arrive_expect_tx(&full[s], p.stage_bytes);
           ptx::bulk_g2s(ring + (size_t)s * p.stage_bytes,
-                        p.strm + ((int64_t)b * p.ntiles + t) * (int64_t)p.stage_bytes, p.stage_bytes, &full[s]);
+                        p.strm + ((int64_t)b * T + t) * (int64_t)p.stage_bytes, p.stage_bytes, &full[s]);
           ++issued;
+          if (++s == p.nslots) {
+            s = 0;
+            wrap ^= 1u;
+          }
         }
-      for (int s = 0; s < p.nst && s < issued; ++s) {  // in-flight copies must land before exit
-        const int last = s + (issued - 1 - s) / p.nst * p.nst;
+      for (int q = 0; q < p.nslots && q < issued; ++q) {  // in-flight copies must land before exit
+        const int last = q + (issued - 1 - q) / p.nslots * p.nslots;
         const unsigned long long t0 = ptx::globaltimer();
-        while (!ptx::mbar_try_wait(&full[s], (last / p.nst) & 1)) {
+        while (!ptx::mbar_try_wait(&full[q], (last / p.nslots) & 1)) {
           if (ptx::globaltimer() - t0 > ptx::kWaitBudgetNs) {
             atomicCAS(&g_mma_err, 0, ptx::kErrTimeoutDrain);
             break;
@@ -142,159 +197,195 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
   // ---------------- consumers (512 threads, named barrier 1)
   const int tid = threadIdx.x;
   const int mc = p.mc;
-  for (int i = tid; i < p.nwk * p.rows_cta * mc; i += kConsumers * 32) ysum[i] = 0.f;
+  for (int i = tid; i < kConsumers * p.rows_cta * mc * 2; i += kConsumers * 32) ysum[i] = 0.f;
 
-  // per-row power-of-two prescale: max|a'| in [2^13, 2^14)
-  {
-    float mx[kMaxM] = {0.f, 0.f, 0.f, 0.f};
-    for (int k = tid; k < p.K; k += kConsumers * 32)
+  // ---- activations: one pass. Loads in flight at once (float4, U deep); per quantisation
+  // block (GL consecutive lanes) a shuffle max picks 2^sigma_b, the digits are written and a
+  // shuffle sum gives the exact block sum of a_int.
+  constexpr int U = 8;
+  constexpr int kC = kConsumers * 32;
+  constexpr int GL = BS / 4;  // float4 per quantisation block (8 / 16 / 32 lanes)
+  const int n4row = p.kp / 4;
+  const int n4 = mc * n4row;
+  for (int base = 0; base < n4; base += kC * U) {
+    const int nu = min(U, (n4 - base + kC - 1) / kC);  // warp-uniform
+    float4 v[U];
 #pragma unroll
-      for (int m = 0; m < kMaxM; ++m)
-        if (m < mc) mx[m] = fmaxf(mx[m], fabsf(load_act(p.a, p.a_dtype, (p.m0 + m) * (int64_t)p.K + k)));
-#pragma unroll
-    for (int m = 0; m < kMaxM; ++m) {
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) mx[m] = fmaxf(mx[m], __shfl_xor_sync(0xffffffffu, mx[m], off));
-      if (lane == 0) sig[8 + warp * kMaxM + m] = mx[m];
+    for (int u = 0; u < U; ++u) {
+      const int f = base + tid + u * kC;
+      const int m = f / n4row;
+      v[u] = (u < nu && f < n4) ? load4(p, m, 4 * (f - m * n4row)) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    ptx::named_bar_sync(1, kConsumers * 32);
-    if (tid < kMaxM) {
-      float v = 0.f;
-      for (int w = 0; w < kConsumers; ++w) v = fmaxf(v, sig[8 + w * kMaxM + tid]);
-      int e = 0;
-      if (v > 0.f && isfinite(v)) frexpf(v, &e);
-      int s = 14 - e;
-      s = max(-100, min(100, s));
-      sig[tid] = ldexpf(1.f, s);
-      sig[4 + tid] = ldexpf(1.f, -s);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (u < nu) {
+        const int f = base + tid + u * kC;
+        float bmax = fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w)));
+#pragma unroll
+        for (int off = 1; off < GL; off <<= 1) bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, off));
+        int e = 0;
+        if (bmax > 0.f && isfinite(bmax)) frexpf(bmax, &e);
+        const int sh = max(-120, min(120, 22 - e));
+        int bsum = 0;
+        if (f < n4) {
+          const int m = f / n4row;
+          bsum = store_digits(dig, p.kp, m, 4 * (f - m * n4row), v[u], ldexpf(1.f, sh));
+        }
+#pragma unroll
+        for (int off = 1; off < GL; off <<= 1) bsum += __shfl_xor_sync(0xffffffffu, bsum, off);
+        if (f < n4 && (lane & (GL - 1)) == 0) {
+          sblk[f / GL] = bsum;
+          sinv[f / GL] = ldexpf(1.f, -sh);
+        }
+      }
     }
-    ptx::named_bar_sync(1, kConsumers * 32);
   }
+  ptx::named_bar_sync(1, kConsumers * 32);
 
-  const bool active = warp < p.groups * p.nwk;
-  const int g = warp / p.nwk, w = warp % p.nwk;
+  // ---- main loop: tile t outer, this CTA's row blocks inner; warp w takes units w, w+16
   const int grp = lane >> 2, tq = lane & 3;
-  constexpr int chunks = KSTEPS / 4;
-  const int segk_full = p.seg_tiles * p.kt;
-  int it = 0;
-
-  for (int seg0 = 0; seg0 < p.ntiles; seg0 += p.seg_tiles) {
-    const int ntl = min(p.seg_tiles, p.ntiles - seg0);
-    const int segk = ntl * p.kt;
-    const int64_t kbase = (int64_t)seg0 * p.kt;
-    // ---- stage split activations: hi / lo fp16 columns (k%16 >= 8 pre-divided by 16)
-    for (int idx = tid; idx < mc * segk; idx += kConsumers * 32) {
-      const int m = idx / segk, kl = idx - m * segk;
-      const int64_t kg = kbase + kl;
-      float x = kg < p.K ? load_act(p.a, p.a_dtype, (p.m0 + m) * (int64_t)p.K + kg) * sig[m] : 0.f;
-      if ((kl & 15) >= 8) x *= 0.0625f;
-      const __half hi = __float2half_rn(x);
-      const __half lo = __float2half_rn(x - __half2float(hi));
-      ahl[(2 * m) * segk_full + kl] = hi;
-      ahl[(2 * m + 1) * segk_full + kl] = lo;
+  const int units = p.kt / UNIT;
+  const int nbp = p.kp / BS;
+  int rs = 0;
+  uint32_t rph = 0;
+  for (int t = 0; t < T; ++t) {
+    // B fragments of this warp's units (digits of columns grp + 8j), held across row blocks
+    uint32_t bf[UPW][STEPS][NT][2];
+    int sv[UPW][UB][NT];      // block sums of a_int for this lane's A row(s)
+    float sif[UPW][UB][NT];   // 2^-sigma of those blocks
+#pragma unroll
+    for (int uu = 0; uu < UPW; ++uu) {
+      const int u = warp + uu * kConsumers;
+      const int kk0 = t * p.kt + u * UNIT;
+#pragma unroll
+      for (int st = 0; st < STEPS; ++st)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const int col = nt * 8 + grp;
+          const bool ok = u < units && col < 4 * mc;
+          const int8_t* d = dig + col * p.kp + kk0 + 32 * st + 4 * tq;
+          bf[uu][st][nt][0] = ok ? *reinterpret_cast<const uint32_t*>(d) : 0u;
+          bf[uu][st][nt][1] = ok ? *reinterpret_cast<const uint32_t*>(d + 16) : 0u;
+        }
+#pragma unroll
+      for (int bl = 0; bl < UB; ++bl)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const int m = nt * 2 + (tq >> 1);
+          const bool okb = u < units && m < mc;
+          sv[uu][bl][nt] = okb ? sblk[m * nbp + kk0 / BS + bl] : 0;
+          sif[uu][bl][nt] = okb ? sinv[m * nbp + kk0 / BS + bl] : 0.f;
+        }
     }
-    // ---- block sums of a' (before the /16)
-    const int nbseg = segk / p.bs;
-    for (int idx = tid; idx < mc * nbseg; idx += kConsumers * 32) {
-      const int m = idx / nbseg, jb = idx - m * nbseg;
-      float s = 0.f;
-      for (int q = 0; q < p.bs; ++q) {
-        const int64_t kg = kbase + (int64_t)jb * p.bs + q;
-        if (kg < p.K) s += load_act(p.a, p.a_dtype, (p.m0 + m) * (int64_t)p.K + kg);
-      }
-      sblk[m * (segk_full / p.bs) + jb] = s * sig[m];
-    }
-    ptx::named_bar_sync(1, kConsumers * 32);
 
-    for (int t = seg0; t < seg0 + ntl; ++t) {
-      // B fragments of this warp's k-slice (reused across the CTA's row blocks)
-      uint32_t bf0[KSTEPS], bf1[KSTEPS];
-      float sv[NBS];  // block sums of this lane's A row
-      const int kl0 = (t - seg0) * p.kt + w * p.ks;
-      const bool colok = active && grp < 2 * mc;
+    for (int i = 0; i < nb_cta; ++i) {
+      const bool ok = wait_or_abort(&full[rs], rph, abort_flag, ptx::kErrTimeoutFull);
+      if (ok) {
+        const uint8_t* base = ring + rs * p.stage_bytes;
+        const float* scp = reinterpret_cast<const float*>(base + p.off_sc);
+        float y0[NT], y1[NT];
 #pragma unroll
-      for (int s = 0; s < KSTEPS; ++s) {
-        bf0[s] = colok ? *reinterpret_cast<const uint32_t*>(ahl + grp * segk_full + kl0 + 16 * s + 2 * tq) : 0u;
-        bf1[s] = colok ? *reinterpret_cast<const uint32_t*>(ahl + grp * segk_full + kl0 + 16 * s + 2 * tq + 8) : 0u;
-      }
+        for (int nt = 0; nt < NT; ++nt) y0[nt] = y1[nt] = 0.f;
 #pragma unroll
-      for (int j = 0; j < NBS; ++j)
-        sv[j] = (active && tq < mc) ? sblk[tq * (segk_full / p.bs) + kl0 / p.bs + j] : 0.f;
-
-      for (int i = 0; i < nb_cta; ++i, ++it) {
-        const int s = it % p.nst;
-        const uint32_t u = it / p.nst;
-        const bool ok = wait_or_abort(&full[s], u & 1, abort_flag, ptx::kErrTimeoutFull);
-        if (ok && active) {
-          const uint8_t* base = ring + (size_t)s * p.stage_bytes;
-          const uint4* nibp = reinterpret_cast<const uint4*>(base) + ((g * p.nwk + w) * chunks) * 32 + lane;
-          uint32_t words[KSTEPS];
+        for (int uu = 0; uu < UPW; ++uu) {
+          const int u = warp + uu * kConsumers;
+          if (u < units) {
+            const uint4* nib = reinterpret_cast<const uint4*>(base) + u * CH * 32 + lane;
+            uint32_t wv[4 * CH];
 #pragma unroll
-          for (int c = 0; c < KSTEPS / 4; ++c) {
-            const uint4 v = nibp[c * 32];
-            words[4 * c + 0] = v.x;
-            words[4 * c + 1] = v.y;
-            words[4 * c + 2] = v.z;
-            words[4 * c + 3] = v.w;
-          }
-          const int unit0 = (g * p.nwk + w) * NBS;
-          const float* scp = reinterpret_cast<const float*>(base + p.off_sc);
-          float y0 = 0.f, y1 = 0.f;
-#pragma unroll
-          for (int j = 0; j < NBS; ++j) {
-            const float s0 = scp[(unit0 + j) * 16 + grp];
-            const float s1 = scp[(unit0 + j) * 16 + grp + 8];
-            float z0 = 8.f, z1 = 8.f;
-            if (p.zp_kind == ZP_PACKED) {
-              const uint2 zw = reinterpret_cast<const uint2*>(base + p.off_zp)[unit0 + j];
-              z0 = (float)((zw.x >> (4 * grp)) & 0xF);
-              z1 = (float)((zw.y >> (4 * grp)) & 0xF);
-            } else if (p.zp_kind == ZP_F32) {
-              const float* zp = reinterpret_cast<const float*>(base + p.off_zp);
-              z0 = zp[(unit0 + j) * 16 + grp];
-              z1 = zp[(unit0 + j) * 16 + grp + 8];
+            for (int c = 0; c < CH; ++c) {
+              const uint4 q4 = nib[c * 32];
+              wv[4 * c + 0] = q4.x;
+              wv[4 * c + 1] = q4.y;
+              wv[4 * c + 2] = q4.z;
+              wv[4 * c + 3] = q4.w;
             }
-            float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int q = j * BSTEPS; q < (j + 1) * BSTEPS; ++q) {
-              const uint32_t x = words[q];
-              const uint32_t x8 = x >> 8;
-              mma16816(c, q_pair(x & 0x000F000Fu), q_pair(x8 & 0x000F000Fu), q_pair(x & 0x00F000F0u),
-                       q_pair(x8 & 0x00F000F0u), bf0[q], bf1[q]);
+            for (int bl = 0; bl < UB; ++bl) {
+              const int blk_local = u * UB + bl;
+              const float s0 = scp[blk_local * 16 + grp];
+              const float s1 = scp[blk_local * 16 + grp + 8];
+              float z0 = 8.f, z1 = 8.f;
+              if (p.zp_kind == ZP_PACKED) {
+                const uint2 zw = reinterpret_cast<const uint2*>(base + p.off_zp)[blk_local];
+                z0 = (float)((zw.x >> (4 * grp)) & 0xF);
+                z1 = (float)((zw.y >> (4 * grp)) & 0xF);
+              } else if (p.zp_kind == ZP_F32) {
+                const float* zf = reinterpret_cast<const float*>(base + p.off_zp);
+                z0 = zf[blk_local * 16 + grp];
+                z1 = zf[blk_local * 16 + grp + 8];
+              }
+              int c[NT][4];
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) c[nt][0] = c[nt][1] = c[nt][2] = c[nt][3] = 0;
+#pragma unroll
+              for (int q = 0; q < BSTEPS; ++q) {
+                const int st = bl * BSTEPS + q;
+                const uint32_t x0 = wv[2 * st], x1 = wv[2 * st + 1];
+                const uint32_t lo0 = x0 & 0x0F0F0F0Fu, hi0 = (x0 >> 4) & 0x0F0F0F0Fu;
+                const uint32_t lo1 = x1 & 0x0F0F0F0Fu, hi1 = (x1 >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+                  imma(c[nt], lo0, hi0, lo1, hi1, bf[uu][st][nt][0], bf[uu][st][nt][1]);
+              }
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) {
+                // even lanes hold digits 0,1 (plus the zero-point term), odd lanes digit 2
+                float f0, f1;
+                if ((tq & 1) == 0) {
+                  const float zs = (float)sv[uu][bl][nt];
+                  f0 = fmaf(-z0, zs, (float)(c[nt][0] + 256 * c[nt][1]));
+                  f1 = fmaf(-z1, zs, (float)(c[nt][2] + 256 * c[nt][3]));
+                } else {
+                  f0 = 65536.f * (float)c[nt][0];
+                  f1 = 65536.f * (float)c[nt][2];
+                }
+                y0[nt] = fmaf(s0 * sif[uu][bl][nt], f0, y0[nt]);
+                y1[nt] = fmaf(s1 * sif[uu][bl][nt], f1, y1[nt]);
+              }
             }
-            y0 = fmaf(s0, fmaf(-z0, sv[j], c[0] + c[1]), y0);
-            y1 = fmaf(s1, fmaf(-z1, sv[j], c[2] + c[3]), y1);
-          }
-          if (tq < mc) {
-            float* yr = ysum + ((int64_t)w * p.rows_cta + i * p.rb + g * 16 + grp) * mc + tq;
-            yr[0] += y0;
-            yr[8 * mc] += y1;
           }
         }
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&empty[s]);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const int m = nt * 2 + (tq >> 1);
+          if (m < mc) {
+            float* yc = ysum + ((warp * p.rows_cta + i * 16 + grp) * mc + m) * 2 + (tq & 1);
+            yc[0] += y0[nt];
+            yc[8 * mc * 2] += y1[nt];
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&empty[rs]);
+      if (++rs == p.nslots) {
+        rs = 0;
+        rph ^= 1u;
       }
     }
-    ptx::named_bar_sync(1, kConsumers * 32);  // the next segment restages the activations
   }
+  ptx::named_bar_sync(1, kConsumers * 32);
 
-  // ---- fixed-order sum over the k-slices, unscale, store (coalesced along rows)
+  // ---- fixed-order sum over warps and digit lanes, unscale, store (coalesced along rows)
   for (int idx = tid; idx < mc * p.rows_cta; idx += kConsumers * 32) {
     const int m = idx / p.rows_cta, r = idx - m * p.rows_cta;
-    const int i = r / p.rb, rl = r - i * p.rb;
-    const int b = blockIdx.x + i * grid;
-    const int64_t row = (int64_t)b * p.rb + rl;
+    const int ib = r >> 4, rl = r & 15;
+    const int b = blockIdx.x + ib * grid;
+    const int64_t row = (int64_t)b * 16 + rl;
     if (b < p.nblk && row < p.n_rows) {
-      float v = 0.f;
-      for (int ww = 0; ww < p.nwk; ++ww) v += ysum[((int64_t)ww * p.rows_cta + r) * mc + m];
-      p.y[(p.m0 + m) * p.ldy + row] = v * sig[4 + m];
+      float acc = 0.f;
+      for (int ww = 0; ww < kConsumers; ++ww) {
+        const float* yc = ysum + ((ww * p.rows_cta + r) * mc + m) * 2;
+        acc += yc[0] + yc[1];
+      }
+      p.y[(p.m0 + m) * p.ldy + row] = acc;
     }
   }
 }
 
-template <int KSTEPS, int BSTEPS>
+template <int BS, int NT>
 int launch(cudaStream_t st, const Args& a, int grid, size_t smem) {
-  auto kern = gemv_mma_kernel<KSTEPS, BSTEPS>;
+  auto kern = gemv_mma_kernel<BS, NT>;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -311,75 +402,92 @@ int launch(cudaStream_t st, const Args& a, int grid, size_t smem) {
 
 inline int align_up(int v, int a) { return (v + a - 1) / a * a; }
 
+// Shared-memory plan for mc rows of A; returns the bytes, or 0 if fewer than 2 stages fit.
+size_t plan_smem(const Weights& w, int mc, int grid, Args& a) {
+  const int kp = w.ntiles * w.kt;
+  const int head = 64 + 16 * kMaxM * 4;
+  const int dig = 4 * mc * kp;
+  const int sb = align_up(8 * mc * (kp / w.block_size), 16);  // block sums + block scales
+  a.rows_cta = ((w.nblk + grid - 1) / grid) * 16;
+  const int ysum = align_up(kConsumers * a.rows_cta * mc * 2 * 4, 16);
+  const int bars = 2 * kMaxSlots * 8 + 16;
+  a.off_dig = align_up(head, 16);
+  a.off_s = a.off_dig + align_up(dig, 16);
+  a.off_ysum = a.off_s + sb;
+  a.off_bar = a.off_ysum + ysum;
+  a.off_ring = align_up(a.off_bar + bars, 128);
+  if (a.off_ring >= kSmemMax) return 0;
+  int slots = (kSmemMax - a.off_ring) / w.stage_bytes;
+  slots = std::min(slots, 5);  // 3..5 stages of 17-35 KB stream best on B200
+  if (slots < 2) return 0;
+  a.nslots = slots;
+  return (size_t)a.off_ring + (size_t)slots * w.stage_bytes;
+}
+
+template <int BS>
+int launch_nt(cudaStream_t st, const Args& a, int grid, size_t smem) {
+  return a.mc <= 2 ? launch<BS, 1>(st, a, grid, smem) : launch<BS, 2>(st, a, grid, smem);
+}
+
 }  // namespace
 
 int run_gemv_mma(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M, float* d_y,
                  int64_t ldy) {
-  if (!w.strm || (w.ks != 64 && w.ks != 128) || w.block_size > w.ks) return MSQ_E_UNSUPPORTED;
+  if (!w.strm || (w.block_size != 32 && w.block_size != 64 && w.block_size != 128)) return MSQ_E_UNSUPPORTED;
+  const int unit = w.block_size > 64 ? w.block_size : 64;
+  if (w.kt / unit > 2 * kConsumers) return MSQ_E_UNSUPPORTED;
   const int sms = num_sms(w.device);
-  for (int64_t m0 = 0; m0 < M; m0 += kMaxM) {
-    const int mc = (int)std::min<int64_t>(kMaxM, M - m0);
+  int64_t m0 = 0;
+  while (m0 < M) {
     Args a{};
     a.strm = w.strm;
     a.a = d_a;
     a.a_dtype = a_dtype;
     a.m0 = m0;
-    a.mc = mc;
     a.y = d_y;
     a.ldy = ldy;
     a.n_rows = w.n_rows;
     a.K = w.K;
-    a.bs = w.block_size;
-    a.ks = w.ks;
-    a.nwk = w.nwk;
-    a.groups = w.groups;
     a.kt = w.kt;
     a.ntiles = w.ntiles;
-    a.rb = w.rb;
     a.nblk = w.nblk;
     a.stage_bytes = w.stage_bytes;
     a.off_sc = w.off_sc;
     a.off_zp = w.off_zp;
     a.zp_kind = w.zp_kind;
-    // grid: one CTA per SM, more when the per-CTA row sums would not fit
-    int grid = std::min(w.nblk, sms);
-    auto ysum_bytes = [&](int gr) { return w.nwk * ((w.nblk + gr - 1) / gr) * w.rb * mc * 4; };
-    while (ysum_bytes(grid) > 48 * 1024 && grid < w.nblk) grid = std::min(w.nblk, grid * 2);
-    a.rows_cta = ((w.nblk + grid - 1) / grid) * w.rb;
-    const int ysum = w.nwk * a.rows_cta * mc * 4;
-    // activations: as many whole k-tiles per segment as leave room for >= 4 stages
-    const int head = 64 + 16 * kMaxM * 4;  // prescale + reduction scratch
-    const int per_tile = 4 * mc * w.kt + 4 * mc * (w.kt / w.block_size);
-    const int bars = 2 * kMaxStages * 8 + 16;
-    const int fixed_no_act = align_up(head, 16) + align_up(ysum, 16) + bars + 128;
-    int seg_tiles = (kSmemMax - fixed_no_act - 4 * w.stage_bytes) / per_tile;
-    if (seg_tiles < 1) {
-      seg_tiles = (kSmemMax - fixed_no_act - 2 * w.stage_bytes) / per_tile;
-      if (seg_tiles < 1) return MSQ_E_UNSUPPORTED;
+    a.kp = w.ntiles * w.kt;
+    {
+      const uintptr_t ap = reinterpret_cast<uintptr_t>(d_a);
+      const int align = a_dtype == MSQ_DT_F32 ? 16 : 8;
+      a.a_vec = (w.K % 4 == 0) && (ap % align == 0);
     }
-    seg_tiles = std::min(seg_tiles, w.ntiles);
-    a.seg_tiles = seg_tiles;
-    const int segk = seg_tiles * w.kt;
-    a.off_ahl = align_up(head, 16);
-    a.off_s = a.off_ahl + align_up(2 * mc * segk * 2, 16);
-    a.off_ysum = a.off_s + align_up(mc * (segk / w.block_size) * 4, 16);
-    a.off_bar = a.off_ysum + align_up(ysum, 16);
-    a.off_ring = align_up(a.off_bar + bars, 128);
-    int nst = (kSmemMax - a.off_ring) / w.stage_bytes;
-    nst = std::min(nst, kMaxStages);
-    if (nst < 2) return MSQ_E_UNSUPPORTED;
-    a.nst = nst;
-    const size_t smem = (size_t)a.off_ring + (size_t)nst * w.stage_bytes;
+    // the widest pass whose digits, row sums and ring fit in shared memory
+    int mc = (int)std::min<int64_t>(kMaxM, M - m0);
+    int grid = std::min(w.nblk, sms);
+    size_t smem = 0;
+    for (;;) {
+      smem = plan_smem(w, mc, grid, a);
+      if (smem) break;
+      if (grid < w.nblk) {
+        grid = std::min(w.nblk, grid * 2);  // fewer rows per CTA -> smaller row-sum buffer
+      } else if (mc > 1) {
+        --mc;
+        grid = std::min(w.nblk, sms);
+      } else {
+        return MSQ_E_UNSUPPORTED;
+      }
+    }
+    a.mc = mc;
     int rc;
-    const int bsteps = w.block_size / 16;
-    if (w.ks == 128)
-      rc = bsteps == 2 ? launch<8, 2>(st, a, grid, smem) : bsteps == 4 ? launch<8, 4>(st, a, grid, smem)
-                                                        : launch<8, 8>(st, a, grid, smem);
-    else
-      rc = bsteps == 2 ? launch<4, 2>(st, a, grid, smem) : launch<4, 4>(st, a, grid, smem);
+    switch (w.block_size) {
+      case 32: rc = launch_nt<32>(st, a, grid, smem); break;
+      case 64: rc = launch_nt<64>(st, a, grid, smem); break;
+      default: rc = launch_nt<128>(st, a, grid, smem); break;
+    }
     if (rc != MSQ_OK) return rc;
+    m0 += mc;
   }
-  note_path(M <= 4 ? "gemv_mma" : "gemv_mma_multipass");
+  note_path(M <= 4 ? "gemv_imma" : "gemv_imma_multipass");
   return MSQ_OK;
 }
 

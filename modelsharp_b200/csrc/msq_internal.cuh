@@ -23,13 +23,13 @@ enum ZpKind : int { ZP_NONE = 0, ZP_PACKED = 1, ZP_F32 = 2 };
 //   sc16  half  [n_rows][sc_pitch]   the same scales rounded to fp16 (GEMM operand path)
 //   zp4   uint8 [n_rows][zp_pitch]   packed zero points as the reference packs them
 //   zpf   float [n_rows][sc_pitch]   float zero points
-//   strm  the decode-GEMV stream, one contiguous stage per (row block, k-tile), stages laid
-//         out [row block][k-tile]. A row block is G groups of 16 rows; a k-tile is nwk warp
-//         slices of ks k. Inside a stage: the nibbles as [group][slice][64-k chunk][lane][16 B]
-//         where lane (r = lane/4, t = lane%4) holds, per 16-k step, one word with the codes of
-//         rows r and r+8 at k = 2t, 2t+1, 2t+8, 2t+9 (the mma.m16n8k16 A-fragment order), then
-//         the fp32 scales [group][slice][block][16 rows], then the zero points
-//         [group][slice][block][16 rows] (packed nibbles or fp32).
+//   strm  the decode-GEMV stream: one contiguous stage per (16-row block, k-tile of kt),
+//         laid out [row block][k-tile]. Inside a stage: the codes as [64-k chunk][lane][16 B]
+//         where lane (r = lane/4, t = lane%4) holds two 32-bit words per 32-k step, the
+//         mma.m16n8k32 A-fragment order: byte j of the first word carries the code of
+//         (row r, k 4t+j) in its low nibble and of (row r+8, k 4t+j) in its high nibble, the
+//         second word the same at k + 16; then the fp32 scales [block][16 rows]; then the zero
+//         points [block][16 rows] (packed nibbles, 8 bytes per block, or fp32).
 // Other handles keep the reference layout (b_ref, sc_ref, zp_ref_*) for the generic
 // kernel.
 struct Weights {
@@ -47,13 +47,9 @@ struct Weights {
   int64_t zp_pitch = 0;
   float* zpf = nullptr;
   uint8_t* strm = nullptr;
-  int ks = 0;           // k per warp slice (multiple of max(block_size, 64))
-  int nwk = 0;          // warp slices per k-tile (<= 16)
-  int groups = 0;       // 16-row groups per row block
-  int kt = 0;           // k per tile = nwk * ks
+  int kt = 0;           // k per tile (multiple of max(block_size, 64))
   int ntiles = 0;       // k-tiles per row
-  int rb = 0;           // rows per row block = 16 * groups
-  int nblk = 0;         // row blocks
+  int nblk = 0;         // 16-row blocks
   int stage_bytes = 0;  // bytes per (row block, k-tile) stage
   int off_sc = 0;       // byte offset of the scales in a stage
   int off_zp = 0;       // byte offset of the zero points in a stage
@@ -69,6 +65,10 @@ struct Weights {
 int fail(int code, const char* fmt, ...);
 int cuda_fail(cudaError_t e, const char* what);
 void note_launch(int n = 1);
+// Stream-ordered scratch from a library-private memory pool that keeps its memory between
+// calls (the default pool would unmap it at every synchronisation).
+int scratch_alloc(void** p, size_t bytes, cudaStream_t st);
+void scratch_free(void* p, cudaStream_t st);
 void note_path(const char* name);
 int num_sms(int device);
 

@@ -57,13 +57,28 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete sleeps (up to the
+// hint, woken early when the phase completes) instead of spinning and taking issue slots
+// from the warps doing the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete; false (and *err set) on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0 && globaltimer() - t0 > kWaitBudgetNs) {
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+    if ((i & 7u) == 0 && globaltimer() - t0 > kWaitBudgetNs) {
       if (err) atomicCAS(err, 0, code);
       return false;
     }

@@ -5,6 +5,8 @@
 // scales [N*nb]; zero points packed [N][zp_row_bytes] or float [N*nb].
 #include "msq_internal.cuh"
 
+#include <algorithm>
+
 namespace msq {
 namespace {
 
@@ -82,63 +84,50 @@ __global__ void widen_kernel(const void* __restrict__ s, int sdt, int64_t off, i
 // One thread per 32-bit word of the decode stream (layout in msq_internal.cuh).
 __global__ void repack_stream_kernel(const uint8_t* __restrict__ b, const void* __restrict__ scales, int sdt,
                                      const void* __restrict__ zp, int zp_kind, int64_t row0, int n_rows, int K,
-                                     int bs, int nb, int blob, int zp_row_bytes, int ks, int nwk, int groups,
-                                     int kt, int ntiles, int stage_words, int off_sc_w, int off_zp_w,
-                                     uint32_t* __restrict__ out, int64_t total_words) {
+                                     int bs, int nb, int blob, int zp_row_bytes, int kt, int ntiles,
+                                     int stage_words, int off_sc_w, int off_zp_w, uint32_t* __restrict__ out,
+                                     int64_t total_words) {
   const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (idx >= total_words) return;
   const int64_t stage = idx / stage_words;
   const int wi = (int)(idx - stage * stage_words);
   const int tile = (int)(stage % ntiles);
   const int64_t blk = stage / ntiles;
-  const int nbs = ks / bs;
-  const int chunks = ks / 64;
+  const int nbt = kt / bs;
+  const int64_t r0 = blk * 16;
   uint32_t val = 0;
   if (wi < off_sc_w) {
-    // nibble words: [group][slice][chunk][lane][4 words]
-    int r = wi;
-    const int step = r & 3; r >>= 2;
-    const int lane = r & 31; r >>= 5;
-    const int chunk = r % chunks; r /= chunks;
-    const int slice = r % nwk;
-    const int g = r / nwk;
-    const int64_t row0r = blk * 16 * groups + g * 16 + (lane >> 2);
-    const int t = lane & 3;
-    const int64_t kb = (int64_t)tile * kt + (int64_t)slice * ks + chunk * 64 + step * 16 + 2 * t;
-    // slot j -> (row offset, k offset): 0:(0,0) 1:(0,8) 2:(8,0) 3:(8,8) 4:(0,1) 5:(0,9) 6:(8,1) 7:(8,9)
-    const int rofs[8] = {0, 0, 8, 8, 0, 0, 8, 8};
-    const int kofs[8] = {0, 8, 0, 8, 1, 9, 1, 9};
+    // code words: [chunk][lane][4 words] = [32-k step 0: k, k+16][step 1: k, k+16]
+    const int word = wi & 3;
+    const int lane = (wi >> 2) & 31;
+    const int chunk = wi >> 7;
+    const int64_t rlo = r0 + (lane >> 2), rhi = rlo + 8;
+    const int64_t kb = (int64_t)tile * kt + chunk * 64 + (word >> 1) * 32 + (word & 1) * 16 + 4 * (lane & 3);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int64_t rr = row0r + rofs[j];
-      const int64_t k = kb + kofs[j];
-      if (rr < n_rows && k < K) {
+    for (int j = 0; j < 4; ++j) {
+      const int64_t k = kb + j;
+      if (k < K) {
         const int64_t bk = k / bs, i = k - bk * bs;
-        const uint8_t byte = b[((row0 + rr) * nb + bk) * (int64_t)blob + (i >> 1)];
-        val |= (uint32_t)((byte >> ((i & 1) * 4)) & 0xF) << (4 * j);
+        const int sh = (i & 1) * 4;
+        if (rlo < n_rows) val |= (uint32_t)((b[((row0 + rlo) * nb + bk) * (int64_t)blob + (i >> 1)] >> sh) & 0xF) << (8 * j);
+        if (rhi < n_rows) val |= (uint32_t)((b[((row0 + rhi) * nb + bk) * (int64_t)blob + (i >> 1)] >> sh) & 0xF) << (8 * j + 4);
       }
     }
   } else if (wi < off_zp_w) {
-    // fp32 scales: [group][slice][block][16 rows]
-    int r = wi - off_sc_w;
-    const int row = r & 15; r >>= 4;
-    const int j = r % nbs; r /= nbs;
-    const int slice = r % nwk;
-    const int g = r / nwk;
-    const int64_t rr = blk * 16 * groups + g * 16 + row;
-    const int64_t bl = ((int64_t)tile * kt + (int64_t)slice * ks) / bs + j;
+    // fp32 scales: [block][16 rows]
+    const int r = wi - off_sc_w;
+    const int row = r & 15, j = r >> 4;
+    const int64_t rr = r0 + row;
+    const int64_t bl = (int64_t)tile * nbt + j;
     if (rr < n_rows && bl < nb) val = __float_as_uint(load_scale(scales, sdt, (row0 + rr) * nb + bl));
   } else if (zp_kind == ZP_PACKED) {
-    // packed: [group][slice][block][2 words of 8 nibbles, nibble = row]
-    int r = wi - off_zp_w;
-    const int half = r & 1; r >>= 1;
-    if (r < groups * nwk * nbs) {
-      const int j = r % nbs; r /= nbs;
-      const int slice = r % nwk;
-      const int g = r / nwk;
-      const int64_t bl = ((int64_t)tile * kt + (int64_t)slice * ks) / bs + j;
+    // packed: [block][2 words of 8 nibbles, nibble = row]
+    const int r = wi - off_zp_w;
+    const int half = r & 1, j = r >> 1;
+    if (j < nbt) {
+      const int64_t bl = (int64_t)tile * nbt + j;
       for (int q = 0; q < 8; ++q) {
-        const int64_t rr = blk * 16 * groups + g * 16 + half * 8 + q;
+        const int64_t rr = r0 + half * 8 + q;
         if (rr < n_rows && bl < nb) {
           const uint8_t zb = static_cast<const uint8_t*>(zp)[(row0 + rr) * zp_row_bytes + (bl >> 1)];
           val |= (uint32_t)((zb >> ((bl & 1) * 4)) & 0xF) << (4 * q);
@@ -146,14 +135,11 @@ __global__ void repack_stream_kernel(const uint8_t* __restrict__ b, const void* 
       }
     }
   } else if (zp_kind == ZP_F32) {
-    int r = wi - off_zp_w;
-    if (r < groups * nwk * nbs * 16) {
-      const int row = r & 15; r >>= 4;
-      const int j = r % nbs; r /= nbs;
-      const int slice = r % nwk;
-      const int g = r / nwk;
-      const int64_t rr = blk * 16 * groups + g * 16 + row;
-      const int64_t bl = ((int64_t)tile * kt + (int64_t)slice * ks) / bs + j;
+    const int r = wi - off_zp_w;
+    const int row = r & 15, j = r >> 4;
+    if (j < nbt) {
+      const int64_t rr = r0 + row;
+      const int64_t bl = (int64_t)tile * nbt + j;
       if (rr < n_rows && bl < nb) val = __float_as_uint(static_cast<const float*>(zp)[(row0 + rr) * nb + bl]);
     }
   }
@@ -193,28 +179,26 @@ int repack_fast4(cudaStream_t st, Weights& w, const uint8_t* d_b, int n_begin,
   return MSQ_OK;
 }
 
-// Decode-stream geometry: warp slices of ks k (a multiple of max(block_size, 64); 128 when
-// K is long enough to fill 16 slices of 128), nwk <= 16 slices per k-tile, and as many
-// 16-row groups per row block as leave the 16 consumer warps busy.
+// Decode-stream geometry: the largest k-tile kt <= kt_max that is a multiple of
+// max(block_size, 64) and divides K rounded up to that unit (so no padding is streamed),
+// falling back to kt_max with a padded last tile when only small divisors exist.
 void plan_stream(Weights& w) {
   const int K = w.K, bs = w.block_size;
   const int unit = bs > 64 ? bs : 64;
-  int ks = unit;
-  if (unit <= 128 && K >= 16 * 128) ks = 128;
-  int nwk = (K + ks - 1) / ks;
-  if (nwk > 16) nwk = 16;
-  w.ks = ks;
-  w.nwk = nwk;
-  w.groups = 16 / nwk;
-  w.kt = nwk * ks;
-  w.ntiles = (K + w.kt - 1) / w.kt;
-  w.rb = 16 * w.groups;
-  w.nblk = (w.n_rows + w.rb - 1) / w.rb;
-  const int nbs = ks / bs;
-  const int units = w.groups * nwk * nbs;
-  const int nib = w.rb * w.kt / 2;
-  const int sc = units * 16 * 4;
-  const int zpb = w.zp_kind == ZP_PACKED ? units * 8 : w.zp_kind == ZP_F32 ? units * 64 : 0;
+  const int kt_max = std::max(unit, (unit == 64 ? 2048 : 4096) / unit * unit);
+  const int units = (K + unit - 1) / unit;
+  int best = 1;
+  for (int d = 1; d * unit <= kt_max; ++d)
+    if (units % d == 0) best = d;
+  int kt = best * unit;
+  if (kt * 4 < std::min(kt_max, units * unit)) kt = std::min(kt_max, units * unit);
+  w.kt = kt;
+  w.ntiles = (K + kt - 1) / kt;
+  w.nblk = (w.n_rows + 15) / 16;
+  const int nbt = kt / bs;
+  const int nib = 16 * kt / 2;
+  const int sc = nbt * 16 * 4;
+  const int zpb = w.zp_kind == ZP_PACKED ? nbt * 8 : w.zp_kind == ZP_F32 ? nbt * 64 : 0;
   w.off_sc = nib;
   w.off_zp = nib + sc;
   w.stage_bytes = (nib + sc + zpb + 15) / 16 * 16;
@@ -227,7 +211,7 @@ int repack_stream(cudaStream_t st, Weights& w, const uint8_t* d_b, int n_begin, 
   const int64_t total = (int64_t)w.nblk * w.ntiles * stage_words;
   repack_stream_kernel<<<grid_for(total, T), T, 0, st>>>(
       d_b, d_scales, scales_dtype, d_zp, w.zp_kind, n_begin, w.n_rows, w.K, w.block_size, w.nb, w.blob,
-      w.zp_row_bytes, w.ks, w.nwk, w.groups, w.kt, w.ntiles, stage_words, w.off_sc / 4, w.off_zp / 4,
+      w.zp_row_bytes, w.kt, w.ntiles, stage_words, w.off_sc / 4, w.off_zp / 4,
       reinterpret_cast<uint32_t*>(w.strm), total);
   note_launch();
   MSQ_CUDA_TRY(cudaGetLastError(), "stream repack launch");
