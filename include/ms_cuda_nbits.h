@@ -129,6 +129,23 @@ int msq_matmul_ex(void* cu_ctx, void* stream, msq_weights_t w,
 int msq_matmul_host(void* cu_ctx, void* stream, msq_weights_t w,
                     const void* a, int a_dtype, int64_t M, float* y);
 
+/* ---- no-allocation GEMM -------------------------------------------------------------
+ * No counterpart in the reference. For callers that cannot allocate device memory while a
+ * node runs (an engine that owns all device memory through its own arena, a plugin called
+ * inside someone else's stream capture, a process under a hard memory cap): the tcgen05
+ * GEMM path of msq_matmul_ex(..., MSQ_PATH_GEMM) with the same arguments and results, but
+ * float32 / bfloat16 (or unaligned float16) A is staged as fp16 in a fixed device array of
+ * MSQ_NOALLOC_SCRATCH_BYTES that the library holds on every GPU that loads it, until exit,
+ * instead of in memory taken from a pool. Calls no cudaMalloc / cudaFree or other allocator.
+ * Limit: M x round_up(K, 8) x 2 <= MSQ_NOALLOC_SCRATCH_BYTES (e.g. M <= 2048 at K = 4096),
+ * else MSQ_E_INVALID; 16-byte-aligned float16 A with K % 8 == 0 needs no staging and has no
+ * limit. The first call in a CUDA context looks up the array's address (set-up); make it
+ * before any stream capture. All calls share the array: calls that overlap on the GPU race. */
+#define MSQ_NOALLOC_SCRATCH_BYTES (16u << 20)
+int msq_matmul_noalloc(void* cu_ctx, void* stream, msq_weights_t w,
+                       const void* d_a, int a_dtype, int64_t M,
+                       float* d_y, int64_t ldy);
+
 /* Synchronizes `stream` and reports whether any kernel of this library on the current
  * device gave up a bounded wait (a pipeline stage that never arrived) since the last call:
  * MSQ_OK, or MSQ_E_TIMEOUT with the kernel and stage in msq_last_error(). Clears the flags.

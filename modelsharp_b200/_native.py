@@ -25,6 +25,7 @@ MSQ_E_TIMEOUT = -6
 DT_ABSENT, DT_F32, DT_F64, DT_F16, DT_I32, DT_I64, DT_I8, DT_U8, DT_BOOL, DT_BF16 = -1, 1, 2, 3, 4, 5, 6, 7, 8, 16
 
 PATH_AUTO, PATH_GENERIC, PATH_GEMV, PATH_GEMM = 0, 1, 2, 3
+NOALLOC_SCRATCH_BYTES = 16 << 20  # MSQ_NOALLOC_SCRATCH_BYTES
 PACK_DEFAULT, PACK_GENERIC_ONLY = 0, 1
 
 LIB_NAME = "libms_cuda_nbits.so"
@@ -51,6 +52,7 @@ SIGNATURES: dict[str, tuple] = {
     "msq_matmul": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp, _i64]),
     "msq_matmul_ex": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp, _i64, _i32]),
     "msq_matmul_host": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp]),
+    "msq_matmul_noalloc": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp, _i64]),
     "msq_device_status": (_i32, [_vp, _vp]),
     "msq_qgemm_nbits": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32]),
 }

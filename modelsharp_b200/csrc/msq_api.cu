@@ -478,6 +478,30 @@ int msq_matmul_host(void* cu_ctx, void* stream, msq_weights_t h, const void* a, 
   return rc;
 }
 
+int msq_matmul_noalloc(void* cu_ctx, void* stream, msq_weights_t h, const void* d_a, int a_dtype, int64_t M,
+                       float* d_y, int64_t ldy) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  Weights* w = reinterpret_cast<Weights*>(h);
+  if (!w) return fail(MSQ_E_INVALID, "msq_matmul_noalloc: NULL weights handle");
+  if (!is_float_act(a_dtype))
+    return fail(MSQ_E_INVALID, "MatMulNBits A must be Float32 or Float16; got %s.", dtype_name(a_dtype));
+  if (M < 0) return fail(MSQ_E_INVALID, "msq_matmul_noalloc: negative M (%lld)", (long long)M);
+  if (ldy < w->n_rows)
+    return fail(MSQ_E_INVALID, "msq_matmul_noalloc: ldy %lld < rows %d", (long long)ldy, w->n_rows);
+  if (M == 0) {
+    note_path("empty");
+    return MSQ_OK;
+  }
+  if (!d_a || !d_y) return fail(MSQ_E_INVALID, "msq_matmul_noalloc: NULL device pointer");
+  int dev;
+  int rc = current_device(&dev);
+  if (rc != MSQ_OK) return rc;
+  if (dev != w->device)
+    return fail(MSQ_E_INVALID, "weights handle lives on device %d but the current device is %d", w->device, dev);
+  return run_gemm_noalloc(static_cast<cudaStream_t>(stream), *w, d_a, a_dtype, M, d_y, ldy);
+}
+
 int msq_device_status(void* cu_ctx, void* stream) {
   CtxGuard g(cu_ctx);
   if (g.rc != MSQ_OK) return g.rc;

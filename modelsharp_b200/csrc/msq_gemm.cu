@@ -371,6 +371,59 @@ int launch_zp(cudaStream_t st, int zp_kind, const CUtensorMap& tmA, const CUtens
 
 }  // namespace
 
+namespace {
+
+// Builds the activation map over fp16 rows of stride lda and launches the tile kernel.
+int launch_gemm(cudaStream_t st, const Weights& w, const CUtensorMap& tmP128, const CUtensorMap& tmP256,
+                const void* a16, int64_t lda, int64_t M, float* d_y, int64_t ldy) {
+  CUtensorMap tmA;
+  int rc = make_map_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, const_cast<void*>(a16), (uint64_t)w.K, (uint64_t)M,
+                       (uint64_t)lda * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != MSQ_OK) return rc;
+  GemmArgs g{};
+  g.y = d_y;
+  g.ldy = ldy;
+  g.M = (int)M;
+  g.n_rows = w.n_rows;
+  g.K = w.K;
+  g.ksteps = (w.K + BK - 1) / BK;
+  g.sc16 = w.sc16;
+  g.sc_pitch = w.sc_pitch;
+  g.zp4 = w.zp4;
+  g.zp_pitch = w.zp_pitch;
+  g.zpf = w.zpf;
+  int sh = 0;
+  while ((1 << sh) < w.block_size) ++sh;
+  g.bs_shift = sh;
+  g.vec_store = (ldy % 4 == 0) && ((reinterpret_cast<uintptr_t>(d_y) & 15) == 0);
+  const int64_t mt = (M + BM - 1) / BM;
+  const int64_t tiles256 = (w.n_rows + 255) / 256 * mt;
+  const bool big = tiles256 >= 2 * num_sms(w.device);
+  if (big) {
+    rc = launch_zp<256>(st, w.zp_kind, tmA, tmP256, g, dim3((w.n_rows + 255) / 256, (unsigned)mt));
+  } else {
+    rc = launch_zp<128>(st, w.zp_kind, tmA, tmP128, g, dim3((w.n_rows + 127) / 128, (unsigned)mt));
+  }
+  if (rc == MSQ_OK) note_path(big ? "gemm_tc_n256" : "gemm_tc_n128");
+  return rc;
+}
+
+int make_weight_maps(const Weights& w, CUtensorMap* tmP128, CUtensorMap* tmP256) {
+  int rc = make_map_2d(tmP128, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.nib, (uint64_t)w.nib_pitch, (uint64_t)w.n_rows,
+                       (uint64_t)w.nib_pitch, BK / 2, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc == MSQ_OK)
+    rc = make_map_2d(tmP256, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.nib, (uint64_t)w.nib_pitch, (uint64_t)w.n_rows,
+                     (uint64_t)w.nib_pitch, BK / 2, 256, CU_TENSOR_MAP_SWIZZLE_NONE);
+  return rc;
+}
+
+// fp16 activations with 16-byte rows feed TMA directly; anything else is staged as fp16.
+bool needs_staging(const Weights& w, const void* d_a, int a_dtype) {
+  return a_dtype != MSQ_DT_F16 || (w.K % 8) != 0 || (reinterpret_cast<uintptr_t>(d_a) & 15) != 0;
+}
+
+}  // namespace
+
 int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t M, float* d_y, int64_t ldy) {
   if (!w.fast4) return fail(MSQ_E_UNSUPPORTED, "GEMM path needs bits=4 and a power-of-two block_size >= 32");
   if (M <= 0) return MSQ_OK;
@@ -378,22 +431,17 @@ int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t 
   GemmState* gs = static_cast<GemmState*>(w.gemm_state);
   if (!gs) {
     gs = new GemmState();
-    int rc = make_map_2d(&gs->tmP128, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.nib, (uint64_t)w.nib_pitch,
-                         (uint64_t)w.n_rows, (uint64_t)w.nib_pitch, BK / 2, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (rc == MSQ_OK)
-      rc = make_map_2d(&gs->tmP256, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.nib, (uint64_t)w.nib_pitch,
-                       (uint64_t)w.n_rows, (uint64_t)w.nib_pitch, BK / 2, 256, CU_TENSOR_MAP_SWIZZLE_NONE);
+    int rc = make_weight_maps(w, &gs->tmP128, &gs->tmP256);
     if (rc != MSQ_OK) {
       delete gs;
       return rc;
     }
     w.gemm_state = gs;
   }
-  // fp16 activations with 16-byte rows feed TMA directly; anything else goes through scratch
   const void* a16 = d_a;
   int64_t lda = w.K;
   void* scratch = nullptr;
-  if (a_dtype != MSQ_DT_F16 || (w.K % 8) != 0 || (reinterpret_cast<uintptr_t>(d_a) & 15) != 0) {
+  if (needs_staging(w, d_a, a_dtype)) {
     lda = (w.K + 7) / 8 * 8;
     const int arc = scratch_alloc(&scratch, sizeof(__half) * (size_t)M * lda, st);
     if (arc != MSQ_OK) return arc;
@@ -401,38 +449,37 @@ int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t 
     note_launch();
     a16 = scratch;
   }
-  CUtensorMap tmA;
-  int rc = make_map_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, const_cast<void*>(a16), (uint64_t)w.K, (uint64_t)M,
-                       (uint64_t)lda * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc == MSQ_OK) {
-    GemmArgs g{};
-    g.y = d_y;
-    g.ldy = ldy;
-    g.M = (int)M;
-    g.n_rows = w.n_rows;
-    g.K = w.K;
-    g.ksteps = (w.K + BK - 1) / BK;
-    g.sc16 = w.sc16;
-    g.sc_pitch = w.sc_pitch;
-    g.zp4 = w.zp4;
-    g.zp_pitch = w.zp_pitch;
-    g.zpf = w.zpf;
-    int sh = 0;
-    while ((1 << sh) < w.block_size) ++sh;
-    g.bs_shift = sh;
-    g.vec_store = (ldy % 4 == 0) && ((reinterpret_cast<uintptr_t>(d_y) & 15) == 0);
-    const int64_t mt = (M + BM - 1) / BM;
-    const int64_t tiles256 = (w.n_rows + 255) / 256 * mt;
-    const bool big = tiles256 >= 2 * num_sms(w.device);
-    if (big) {
-      rc = launch_zp<256>(st, w.zp_kind, tmA, gs->tmP256, g, dim3((w.n_rows + 255) / 256, (unsigned)mt));
-    } else {
-      rc = launch_zp<128>(st, w.zp_kind, tmA, gs->tmP128, g, dim3((w.n_rows + 127) / 128, (unsigned)mt));
-    }
-    if (rc == MSQ_OK) note_path(big ? "gemm_tc_n256" : "gemm_tc_n128");
-  }
+  const int rc = launch_gemm(st, w, gs->tmP128, gs->tmP256, a16, lda, M, d_y, ldy);
   scratch_free(scratch, st);
   return rc;
+}
+
+size_t gemm_staging_bytes(const Weights& w, const void* d_a, int a_dtype, int64_t M) {
+  if (M <= 0 || !needs_staging(w, d_a, a_dtype)) return 0;
+  return sizeof(__half) * (size_t)M * (size_t)((w.K + 7) / 8 * 8);
+}
+
+int run_gemm_staged(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M, float* d_y,
+                    int64_t ldy, void* staging, size_t staging_bytes) {
+  if (!w.fast4) return fail(MSQ_E_UNSUPPORTED, "GEMM path needs bits=4 and a power-of-two block_size >= 32");
+  if (M <= 0) return MSQ_OK;
+  if (M > 0x7fffffff) return fail(MSQ_E_INVALID, "GEMM: M too large");
+  CUtensorMap tmP128, tmP256;
+  int rc = make_weight_maps(w, &tmP128, &tmP256);
+  if (rc != MSQ_OK) return rc;
+  const void* a16 = d_a;
+  int64_t lda = w.K;
+  const size_t need = gemm_staging_bytes(w, d_a, a_dtype, M);
+  if (need) {
+    if (need > staging_bytes || !staging)
+      return fail(MSQ_E_INVALID, "GEMM staging needs %zu bytes; %zu available", need, staging_bytes);
+    lda = (w.K + 7) / 8 * 8;
+    to_half_kernel<<<num_sms(w.device) * 4, 256, 0, st>>>(d_a, a_dtype, M, w.K, static_cast<__half*>(staging), lda);
+    note_launch();
+    MSQ_CUDA_TRY(cudaGetLastError(), "staging launch");
+    a16 = staging;
+  }
+  return launch_gemm(st, w, tmP128, tmP256, a16, lda, M, d_y, ldy);
 }
 
 void release_gemm_state(Weights& w) {

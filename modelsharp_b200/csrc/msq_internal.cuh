@@ -99,6 +99,15 @@ int run_gemv_mma(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype
 int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t M,
              float* d_y, int64_t ldy);
 void release_gemm_state(Weights& w);
+// Bytes of fp16 activation staging the GEMM needs for this call (0 when A feeds TMA as is).
+size_t gemm_staging_bytes(const Weights& w, const void* d_a, int a_dtype, int64_t M);
+// The GEMM with its activation staging in caller-provided device memory: no allocation,
+// no state kept on the handle.
+int run_gemm_staged(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M,
+                    float* d_y, int64_t ldy, void* staging, size_t staging_bytes);
+// The GEMM with its staging in this library's fixed device array (msq_noalloc.cu).
+int run_gemm_noalloc(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M,
+                     float* d_y, int64_t ldy);
 
 // Loads element idx of an activation tensor of dtype dt (f32 / f16 / bf16) as fp32.
 __device__ __forceinline__ float load_act(const void* a, int dt, int64_t idx) {

@@ -101,3 +101,8 @@ def test_pack_rejects_before_touching_a_device(native_lib):
                              2, 4, 4, 4, 1, 1, 0, C.byref(h))
     assert rc == N.MSQ_E_INVALID and "row range" in N.last_error()
     assert not h.value
+
+
+def test_noalloc_scratch_size_constant():
+    m = re.search(r"#define\s+MSQ_NOALLOC_SCRATCH_BYTES\s+\((\d+)u\s*<<\s*(\d+)\)", N.HEADER.read_text())
+    assert m and int(m.group(1)) << int(m.group(2)) == N.NOALLOC_SCRATCH_BYTES
