@@ -256,33 +256,45 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         ms = float(t.item())
     value = world * nbytes * args.steps / (ms * 1e-3) / 1e9
 
-    # ---- roofline: per-launch CUDA events on the launching stream, same kernels
-    per_shape = []
-    tot_bytes, tot_ms = 0, 0.0
+    # ---- roofline. Every launch of the timed region is the decode GEMV, so its average
+    # launch duration there is ms_per_step / launches_per_step and the algorithmic bytes per
+    # launch are bytes_per_step / launches_per_step. Per-shape figures come from one CUDA
+    # graph per shape of 2 * REPLICAS back-to-back launches (the same launch chaining as the
+    # step), timed with CUDA events on the launching stream.
     from modelsharp_b200 import synth
-    with torch.cuda.stream(stream):
-        for si, c in enumerate(cases):
-            b = synth.algorithmic_bytes(c["N"], c["K"], 4, BS, "packed")
-            evs = []
-            for it in range(4 * REPLICAS):
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    per_shape = []
+    for si, c in enumerate(cases):
+        b = synth.algorithmic_bytes(c["N"], c["K"], 4, BS, "packed")
+        g = torch.cuda.CUDAGraph()
+        n_in = 2 * REPLICAS
+        with torch.cuda.graph(g, stream=stream):
+            for it in range(n_in):
                 w = reps[it % REPLICAS][si]
-                e0.record(stream)
-                lib.msq_matmul(None, sptr, w.handle, a_dev[si].data_ptr(), N.DT_F32, 1, y_dev[si].data_ptr(), c["N"])
-                e1.record(stream)
-                evs.append((e0, e1))
-            stream.synchronize()
-            d = [e0.elapsed_time(e1) for e0, e1 in evs[REPLICAS:]]
-            avg = sum(d) / len(d)
-            per_shape.append({"K": c["K"], "N": c["N"], "bytes": b, "us": avg * 1e3, "GB/s": b / (avg * 1e-3) / 1e9})
-            tot_bytes += b
-            tot_ms += avg
+                rc = lib.msq_matmul(None, sptr, w.handle, a_dev[si].data_ptr(), N.DT_F32, 1, y_dev[si].data_ptr(),
+                                    c["N"])
+                if rc:
+                    N.check(rc)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                g.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            n_rep = 50
+            for _ in range(n_rep):
+                g.replay()
+            e1.record(stream)
+        stream.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (n_rep * n_in)
+        per_shape.append({"K": c["K"], "N": c["N"], "bytes": b, "us": us, "GB/s": b / (us * 1e-6) / 1e9})
+        del g
     peak, peak_kind = peaks()
-    achieved = tot_bytes / (tot_ms * 1e-3) / 1e9
+    launch_us = ms * 1e3 / args.steps / launches_per_step
+    bytes_per_launch = nbytes / launches_per_step
+    achieved = bytes_per_launch / (launch_us * 1e-6) / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": (NCU_DRAM_PER_ALG_BYTE * tot_bytes / len(cases)) if NCU_DRAM_PER_ALG_BYTE else None,
+                "traffic": (NCU_DRAM_PER_ALG_BYTE * bytes_per_launch) if NCU_DRAM_PER_ALG_BYTE else None,
                 "peak_source": f"{peak_kind} HBM copy bandwidth", "kernel": path,
-                "bytes_per_launch": tot_bytes / len(cases), "per_shape": per_shape}
+                "bytes_per_launch": bytes_per_launch, "launch_us": launch_us, "per_shape": per_shape}
 
     # ---- e2e: host buffers through the C ABI, copies inside the timed region
     a_host = [torch.from_numpy(c["a"]).pin_memory() for c in cases]
@@ -361,7 +373,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--shapes", default="",
+                    help="restrict the step to these KxN shapes (comma separated), for profiling one shape")
     args = ap.parse_args()
+    if args.shapes:
+        global WORKLOAD
+        SWEEP[:] = [tuple(int(v) for v in sh.lower().split("x")) for sh in args.shapes.split(",")]
+        WORKLOAD = ("subset of the 7B decode GEMV sweep at M=1: (K,N) = " +
+                    ", ".join(f"({k},{n})" for k, n in SWEEP) + "; bits=4, block_size=128, packed zero points")
     if args.warmup < 3:
         args.warmup = 3
     rank = int(os.environ.get("RANK", 0))

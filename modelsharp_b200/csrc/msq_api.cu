@@ -151,6 +151,7 @@ int dev_alloc(T** p, size_t n, int64_t* total) {
 void free_weights(Weights* w) {
   if (!w) return;
   release_gemm_state(*w);
+  if (w->packed_ev) cudaEventDestroy(w->packed_ev);
   void* ptrs[] = {w->nib, w->sc, w->sc16, w->zp4, w->zpf, w->strm, w->b_ref, w->sc_ref, w->zp_ref_u8, w->zp_ref_f32};
   for (void* p : ptrs)
     if (p) cudaFree(p);
@@ -214,8 +215,30 @@ int pack_impl(cudaStream_t st, const uint8_t* d_b, int64_t b_len, const void* d_
     free_weights(w);
     return rc;
   }
+  if (cudaEventCreateWithFlags(&w->packed_ev, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventRecord(w->packed_ev, st) != cudaSuccess) {
+    cudaGetLastError();  // without the event the weights count as unsettled (no early reads)
+    if (w->packed_ev) cudaEventDestroy(w->packed_ev);
+    w->packed_ev = nullptr;
+  }
   *out = reinterpret_cast<msq_weights_t>(w);
   return MSQ_OK;
+}
+
+// Marks the weights settled once the host sees their repack complete. Skipped while the
+// stream is being captured (event queries are not allowed then); the weights stay
+// unsettled until a later uncaptured call.
+void refresh_settled(Weights& w, cudaStream_t st) {
+  if (w.settled.load(std::memory_order_relaxed) || !w.packed_ev) return;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess) {
+    cudaGetLastError();
+    return;
+  }
+  if (cs != cudaStreamCaptureStatusNone) return;
+  const cudaError_t e = cudaEventQuery(w.packed_ev);
+  if (e == cudaSuccess) w.settled.store(true, std::memory_order_relaxed);
+  else if (cudaPeekAtLastError() == cudaErrorNotReady) cudaGetLastError();  // clear only our own status
 }
 
 int matmul_impl(cudaStream_t st, Weights* w, const void* d_a, int a_dtype, int64_t M, float* d_y, int64_t ldy,
@@ -235,6 +258,7 @@ int matmul_impl(cudaStream_t st, Weights* w, const void* d_a, int a_dtype, int64
   if (rc != MSQ_OK) return rc;
   if (dev != w->device)
     return fail(MSQ_E_INVALID, "weights handle lives on device %d but the current device is %d", w->device, dev);
+  refresh_settled(*w, st);
   if (path == MSQ_PATH_AUTO) {
     if (!w->fast4) path = MSQ_PATH_GENERIC;
     else if (M >= 17 && w->K >= 64) path = MSQ_PATH_GEMM;

@@ -428,6 +428,8 @@ int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t 
   if (!w.fast4) return fail(MSQ_E_UNSUPPORTED, "GEMM path needs bits=4 and a power-of-two block_size >= 32");
   if (M <= 0) return MSQ_OK;
   if (M > 0x7fffffff) return fail(MSQ_E_INVALID, "GEMM: M too large");
+  static std::mutex state_mu;  // first calls on one handle from several threads
+  std::lock_guard<std::mutex> lk(state_mu);
   GemmState* gs = static_cast<GemmState*>(w.gemm_state);
   if (!gs) {
     gs = new GemmState();

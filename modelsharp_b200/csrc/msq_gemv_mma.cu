@@ -48,6 +48,7 @@ struct Args {
   int nslots, rows_cta;
   int kp;     // ntiles * kt: K padded to whole tiles
   int a_vec;  // rows of A may be read 4 elements at a time
+  int prefetch;  // weights settled: stream them before the programmatic-dependency wait
   int off_dig, off_s, off_ysum, off_bar, off_ring;  // shared-memory offsets (bytes)
 };
 
@@ -67,6 +68,15 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
     }
   }
 }
+
+// Programmatic dependent launch. launch_dependents lets the next kernel of the stream that
+// was launched with programmatic serialization get scheduled as SMs free up; wait blocks
+// until every prerequisite grid has completed and its memory is visible (a no-op when the
+// launch had no programmatic dependency).
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ void imma(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                      uint32_t b1) {
@@ -155,12 +165,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
     }
     *abort_flag = 0;
     ptx::fence_mbar_init();
+    griddep_launch_dependents();
   }
   __syncthreads();
 
   if (warp == kConsumers) {
-    // ---------------- producer: stages in (tile, row block) order
+    // ---------------- producer: stages in (tile, row block) order. Settled weights are
+    // never written by an earlier kernel, so their stream starts before the dependency wait
+    // and overlaps the previous kernel's tail.
     if (lane == 0) {
+      if (!p.prefetch) griddep_wait();
       int issued = 0, s = 0;
       uint32_t wrap = 0;
       bool ok = true;
@@ -198,6 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
   const int tid = threadIdx.x;
   const int mc = p.mc;
   for (int i = tid; i < kConsumers * p.rows_cta * mc * 2; i += kConsumers * 32) ysum[i] = 0.f;
+  griddep_wait();  // A may come from the previous kernel, and Y may still be read by it
 
   // ---- activations: one pass. Loads in flight at once (float4, U deep); per quantisation
   // block (GL consecutive lanes) a shuffle max picks 2^sigma_b, the digits are written and a
@@ -394,9 +409,18 @@ int launch(cudaStream_t st, const Args& a, int grid, size_t smem) {
                  "mma gemv smem attribute");
     configured[dev] = true;
   }
-  kern<<<grid, kThreads, smem, st>>>(a);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  MSQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a), "mma gemv launch");
   note_launch();
-  MSQ_CUDA_TRY(cudaGetLastError(), "mma gemv launch");
   return MSQ_OK;
 }
 
@@ -456,6 +480,7 @@ int run_gemv_mma(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype
     a.off_zp = w.off_zp;
     a.zp_kind = w.zp_kind;
     a.kp = w.ntiles * w.kt;
+    a.prefetch = w.settled.load(std::memory_order_relaxed) ? 1 : 0;
     {
       const uintptr_t ap = reinterpret_cast<uintptr_t>(d_a);
       const int align = a_dtype == MSQ_DT_F32 ? 16 : 8;

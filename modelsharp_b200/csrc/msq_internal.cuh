@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
+#include <atomic>
 #include <cstdint>
 
 #include "../../include/ms_cuda_nbits.h"
@@ -59,6 +60,9 @@ struct Weights {
   float* zp_ref_f32 = nullptr;
   int64_t device_bytes = 0;
   void* gemm_state = nullptr;
+  cudaEvent_t packed_ev = nullptr;   // recorded on the packing stream after the repack kernels
+  std::atomic<bool> settled{false};  // the host has seen packed_ev complete: kernels may read
+                                     // the weights before their programmatic-dependency wait
 };
 
 // ---- error and diagnostics plumbing (msq_api.cu) ----
