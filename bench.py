@@ -46,8 +46,8 @@ WORKLOAD = ("7B decode GEMV sweep (BASELINE configs[1]) at M=1: (K,N) = (4096,40
             "scales")
 FALLBACK_HBM_GBS = 6650.0
 # dram bytes per algorithmic byte of the decode GEMV, from the ncu capture summarised in
-# profiles/gemv_q4_decode_7b.md (None until a capture exists).
-NCU_DRAM_PER_ALG_BYTE = None
+# profiles/gemv_q4_decode_7b_sweep.md (K=4096, N=14336, one launch).
+NCU_DRAM_PER_ALG_BYTE = 31505152 / 31424512
 
 
 def log(*a):
