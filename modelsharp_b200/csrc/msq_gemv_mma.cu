@@ -33,6 +33,8 @@ constexpr int kThreads = (kConsumers + 1) * 32;
 constexpr int kMaxSlots = 8;
 constexpr int kSmemMax = 227 * 1024;
 constexpr int kMaxM = 4;  // B columns: 4 per A row (3 digits + 1 zero) -> two n8 tiles for 4 rows
+constexpr int kYSlots = kConsumers + 1;  // per-warp partial sums of one output, padded against
+constexpr int kYPitch = 2 * kYSlots;     // bank conflicts in the per-stage update
 
 __device__ int g_mma_err;
 
@@ -47,6 +49,7 @@ struct Args {
   int n_rows, K, kt, ntiles, nblk, stage_bytes, off_sc, off_zp, zp_kind;
   int nslots, rows_cta;
   int kp;     // ntiles * kt: K padded to whole tiles
+  int kpp;    // row pitch of the digit array: kp + 16 bytes (column c starts 4c banks later)
   int a_vec;  // rows of A may be read 4 elements at a time
   int prefetch;  // weights settled: stream them before the programmatic-dependency wait
   int off_dig, off_s, off_ysum, off_bar, off_ring;  // shared-memory offsets (bytes)
@@ -112,9 +115,10 @@ __device__ __forceinline__ float4 load4(const Args& p, int m, int k) {
 // rint(x * 2^sigma) as a 24-bit integer.
 __device__ __forceinline__ int fixed24(float x, float sc) { return __float2int_rn(x * sc); }
 
-// Writes the three balanced int8 digits of 4 consecutive k of row m (columns 4m..4m+2; the
-// fourth column of each row stays zero) and returns their exact integer sum.
-__device__ __forceinline__ int store_digits(int8_t* dig, int kp, int m, int k, float4 v, float sc) {
+// Writes the three balanced int8 digits of 4 consecutive k of row m (columns 4m..4m+2 of the
+// digit array, row pitch kpp; the fourth column of each row is never read) and returns their
+// exact integer sum.
+__device__ __forceinline__ int store_digits(int8_t* dig, int kpp, int m, int k, float4 v, float sc) {
   const int a[4] = {fixed24(v.x, sc), fixed24(v.y, sc), fixed24(v.z, sc), fixed24(v.w, sc)};
   uint32_t w0 = 0, w1 = 0, w2 = 0;
 #pragma unroll
@@ -127,12 +131,20 @@ __device__ __forceinline__ int store_digits(int8_t* dig, int kp, int m, int k, f
     w1 |= (uint32_t)(d1 & 255) << (8 * j);
     w2 |= (uint32_t)(d2 & 255) << (8 * j);
   }
-  *reinterpret_cast<uint32_t*>(dig + (4 * m + 0) * kp + k) = w0;
-  *reinterpret_cast<uint32_t*>(dig + (4 * m + 1) * kp + k) = w1;
-  *reinterpret_cast<uint32_t*>(dig + (4 * m + 2) * kp + k) = w2;
-  *reinterpret_cast<uint32_t*>(dig + (4 * m + 3) * kp + k) = 0u;
+  *reinterpret_cast<uint32_t*>(dig + (4 * m + 0) * kpp + k) = w0;
+  *reinterpret_cast<uint32_t*>(dig + (4 * m + 1) * kpp + k) = w1;
+  *reinterpret_cast<uint32_t*>(dig + (4 * m + 2) * kpp + k) = w2;
   return (a[0] + a[1]) + (a[2] + a[3]);
 }
+
+// Exponent e of frexp(x) for finite x > 0 (x = f * 2^e, f in [0.5, 1)), -126 for subnormals,
+// 0 for zero, infinity and NaN; and 2^s for |s| <= 126 from the exponent bits.
+__device__ __forceinline__ int frexp_exponent(float x) {
+  const int be = (__float_as_int(x) >> 23) & 0xFF;
+  if (!(x > 0.f) || be == 0xFF) return 0;
+  return be == 0 ? -126 : be - 126;
+}
+__device__ __forceinline__ float exp2i(int s) { return __int_as_float((s + 127) << 23); }
 
 // BS = quantisation block size (32 / 64 / 128); NT = n8 tiles of B (1: M <= 2, 2: M <= 4).
 // A "unit" is max(BS, 64) k: one or two 64-k chunks (a uint4 of code words per lane each).
@@ -145,10 +157,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
   constexpr int BSTEPS = BS / 32;   // k32 steps per block
   constexpr int UPW = 2;            // units per warp per tile (kt <= 32 units)
   extern __shared__ __align__(16) uint8_t smem[];
-  int8_t* dig = reinterpret_cast<int8_t*>(smem + p.off_dig);  // [4*mc][kp] digits
+  int8_t* dig = reinterpret_cast<int8_t*>(smem + p.off_dig);  // [4*mc][kpp] digits
   int* sblk = reinterpret_cast<int*>(smem + p.off_s);         // [mc][kp/BS] exact block sums of a_int
   float* sinv = reinterpret_cast<float*>(sblk + p.mc * (p.kp / BS));  // [mc][kp/BS] 2^-sigma_b
-  float* ysum = reinterpret_cast<float*>(smem + p.off_ysum);  // [16 warps][rows_cta][mc][2]
+  float* ysum = reinterpret_cast<float*>(smem + p.off_ysum);  // [rows_cta][mc][17][2]: per warp, parity
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bar);
   uint64_t* empty = full + kMaxSlots;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kMaxSlots);
@@ -211,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
   // ---------------- consumers (512 threads, named barrier 1)
   const int tid = threadIdx.x;
   const int mc = p.mc;
-  for (int i = tid; i < kConsumers * p.rows_cta * mc * 2; i += kConsumers * 32) ysum[i] = 0.f;
+  for (int i = tid; i < p.rows_cta * mc * kYPitch; i += kConsumers * 32) ysum[i] = 0.f;
   griddep_wait();  // A may come from the previous kernel, and Y may still be read by it
 
   // ---- activations: one pass. Loads in flight at once (float4, U deep); per quantisation
@@ -238,19 +250,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
         float bmax = fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w)));
 #pragma unroll
         for (int off = 1; off < GL; off <<= 1) bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, off));
-        int e = 0;
-        if (bmax > 0.f && isfinite(bmax)) frexpf(bmax, &e);
-        const int sh = max(-120, min(120, 22 - e));
+        const int sh = max(-120, min(120, 22 - frexp_exponent(bmax)));
         int bsum = 0;
         if (f < n4) {
           const int m = f / n4row;
-          bsum = store_digits(dig, p.kp, m, 4 * (f - m * n4row), v[u], ldexpf(1.f, sh));
+          bsum = store_digits(dig, p.kpp, m, 4 * (f - m * n4row), v[u], exp2i(sh));
         }
 #pragma unroll
         for (int off = 1; off < GL; off <<= 1) bsum += __shfl_xor_sync(0xffffffffu, bsum, off);
         if (f < n4 && (lane & (GL - 1)) == 0) {
           sblk[f / GL] = bsum;
-          sinv[f / GL] = ldexpf(1.f, -sh);
+          sinv[f / GL] = exp2i(-sh);
         }
       }
     }
@@ -259,6 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
 
   // ---- main loop: tile t outer, this CTA's row blocks inner; warp w takes units w, w+16
   const int grp = lane >> 2, tq = lane & 3;
+  const float wdig = (tq & 1) ? 65536.f : 1.f;  // weight of this lane's first digit column
   const int units = p.kt / UNIT;
   const int nbp = p.kp / BS;
   int rs = 0;
@@ -266,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
   for (int t = 0; t < T; ++t) {
     // B fragments of this warp's units (digits of columns grp + 8j), held across row blocks
     uint32_t bf[UPW][STEPS][NT][2];
-    int sv[UPW][UB][NT];      // block sums of a_int for this lane's A row(s)
+    float sv[UPW][UB][NT];    // block sums of a_int for this lane's A row(s), 0 on odd lanes
     float sif[UPW][UB][NT];   // 2^-sigma of those blocks
 #pragma unroll
     for (int uu = 0; uu < UPW; ++uu) {
@@ -277,8 +288,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           const int col = nt * 8 + grp;
-          const bool ok = u < units && col < 4 * mc;
-          const int8_t* d = dig + col * p.kp + kk0 + 32 * st + 4 * tq;
+          const bool ok = u < units && col < 4 * mc && (col & 3) != 3;
+          const int8_t* d = dig + col * p.kpp + kk0 + 32 * st + 4 * tq;
           bf[uu][st][nt][0] = ok ? *reinterpret_cast<const uint32_t*>(d) : 0u;
           bf[uu][st][nt][1] = ok ? *reinterpret_cast<const uint32_t*>(d + 16) : 0u;
         }
@@ -288,7 +299,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
         for (int nt = 0; nt < NT; ++nt) {
           const int m = nt * 2 + (tq >> 1);
           const bool okb = u < units && m < mc;
-          sv[uu][bl][nt] = okb ? sblk[m * nbp + kk0 / BS + bl] : 0;
+          // the zero-point term rides on the lanes of digits 0 and 1 (even tq) only
+          sv[uu][bl][nt] = okb && (tq & 1) == 0 ? (float)sblk[m * nbp + kk0 / BS + bl] : 0.f;
           sif[uu][bl][nt] = okb ? sinv[m * nbp + kk0 / BS + bl] : 0.f;
         }
     }
@@ -319,16 +331,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
             for (int bl = 0; bl < UB; ++bl) {
               const int blk_local = u * UB + bl;
               const float s0 = scp[blk_local * 16 + grp];
-              const float s1 = scp[blk_local * 16 + grp + 8];
-              float z0 = 8.f, z1 = 8.f;
+              const float s1 = scp[blk_local * 16 + grp + 8] * 0.0625f;  // undoes the 16 q
+              // z1 is for the high-nibble rows, whose products come out 16x (see below)
+              float z0 = 8.f, z1 = 128.f;
               if (p.zp_kind == ZP_PACKED) {
                 const uint2 zw = reinterpret_cast<const uint2*>(base + p.off_zp)[blk_local];
                 z0 = (float)((zw.x >> (4 * grp)) & 0xF);
-                z1 = (float)((zw.y >> (4 * grp)) & 0xF);
+                z1 = (float)((zw.y >> (4 * grp)) & 0xF) * 16.f;
               } else if (p.zp_kind == ZP_F32) {
                 const float* zf = reinterpret_cast<const float*>(base + p.off_zp);
                 z0 = zf[blk_local * 16 + grp];
-                z1 = zf[blk_local * 16 + grp + 8];
+                z1 = zf[blk_local * 16 + grp + 8] * 16.f;
               }
               int c[NT][4];
 #pragma unroll
@@ -336,27 +349,25 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
 #pragma unroll
               for (int q = 0; q < BSTEPS; ++q) {
                 const int st = bl * BSTEPS + q;
+                // rows r+8 keep their codes in the high nibble: 16 q as a u8, exact
                 const uint32_t x0 = wv[2 * st], x1 = wv[2 * st + 1];
-                const uint32_t lo0 = x0 & 0x0F0F0F0Fu, hi0 = (x0 >> 4) & 0x0F0F0F0Fu;
-                const uint32_t lo1 = x1 & 0x0F0F0F0Fu, hi1 = (x1 >> 4) & 0x0F0F0F0Fu;
+                const uint32_t lo0 = x0 & 0x0F0F0F0Fu, hi0 = x0 & 0xF0F0F0F0u;
+                const uint32_t lo1 = x1 & 0x0F0F0F0Fu, hi1 = x1 & 0xF0F0F0F0u;
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
                   imma(c[nt], lo0, hi0, lo1, hi1, bf[uu][st][nt][0], bf[uu][st][nt][1]);
               }
 #pragma unroll
               for (int nt = 0; nt < NT; ++nt) {
-                // even lanes hold digits 0,1 (plus the zero-point term), odd lanes digit 2
-                float f0, f1;
-                if ((tq & 1) == 0) {
-                  const float zs = (float)sv[uu][bl][nt];
-                  f0 = fmaf(-z0, zs, (float)(c[nt][0] + 256 * c[nt][1]));
-                  f1 = fmaf(-z1, zs, (float)(c[nt][2] + 256 * c[nt][3]));
-                } else {
-                  f0 = 65536.f * (float)c[nt][0];
-                  f1 = 65536.f * (float)c[nt][2];
-                }
-                y0[nt] = fmaf(s0 * sif[uu][bl][nt], f0, y0[nt]);
-                y1[nt] = fmaf(s1 * sif[uu][bl][nt], f1, y1[nt]);
+                // even lanes hold digits 0 and 1 (and the zero-point term), odd lanes digit 2
+                // and the always-zero fourth column: f = (c_a + 256 c_b) * wdig - z * S, the
+                // integer combination exact in s32 (|c| < 2^22 even for the 16x rows)
+                const float zs = sv[uu][bl][nt];
+                const float f0 = fmaf((float)(c[nt][0] + 256 * c[nt][1]), wdig, -z0 * zs);
+                const float f1 = fmaf((float)(c[nt][2] + 256 * c[nt][3]), wdig, -z1 * zs);
+                const float g = sif[uu][bl][nt];
+                y0[nt] = fmaf(s0 * g, f0, y0[nt]);
+                y1[nt] = fmaf(s1 * g, f1, y1[nt]);
               }
             }
           }
@@ -365,9 +376,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
         for (int nt = 0; nt < NT; ++nt) {
           const int m = nt * 2 + (tq >> 1);
           if (m < mc) {
-            float* yc = ysum + ((warp * p.rows_cta + i * 16 + grp) * mc + m) * 2 + (tq & 1);
+            float* yc = ysum + (((i * 16 + grp) * mc + m) * kYSlots + warp) * 2 + (tq & 1);
             yc[0] += y0[nt];
-            yc[8 * mc * 2] += y1[nt];
+            yc[8 * mc * kYPitch] += y1[nt];
           }
         }
       }
@@ -381,19 +392,27 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
   }
   ptx::named_bar_sync(1, kConsumers * 32);
 
-  // ---- fixed-order sum over warps and digit lanes, unscale, store (coalesced along rows)
-  for (int idx = tid; idx < mc * p.rows_cta; idx += kConsumers * 32) {
-    const int m = idx / p.rows_cta, r = idx - m * p.rows_cta;
-    const int ib = r >> 4, rl = r & 15;
-    const int b = blockIdx.x + ib * grid;
-    const int64_t row = (int64_t)b * 16 + rl;
-    if (b < p.nblk && row < p.n_rows) {
-      float acc = 0.f;
-      for (int ww = 0; ww < kConsumers; ++ww) {
-        const float* yc = ysum + ((ww * p.rows_cta + r) * mc + m) * 2;
-        acc += yc[0] + yc[1];
-      }
-      p.y[(p.m0 + m) * p.ldy + row] = acc;
+  // ---- fixed-order sum of the 32 partials (warp, parity) of each output: groups of G
+  // consecutive threads per output (G as large as fits all outputs in one pass of 512
+  // threads), each thread summing 32/G partials in order, then a fixed shuffle tree over G
+  const int nout = mc * p.rows_cta;
+  int G = 32;
+  while (G > 1 && G * nout > kConsumers * 32) G >>= 1;
+  const int per = 32 / G;
+  for (int base = 0; base < nout * G; base += kConsumers * 32) {
+    const int idx = base + tid;
+    const int o = idx / G, j = idx - o * G;
+    float acc = 0.f;
+    if (o < nout) {
+      const float* src = ysum + o * kYPitch + j * per;
+      for (int q = 0; q < per; ++q) acc += src[q];
+    }
+    for (int off = G >> 1; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (o < nout && j == 0) {
+      const int r = o / mc, m = o - r * mc;
+      const int b = blockIdx.x + (r >> 4) * grid;
+      const int64_t row = (int64_t)b * 16 + (r & 15);
+      if (b < p.nblk && row < p.n_rows) p.y[(p.m0 + m) * p.ldy + row] = acc;
     }
   }
 }
@@ -430,10 +449,10 @@ inline int align_up(int v, int a) { return (v + a - 1) / a * a; }
 size_t plan_smem(const Weights& w, int mc, int grid, Args& a) {
   const int kp = w.ntiles * w.kt;
   const int head = 64 + 16 * kMaxM * 4;
-  const int dig = 4 * mc * kp;
+  const int dig = 4 * mc * (kp + 16);
   const int sb = align_up(8 * mc * (kp / w.block_size), 16);  // block sums + block scales
   a.rows_cta = ((w.nblk + grid - 1) / grid) * 16;
-  const int ysum = align_up(kConsumers * a.rows_cta * mc * 2 * 4, 16);
+  const int ysum = align_up(a.rows_cta * mc * kYPitch * 4, 16);
   const int bars = 2 * kMaxSlots * 8 + 16;
   a.off_dig = align_up(head, 16);
   a.off_s = a.off_dig + align_up(dig, 16);
@@ -480,6 +499,7 @@ int run_gemv_mma(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype
     a.off_zp = w.off_zp;
     a.zp_kind = w.zp_kind;
     a.kp = w.ntiles * w.kt;
+    a.kpp = a.kp + 16;
     a.prefetch = w.settled.load(std::memory_order_relaxed) ? 1 : 0;
     {
       const uintptr_t ap = reinterpret_cast<uintptr_t>(d_a);
