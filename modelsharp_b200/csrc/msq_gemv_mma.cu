@@ -33,8 +33,9 @@ constexpr int kThreads = (kConsumers + 1) * 32;
 constexpr int kMaxSlots = 8;
 constexpr int kSmemMax = 227 * 1024;
 constexpr int kMaxM = 4;  // B columns: 4 per A row (3 digits + 1 zero) -> two n8 tiles for 4 rows
-constexpr int kYSlots = kConsumers + 1;  // per-warp partial sums of one output, padded against
-constexpr int kYPitch = 2 * kYSlots;     // bank conflicts in the per-stage update
+constexpr int kUpw = 2;                 // k-units per warp per tile
+constexpr int kYPitch = kConsumers + 1;  // per-warp partial sums of one output, padded against
+                                         // bank conflicts in the per-stage update
 
 __device__ int g_mma_err;
 
@@ -155,12 +156,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
   constexpr int UB = UNIT / BS;     // blocks per unit
   constexpr int STEPS = UNIT / 32;  // k32 mma steps per unit
   constexpr int BSTEPS = BS / 32;   // k32 steps per block
-  constexpr int UPW = 2;            // units per warp per tile (kt <= 32 units)
+  constexpr int UPW = kUpw;
   extern __shared__ __align__(16) uint8_t smem[];
   int8_t* dig = reinterpret_cast<int8_t*>(smem + p.off_dig);  // [4*mc][kpp] digits
   int* sblk = reinterpret_cast<int*>(smem + p.off_s);         // [mc][kp/BS] exact block sums of a_int
   float* sinv = reinterpret_cast<float*>(sblk + p.mc * (p.kp / BS));  // [mc][kp/BS] 2^-sigma_b
-  float* ysum = reinterpret_cast<float*>(smem + p.off_ysum);  // [rows_cta][mc][17][2]: per warp, parity
+  float* ysum = reinterpret_cast<float*>(smem + p.off_ysum);  // [rows_cta][mc][33]: per warp
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bar);
   uint64_t* empty = full + kMaxSlots;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kMaxSlots);
@@ -229,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
   // ---- activations: one pass. Loads in flight at once (float4, U deep); per quantisation
   // block (GL consecutive lanes) a shuffle max picks 2^sigma_b, the digits are written and a
   // shuffle sum gives the exact block sum of a_int.
-  constexpr int U = 8;
+  constexpr int U = 4;
   constexpr int kC = kConsumers * 32;
   constexpr int GL = BS / 4;  // float4 per quantisation block (8 / 16 / 32 lanes)
   const int n4row = p.kp / 4;
@@ -306,79 +307,105 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
     }
 
     for (int i = 0; i < nb_cta; ++i) {
-      const bool ok = wait_or_abort(&full[rs], rph, abort_flag, ptx::kErrTimeoutFull);
+      // warp-uniform: the stage's epilogue shuffles need every lane
+      const bool ok = __all_sync(0xffffffffu, wait_or_abort(&full[rs], rph, abort_flag, ptx::kErrTimeoutFull));
       if (ok) {
         const uint8_t* base = ring + rs * p.stage_bytes;
         const float* scp = reinterpret_cast<const float*>(base + p.off_sc);
+        // Both units of this warp as independent chains, each block's k32 steps split over
+        // two accumulators, so the tensor-core latency overlaps; a missing second unit
+        // (kt < 32 units) reads unit 0's words and contributes nothing (its sif is 0).
+        uint32_t wv[UPW][4 * CH];
+        float s0[UPW][UB], s1[UPW][UB], z0[UPW][UB], z1[UPW][UB];
+#pragma unroll
+        for (int uu = 0; uu < UPW; ++uu) {
+          const int u = warp + uu * kConsumers;
+          const int ul = u < units ? u : 0;  // unit 0 always exists in a stage
+          const uint4* nib = reinterpret_cast<const uint4*>(base) + ul * CH * 32 + lane;
+#pragma unroll
+          for (int c = 0; c < CH; ++c) {
+            const uint4 q4 = nib[c * 32];
+            wv[uu][4 * c + 0] = q4.x;
+            wv[uu][4 * c + 1] = q4.y;
+            wv[uu][4 * c + 2] = q4.z;
+            wv[uu][4 * c + 3] = q4.w;
+          }
+#pragma unroll
+          for (int bl = 0; bl < UB; ++bl) {
+            const int blk_local = ul * UB + bl;
+            s0[uu][bl] = scp[blk_local * 16 + grp];
+            s1[uu][bl] = scp[blk_local * 16 + grp + 8] * 0.0625f;  // undoes the 16 q
+            // z1 is for the high-nibble rows, whose products come out 16x (see below)
+            if (p.zp_kind == ZP_PACKED) {
+              const uint2 zw = reinterpret_cast<const uint2*>(base + p.off_zp)[blk_local];
+              z0[uu][bl] = (float)((zw.x >> (4 * grp)) & 0xF);
+              z1[uu][bl] = (float)((zw.y >> (4 * grp)) & 0xF) * 16.f;
+            } else if (p.zp_kind == ZP_F32) {
+              const float* zf = reinterpret_cast<const float*>(base + p.off_zp);
+              z0[uu][bl] = zf[blk_local * 16 + grp];
+              z1[uu][bl] = zf[blk_local * 16 + grp + 8] * 16.f;
+            } else {
+              z0[uu][bl] = 8.f;
+              z1[uu][bl] = 128.f;
+            }
+          }
+        }
+        int c[UPW][UB][2][NT][4];
+#pragma unroll
+        for (int uu = 0; uu < UPW; ++uu)
+#pragma unroll
+          for (int bl = 0; bl < UB; ++bl)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt) c[uu][bl][h][nt][0] = c[uu][bl][h][nt][1] = c[uu][bl][h][nt][2] = c[uu][bl][h][nt][3] = 0;
+#pragma unroll
+        for (int q = 0; q < BSTEPS; ++q)
+#pragma unroll
+          for (int bl = 0; bl < UB; ++bl)
+#pragma unroll
+            for (int uu = 0; uu < UPW; ++uu) {
+              const int st = bl * BSTEPS + q;
+              // rows r+8 keep their codes in the high nibble: 16 q as a u8, exact
+              const uint32_t x0 = wv[uu][2 * st], x1 = wv[uu][2 * st + 1];
+              const uint32_t lo0 = x0 & 0x0F0F0F0Fu, hi0 = x0 & 0xF0F0F0F0u;
+              const uint32_t lo1 = x1 & 0x0F0F0F0Fu, hi1 = x1 & 0xF0F0F0F0u;
+#pragma unroll
+              for (int nt = 0; nt < NT; ++nt)
+                imma(c[uu][bl][q & 1][nt], lo0, hi0, lo1, hi1, bf[uu][st][nt][0], bf[uu][st][nt][1]);
+            }
         float y0[NT], y1[NT];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) y0[nt] = y1[nt] = 0.f;
 #pragma unroll
-        for (int uu = 0; uu < UPW; ++uu) {
-          const int u = warp + uu * kConsumers;
-          if (u < units) {
-            const uint4* nib = reinterpret_cast<const uint4*>(base) + u * CH * 32 + lane;
-            uint32_t wv[4 * CH];
+        for (int uu = 0; uu < UPW; ++uu)
 #pragma unroll
-            for (int c = 0; c < CH; ++c) {
-              const uint4 q4 = nib[c * 32];
-              wv[4 * c + 0] = q4.x;
-              wv[4 * c + 1] = q4.y;
-              wv[4 * c + 2] = q4.z;
-              wv[4 * c + 3] = q4.w;
+          for (int bl = 0; bl < UB; ++bl)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              int cc[4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) cc[j] = c[uu][bl][0][nt][j] + c[uu][bl][1][nt][j];
+              // even lanes hold digits 0 and 1 (and the zero-point term), odd lanes digit 2
+              // and the always-zero fourth column: f = (c_a + 256 c_b) * wdig - z * S, the
+              // integer combination exact in s32 (|c| < 2^22 even for the 16x rows)
+              const float zs = sv[uu][bl][nt];
+              const float f0 = fmaf((float)(cc[0] + 256 * cc[1]), wdig, -z0[uu][bl] * zs);
+              const float f1 = fmaf((float)(cc[2] + 256 * cc[3]), wdig, -z1[uu][bl] * zs);
+              const float g = sif[uu][bl][nt];
+              y0[nt] = fmaf(s0[uu][bl] * g, f0, y0[nt]);
+              y1[nt] = fmaf(s1[uu][bl] * g, f1, y1[nt]);
             }
-#pragma unroll
-            for (int bl = 0; bl < UB; ++bl) {
-              const int blk_local = u * UB + bl;
-              const float s0 = scp[blk_local * 16 + grp];
-              const float s1 = scp[blk_local * 16 + grp + 8] * 0.0625f;  // undoes the 16 q
-              // z1 is for the high-nibble rows, whose products come out 16x (see below)
-              float z0 = 8.f, z1 = 128.f;
-              if (p.zp_kind == ZP_PACKED) {
-                const uint2 zw = reinterpret_cast<const uint2*>(base + p.off_zp)[blk_local];
-                z0 = (float)((zw.x >> (4 * grp)) & 0xF);
-                z1 = (float)((zw.y >> (4 * grp)) & 0xF) * 16.f;
-              } else if (p.zp_kind == ZP_F32) {
-                const float* zf = reinterpret_cast<const float*>(base + p.off_zp);
-                z0 = zf[blk_local * 16 + grp];
-                z1 = zf[blk_local * 16 + grp + 8] * 16.f;
-              }
-              int c[NT][4];
-#pragma unroll
-              for (int nt = 0; nt < NT; ++nt) c[nt][0] = c[nt][1] = c[nt][2] = c[nt][3] = 0;
-#pragma unroll
-              for (int q = 0; q < BSTEPS; ++q) {
-                const int st = bl * BSTEPS + q;
-                // rows r+8 keep their codes in the high nibble: 16 q as a u8, exact
-                const uint32_t x0 = wv[2 * st], x1 = wv[2 * st + 1];
-                const uint32_t lo0 = x0 & 0x0F0F0F0Fu, hi0 = x0 & 0xF0F0F0F0u;
-                const uint32_t lo1 = x1 & 0x0F0F0F0Fu, hi1 = x1 & 0xF0F0F0F0u;
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
-                  imma(c[nt], lo0, hi0, lo1, hi1, bf[uu][st][nt][0], bf[uu][st][nt][1]);
-              }
-#pragma unroll
-              for (int nt = 0; nt < NT; ++nt) {
-                // even lanes hold digits 0 and 1 (and the zero-point term), odd lanes digit 2
-                // and the always-zero fourth column: f = (c_a + 256 c_b) * wdig - z * S, the
-                // integer combination exact in s32 (|c| < 2^22 even for the 16x rows)
-                const float zs = sv[uu][bl][nt];
-                const float f0 = fmaf((float)(c[nt][0] + 256 * c[nt][1]), wdig, -z0 * zs);
-                const float f1 = fmaf((float)(c[nt][2] + 256 * c[nt][3]), wdig, -z1 * zs);
-                const float g = sif[uu][bl][nt];
-                y0[nt] = fmaf(s0 * g, f0, y0[nt]);
-                y1[nt] = fmaf(s1 * g, f1, y1[nt]);
-              }
-            }
-          }
-        }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
+          // digits 0,1 (even lane) + digit 2 (odd lane) of one A row: fold the pair
+          const float v0 = y0[nt] + __shfl_xor_sync(0xffffffffu, y0[nt], 1);
+          const float v1 = y1[nt] + __shfl_xor_sync(0xffffffffu, y1[nt], 1);
           const int m = nt * 2 + (tq >> 1);
-          if (m < mc) {
-            float* yc = ysum + (((i * 16 + grp) * mc + m) * kYSlots + warp) * 2 + (tq & 1);
-            yc[0] += y0[nt];
-            yc[8 * mc * kYPitch] += y1[nt];
+          if (m < mc && (tq & 1) == 0) {
+            float* yc = ysum + ((i * 16 + grp) * mc + m) * kYPitch + warp;
+            yc[0] += v0;
+            yc[8 * mc * kYPitch] += v1;
           }
         }
       }
@@ -392,13 +419,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
   }
   ptx::named_bar_sync(1, kConsumers * 32);
 
-  // ---- fixed-order sum of the 32 partials (warp, parity) of each output: groups of G
-  // consecutive threads per output (G as large as fits all outputs in one pass of 512
-  // threads), each thread summing 32/G partials in order, then a fixed shuffle tree over G
+  // ---- fixed-order sum of the kConsumers per-warp partials of each output: groups of G
+  // consecutive threads per output (G as large as fits all outputs in one pass of the
+  // consumer threads), each thread summing kConsumers/G partials in order, then a fixed
+  // shuffle tree over G lanes
   const int nout = mc * p.rows_cta;
-  int G = 32;
+  int G = kConsumers;
   while (G > 1 && G * nout > kConsumers * 32) G >>= 1;
-  const int per = 32 / G;
+  const int per = kConsumers / G;
   for (int base = 0; base < nout * G; base += kConsumers * 32) {
     const int idx = base + tid;
     const int o = idx / G, j = idx - o * G;
@@ -478,7 +506,7 @@ int run_gemv_mma(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype
                  int64_t ldy) {
   if (!w.strm || (w.block_size != 32 && w.block_size != 64 && w.block_size != 128)) return MSQ_E_UNSUPPORTED;
   const int unit = w.block_size > 64 ? w.block_size : 64;
-  if (w.kt / unit > 2 * kConsumers) return MSQ_E_UNSUPPORTED;
+  if (w.kt / unit > kUpw * kConsumers) return MSQ_E_UNSUPPORTED;
   const int sms = num_sms(w.device);
   int64_t m0 = 0;
   while (m0 < M) {
