@@ -113,29 +113,33 @@ __device__ __forceinline__ float4 load4(const Args& p, int m, int k) {
   return make_float4(v[0], v[1], v[2], v[3]);
 }
 
-// rint(x * 2^sigma) as a 24-bit integer.
-__device__ __forceinline__ int fixed24(float x, float sc) { return __float2int_rn(x * sc); }
+// Digits of 4 consecutive k: a = rint(x * 2^sigma) (|a| < 2^22) in balanced base 256,
+// a = d0 + 256 d1 + 65536 d2 with d_i in [-128, 127]. u = a + 0x808080 holds d_i + 128 in its
+// byte i, and the magic constant 1.5 * 2^23 makes one fma produce u in the low mantissa bits
+// (the product is exact, the add rounds to nearest even at integer granularity). The bytes
+// are transposed into one word per digit (w0: d0 of the 4 k, ...); returns sum a exactly.
+__device__ __forceinline__ uint32_t biased24(float x, float sc) {
+  return __float_as_uint(fmaf(x, sc, 12582912.0f)) - (0x4B400000u - 0x808080u);
+}
+__device__ __forceinline__ int digit_words(float4 v, float sc, uint32_t& w0, uint32_t& w1, uint32_t& w2) {
+  const uint32_t u0 = biased24(v.x, sc), u1 = biased24(v.y, sc), u2 = biased24(v.z, sc), u3 = biased24(v.w, sc);
+  const uint32_t t01 = __byte_perm(u0, u1, 0x5140), t23 = __byte_perm(u2, u3, 0x5140);  // b0,b0',b1,b1'
+  const uint32_t s01 = __byte_perm(u0, u1, 0x0062), s23 = __byte_perm(u2, u3, 0x0062);  // b2,b2'
+  w0 = __byte_perm(t01, t23, 0x5410) ^ 0x80808080u;
+  w1 = __byte_perm(t01, t23, 0x7632) ^ 0x80808080u;
+  w2 = __byte_perm(s01, s23, 0x5410) ^ 0x80808080u;
+  return (int)((u0 + u1) + (u2 + u3) - 4u * 0x808080u);
+}
 
-// Writes the three balanced int8 digits of 4 consecutive k of row m (columns 4m..4m+2 of the
-// digit array, row pitch kpp; the fourth column of each row is never read) and returns their
-// exact integer sum.
+// Writes the digit words of 4 consecutive k of row m (columns 4m..4m+2 of the digit array,
+// row pitch kpp; the fourth column of each row is never read) and returns their exact sum.
 __device__ __forceinline__ int store_digits(int8_t* dig, int kpp, int m, int k, float4 v, float sc) {
-  const int a[4] = {fixed24(v.x, sc), fixed24(v.y, sc), fixed24(v.z, sc), fixed24(v.w, sc)};
-  uint32_t w0 = 0, w1 = 0, w2 = 0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int d0 = ((a[j] + 128) & 255) - 128;
-    const int r1 = (a[j] - d0) >> 8;
-    const int d1 = ((r1 + 128) & 255) - 128;
-    const int d2 = (r1 - d1) >> 8;
-    w0 |= (uint32_t)(d0 & 255) << (8 * j);
-    w1 |= (uint32_t)(d1 & 255) << (8 * j);
-    w2 |= (uint32_t)(d2 & 255) << (8 * j);
-  }
+  uint32_t w0, w1, w2;
+  const int sum = digit_words(v, sc, w0, w1, w2);
   *reinterpret_cast<uint32_t*>(dig + (4 * m + 0) * kpp + k) = w0;
   *reinterpret_cast<uint32_t*>(dig + (4 * m + 1) * kpp + k) = w1;
   *reinterpret_cast<uint32_t*>(dig + (4 * m + 2) * kpp + k) = w2;
-  return (a[0] + a[1]) + (a[2] + a[3]);
+  return sum;
 }
 
 // Exponent e of frexp(x) for finite x > 0 (x = f * 2^e, f in [0.5, 1)), -126 for subnormals,
@@ -249,16 +253,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
       if (u < nu) {
         const int f = base + tid + u * kC;
         float bmax = fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w)));
+        if constexpr (GL == 32) {  // one block per warp: non-negative floats order as their bits
+          bmax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(bmax)));
+        } else {
 #pragma unroll
-        for (int off = 1; off < GL; off <<= 1) bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, off));
+          for (int off = 1; off < GL; off <<= 1) bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, off));
+        }
         const int sh = max(-120, min(120, 22 - frexp_exponent(bmax)));
         int bsum = 0;
         if (f < n4) {
           const int m = f / n4row;
           bsum = store_digits(dig, p.kpp, m, 4 * (f - m * n4row), v[u], exp2i(sh));
         }
+        if constexpr (GL == 32) {
+          bsum = (int)__reduce_add_sync(0xffffffffu, (uint32_t)bsum);
+        } else {
 #pragma unroll
-        for (int off = 1; off < GL; off <<= 1) bsum += __shfl_xor_sync(0xffffffffu, bsum, off);
+          for (int off = 1; off < GL; off <<= 1) bsum += __shfl_xor_sync(0xffffffffu, bsum, off);
+        }
         if (f < n4 && (lane & (GL - 1)) == 0) {
           sblk[f / GL] = bsum;
           sinv[f / GL] = exp2i(-sh);
