@@ -366,6 +366,147 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             w.free()
 
 
+# ---------------------------------------------------------------- N-split workload
+NSPLIT_LAYERS = [(8192, 28672), (28672, 8192)]  # (K, N): 70B MLP up-proj, then down-proj
+NSPLIT_WORKLOAD = ("70B-shaped MLP (BASELINE configs[3]) column-split over the ranks with an NCCL all-gather of Y: "
+                   "up-proj K=8192 N=28672 then down-proj K=28672 N=8192 fed with the gathered up-proj output; "
+                   "bits=4, block_size=128, packed zero points, fp16 scales, fp16 A")
+
+
+def run_nsplit(args, rank: int, world: int, local_rank: int):
+    """Each rank packs its row shard of both layers; one step = up-proj shard, all-gather, down-proj
+    shard, all-gather, captured in one CUDA graph; value = the layers' algorithmic bytes per step
+    over the max-over-ranks step time (total work fixed: strong scaling)."""
+    import torch
+    import torch.distributed as dist
+
+    from modelsharp_b200 import synth
+    from modelsharp_b200.nsplit import ShardedMatMulNBits
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    M = args.m
+    cases = [synth.make_case(100 + i, M, n, k, 4, BS, "packed", a_dtype="f16", scale_dtype="f16",
+                             scale_lo=SCALE_LO, scale_hi=SCALE_HI) for i, (k, n) in enumerate(NSPLIT_LAYERS)]
+    nbytes = sum(synth.algorithmic_bytes(n, k, 4, BS, "packed", scale_bytes=2) for k, n in NSPLIT_LAYERS)
+    shard_bytes = nbytes / world
+    # enough replicas of this rank's shards that the rotation exceeds L2 (>= 320 MB per rank)
+    reps_n = max(2, -(-int(320e6) // int(shard_bytes)))
+    full = [[torch.from_numpy(np.ascontiguousarray(x)).to(dev) if x is not None else None
+             for x in (c["b"], c["scales"], c["zp"])] for c in cases]
+    reps = [[ShardedMatMulNBits(b, s, z, c["N"], c["K"], 4, BS, device=dev) for (b, s, z), c in zip(full, cases)]
+            for _ in range(reps_n)]
+    del full
+    a0 = torch.from_numpy(cases[0]["a"]).to(dev)
+    stream = torch.cuda.Stream(dev)
+
+    def step(r: int, a: torch.Tensor) -> torch.Tensor:
+        y_up = reps[r][0](a)
+        return reps[r][1](y_up)
+
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            y = step(i % reps_n, a0)
+    stream.synchronize()
+    graphs, outs = [], []
+    for r in range(reps_n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            outs.append(step(r, a0))
+        graphs.append(g)
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            graphs[i % reps_n].replay()
+    stream.synchronize()
+    y_chk = outs[0].float().cpu().numpy()
+
+    dist.barrier() if world > 1 else None
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        ev0.record(stream)
+        with torch.cuda.stream(stream):
+            for i in range(args.steps):
+                graphs[i % reps_n].replay()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    dist.barrier() if world > 1 else None
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = nbytes * args.steps / (ms * 1e-3) / 1e9
+
+    # e2e through the sharded op with host buffers: A in, the down-proj Y out, every step
+    a_host = torch.from_numpy(cases[0]["a"]).pin_memory()
+    y_host = torch.empty(M, NSPLIT_LAYERS[1][1]).pin_memory()
+    e2e_steps = max(1, min(args.steps, 500))
+    for i in range(max(args.warmup, 3)):
+        y_host.copy_(step(i % reps_n, a_host.to(dev, non_blocking=True)), non_blocking=True)
+    torch.cuda.synchronize(dev)
+    dist.barrier() if world > 1 else None
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(e2e_steps):
+        y_host.copy_(step(i % reps_n, a_host.to(dev, non_blocking=True)), non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = nbytes * e2e_steps / (e2e_ms * 1e-3) / 1e9
+
+    peak, peak_kind = peaks()
+    per_rank_achieved = shard_bytes / (ms / args.steps * 1e-3) / 1e9
+    if rank == 0:
+        from oracle import oracle
+        # parity of the assembled output against the checker chain (up-proj output fed to the down-proj)
+        y_up_ref = oracle.managed(cases[0])
+        c1 = dict(cases[1], a=y_up_ref, M=M)
+        parity = oracle.rel_l2(y_chk, oracle.managed(c1))
+        cpu = None
+        if world == 1:
+            t0 = time.perf_counter()
+            reps_cpu = 0
+            while time.perf_counter() - t0 < max(args.cpu_seconds, 0.1) or reps_cpu < 1:
+                ref_fn = oracle.reference_native if oracle.reference_available() else oracle.managed
+                ref_fn(dict(cases[0], a=cases[0]["a"].astype(np.float32), scales=cases[0]["scales"].astype(np.float32)))
+                ref_fn(dict(c1, scales=c1["scales"].astype(np.float32)))
+                reps_cpu += 1
+            dt = (time.perf_counter() - t0) / reps_cpu
+            cpu = {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": os.cpu_count(),
+                   "kind": "reference" if oracle.reference_available() else "port",
+                   "sample": f"{reps_cpu} steps (both layers, fp16 inputs widened to fp32), mean, all host threads"}
+        out = {
+            "metric": "MatMulNBits INT4 N-split HBM GB/s", "value": value, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f16 in, f32 accumulate", "data": "synthetic",
+            "config": {"workload": NSPLIT_WORKLOAD, "M": M, "bytes_per_step": nbytes, "parallelism": f"nsplit{world}",
+                       "l2": f"{reps_n} replicas of each rank's shards rotate ({reps_n * shard_bytes / 1e6:.0f} MB per rank)",
+                       "launch": "one CUDA graph replay per step (2 local GEMV launches + 2 NCCL all-gathers)",
+                       "parity_rel_l2": parity},
+            "roofline": {"bound": "hbm", "achieved": per_rank_achieved, "peak": peak, "unit": "GB/s",
+                         "frac": per_rank_achieved / peak, "traffic": None,
+                         "peak_source": f"{peak_kind} HBM copy bandwidth",
+                         "note": "per-rank shard bytes over the whole step time (all-gathers included)"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": a_host.numel() * 2,
+                    "d2h_bytes_per_step": y_host.numel() * 4, "steps": e2e_steps, "entry": "ShardedMatMulNBits"},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(out), flush=True)
+    for g in graphs:
+        del g
+    graphs.clear()
+    for rr in reps:
+        for sh in rr:
+            sh.free()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -373,6 +514,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--workload", default="sweep7b", choices=["sweep7b", "nsplit70b"])
+    ap.add_argument("--m", type=int, default=1, help="A rows for the nsplit70b workload")
     ap.add_argument("--shapes", default="",
                     help="restrict the step to these KxN shapes (comma separated), for profiling one shape")
     args = ap.parse_args()
@@ -398,7 +541,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, rank, world, local_rank)
+        if args.workload == "nsplit70b":
+            run_nsplit(args, rank, world, local_rank)
+        else:
+            run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist
