@@ -368,7 +368,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
 # ---------------------------------------------------------------- N-split workload
 NSPLIT_LAYERS = [(8192, 28672), (28672, 8192)]  # (K, N): 70B MLP up-proj, then down-proj
-NSPLIT_WORKLOAD = ("70B-shaped MLP (BASELINE configs[3]) column-split over the ranks with an NCCL all-gather of Y: "
+NSPLIT_WORKLOAD = ("70B-shaped MLP (BASELINE configs[3]) column-split over the ranks with a gather of Y: "
                    "up-proj K=8192 N=28672 then down-proj K=28672 N=8192 fed with the gathered up-proj output; "
                    "bits=4, block_size=128, packed zero points, fp16 scales, fp16 A")
 
@@ -394,15 +394,16 @@ def run_nsplit(args, rank: int, world: int, local_rank: int):
     reps_n = max(2, -(-int(320e6) // int(shard_bytes)))
     full = [[torch.from_numpy(np.ascontiguousarray(x)).to(dev) if x is not None else None
              for x in (c["b"], c["scales"], c["zp"])] for c in cases]
-    reps = [[ShardedMatMulNBits(b, s, z, c["N"], c["K"], 4, BS, device=dev) for (b, s, z), c in zip(full, cases)]
-            for _ in range(reps_n)]
+    gather = args.gather if M <= 4 else "nccl"
+    reps = [[ShardedMatMulNBits(b, s, z, c["N"], c["K"], 4, BS, device=dev, gather=gather)
+             for (b, s, z), c in zip(full, cases)] for _ in range(reps_n)]
     del full
     a0 = torch.from_numpy(cases[0]["a"]).to(dev)
     stream = torch.cuda.Stream(dev)
 
     def step(r: int, a: torch.Tensor) -> torch.Tensor:
         y_up = reps[r][0](a)
-        return reps[r][1](y_up)
+        return reps[r][1](y_up, wait=reps[r][0].out_wait)
 
     with torch.cuda.stream(stream):
         for i in range(max(args.warmup, 3)):
@@ -417,6 +418,9 @@ def run_nsplit(args, rank: int, world: int, local_rank: int):
     with torch.cuda.stream(stream):
         for i in range(max(args.warmup, 3)):
             graphs[i % reps_n].replay()
+    with torch.cuda.stream(stream):
+        graphs[0].replay()
+        reps[0][1].wait_gathered()  # every rank's shard of the output has landed here
     stream.synchronize()
     y_chk = outs[0].float().cpu().numpy()
 
@@ -442,14 +446,19 @@ def run_nsplit(args, rank: int, world: int, local_rank: int):
     a_host = torch.from_numpy(cases[0]["a"]).pin_memory()
     y_host = torch.empty(M, NSPLIT_LAYERS[1][1]).pin_memory()
     e2e_steps = max(1, min(args.steps, 500))
+    def e2e_step(i: int):
+        y = step(i % reps_n, a_host.to(dev, non_blocking=True))
+        reps[i % reps_n][1].wait_gathered()
+        y_host.copy_(y, non_blocking=True)
+
     for i in range(max(args.warmup, 3)):
-        y_host.copy_(step(i % reps_n, a_host.to(dev, non_blocking=True)), non_blocking=True)
+        e2e_step(i)
     torch.cuda.synchronize(dev)
     dist.barrier() if world > 1 else None
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(e2e_steps):
-        y_host.copy_(step(i % reps_n, a_host.to(dev, non_blocking=True)), non_blocking=True)
+        e2e_step(i)
     e1.record()
     torch.cuda.synchronize(dev)
     e2e_ms = e0.elapsed_time(e1)
@@ -486,7 +495,10 @@ def run_nsplit(args, rank: int, world: int, local_rank: int):
             "scaling": "strong", "vs_baseline": None, "dtype": "f16 in, f32 accumulate", "data": "synthetic",
             "config": {"workload": NSPLIT_WORKLOAD, "M": M, "bytes_per_step": nbytes, "parallelism": f"nsplit{world}",
                        "l2": f"{reps_n} replicas of each rank's shards rotate ({reps_n * shard_bytes / 1e6:.0f} MB per rank)",
-                       "launch": "one CUDA graph replay per step (2 local GEMV launches + 2 NCCL all-gathers)",
+                       "launch": ("one CUDA graph replay per step: 2 GEMV launches that store into every rank's "
+                                  "Y over NVLink and signal completion" if gather == "p2p" else
+                                  "one CUDA graph replay per step (2 local GEMV launches + 2 NCCL all-gathers)"),
+                       "gather": gather,
                        "parity_rel_l2": parity},
             "roofline": {"bound": "hbm", "achieved": per_rank_achieved, "peak": peak, "unit": "GB/s",
                          "frac": per_rank_achieved / peak, "traffic": None,
@@ -516,6 +528,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--workload", default="sweep7b", choices=["sweep7b", "nsplit70b"])
     ap.add_argument("--m", type=int, default=1, help="A rows for the nsplit70b workload")
+    ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
+                    help="nsplit70b: fused peer-store gather (M <= 4) or NCCL all-gather")
     ap.add_argument("--shapes", default="",
                     help="restrict the step to these KxN shapes (comma separated), for profiling one shape")
     args = ap.parse_args()

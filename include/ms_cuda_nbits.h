@@ -152,6 +152,66 @@ int msq_matmul_noalloc(void* cu_ctx, void* stream, msq_weights_t w,
  * No counterpart in the reference (its kernels have no device-side waits).              */
 int msq_device_status(void* cu_ctx, void* stream);
 
+/* ---- column split across GPUs with a fused gather ------------------------------------
+ * The multi-GPU form of the op (rows of B split over ranks, one process per GPU). No
+ * counterpart in the reference, which runs on one device: it replaces the all-gather of
+ * Y that would follow each shard's msq_matmul. The decode GEMV of a shard stores its
+ * outputs straight into every rank's full-Y buffer (peer stores over NVLink), then its last
+ * CTA adds 1 to every rank's arrival counter; a later launch that reads a gathered Y waits
+ * (bounded, 2 s, then MSQ_E_TIMEOUT through msq_device_status) until its rank's counter has
+ * all ranks' arrivals for that output. Counters live in device memory, so repeated CUDA-graph
+ * replays stay in step. Buffers are shared between processes with CUDA IPC.            */
+#define MSQ_MAX_RANKS 8
+#define MSQ_IPC_HANDLE_BYTES 64
+
+/* One layer's output exchange, seen from one rank (all pointers device pointers mapped in
+ * this process). Two of these, with two sets of full-Y buffers, alternate between calls:
+ * each rank reads a gathered output before its next-but-one call of the same layer, and
+ * every rank's calls wait for all ranks' previous outputs, so no rank overwrites a buffer
+ * another rank may still be reading.                                                     */
+typedef struct msq_gather {
+  int nranks;                                   /* ranks of the split (<= MSQ_MAX_RANKS) */
+  int rank;                                     /* this rank                             */
+  float* y[MSQ_MAX_RANKS];                      /* every rank's full-Y buffer            */
+  unsigned long long* arrivals[MSQ_MAX_RANKS];  /* every rank's arrival counter          */
+  int64_t ldy;                                  /* row stride of the full-Y buffers      */
+  int64_t col0;                                 /* first column of this rank's shard     */
+  unsigned long long* produced;                 /* this rank's count of outputs produced */
+  unsigned int* done;                           /* this rank's CTA completion counter    */
+} msq_gather_t;
+
+/* A gathered input: complete on this rank once arrivals >= produced * nranks (the producing
+ * launch on this rank precedes the reader in stream order, so `produced` counts it).     */
+typedef struct msq_wait {
+  const unsigned long long* arrivals;           /* this rank's arrival counter           */
+  const unsigned long long* produced;           /* this rank's produced counter          */
+  int nranks;
+} msq_wait_t;
+
+/* Zeroed device memory for exchange buffers and counters (cudaMalloc'd, so it can be
+ * shared with CUDA IPC); freed with msq_xbuf_free.                                      */
+int msq_xbuf_alloc(void* cu_ctx, int64_t bytes, void** d_ptr);
+int msq_xbuf_free(void* cu_ctx, void* d_ptr);
+
+/* CUDA IPC: the handle (MSQ_IPC_HANDLE_BYTES) of an msq_xbuf_alloc buffer, and mapping a
+ * peer's handle into this process (peer access enabled lazily); close unmaps.            */
+int msq_ipc_handle(void* cu_ctx, void* d_ptr, void* handle);
+int msq_ipc_open(void* cu_ctx, const void* handle, void** d_ptr);
+int msq_ipc_close(void* cu_ctx, void* d_ptr);
+
+/* msq_matmul on this rank's shard (decode GEMV, 1 <= M <= 4) whose output goes to columns
+ * [col0, col0 + n_rows) of rows 0..M-1 of every rank's full-Y buffer. `wait` (or NULL) names
+ * a gathered input: A is read only once all ranks' shards of it have arrived. Every rank
+ * makes the same calls in the same order.                                               */
+int msq_matmul_gather(void* cu_ctx, void* stream, msq_weights_t w,
+                      const void* d_a, int a_dtype, int64_t M,
+                      const msq_wait_t* wait, const msq_gather_t* gather);
+
+/* Waits on `stream` (one small kernel, bounded like the GEMV's wait) until the latest
+ * gathered output is complete on this rank: for readers outside this library, such as a
+ * copy to the host.                                                                      */
+int msq_wait_gathered(void* cu_ctx, void* stream, const msq_wait_t* wait);
+
 /* ---- one-shot drop-in for ms_qgemm_nbits (native/ms_kernels.h:42-44) -----------------
  * Host pointers, fp32 A / scales, packed or NULL zero points; uploads, runs on the
  * current device and downloads per call. Returns a status where the original is void. */

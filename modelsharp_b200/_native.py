@@ -26,6 +26,20 @@ DT_ABSENT, DT_F32, DT_F64, DT_F16, DT_I32, DT_I64, DT_I8, DT_U8, DT_BOOL, DT_BF1
 
 PATH_AUTO, PATH_GENERIC, PATH_GEMV, PATH_GEMM = 0, 1, 2, 3
 NOALLOC_SCRATCH_BYTES = 16 << 20  # MSQ_NOALLOC_SCRATCH_BYTES
+MAX_RANKS = 8  # MSQ_MAX_RANKS
+IPC_HANDLE_BYTES = 64  # MSQ_IPC_HANDLE_BYTES
+
+
+class GatherT(C.Structure):
+    """msq_gather_t: one layer's output exchange seen from one rank."""
+    _fields_ = [("nranks", C.c_int), ("rank", C.c_int), ("y", C.c_void_p * MAX_RANKS),
+                ("arrivals", C.c_void_p * MAX_RANKS), ("ldy", C.c_int64), ("col0", C.c_int64),
+                ("produced", C.c_void_p), ("done", C.c_void_p)]
+
+
+class WaitT(C.Structure):
+    """msq_wait_t: a gathered input to wait for."""
+    _fields_ = [("arrivals", C.c_void_p), ("produced", C.c_void_p), ("nranks", C.c_int)]
 PACK_DEFAULT, PACK_GENERIC_ONLY = 0, 1
 
 LIB_NAME = "libms_cuda_nbits.so"
@@ -54,6 +68,13 @@ SIGNATURES: dict[str, tuple] = {
     "msq_matmul_host": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp]),
     "msq_matmul_noalloc": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp, _i64]),
     "msq_device_status": (_i32, [_vp, _vp]),
+    "msq_xbuf_alloc": (_i32, [_vp, _i64, _vp]),
+    "msq_xbuf_free": (_i32, [_vp, _vp]),
+    "msq_ipc_handle": (_i32, [_vp, _vp, _vp]),
+    "msq_ipc_open": (_i32, [_vp, _vp, _vp]),
+    "msq_ipc_close": (_i32, [_vp, _vp]),
+    "msq_matmul_gather": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp, _vp]),
+    "msq_wait_gathered": (_i32, [_vp, _vp, _vp]),
     "msq_qgemm_nbits": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32]),
 }
 

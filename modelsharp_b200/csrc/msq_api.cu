@@ -535,10 +535,114 @@ int msq_device_status(void* cu_ctx, void* stream) {
   if (rc == MSQ_OK) rc = read_gemm_errors(st, &fm);
   if (rc != MSQ_OK) return rc;
   static const char* what[] = {"", "waiting for a stage to arrive", "waiting for a free stage",
-                               "waiting for the tensor core", "draining in-flight copies"};
-  if (fv) return fail(MSQ_E_TIMEOUT, "decode GEMV kernel gave up %s", what[fv > 0 && fv < 5 ? fv : 0]);
-  if (fm) return fail(MSQ_E_TIMEOUT, "GEMM kernel gave up %s", what[fm > 0 && fm < 5 ? fm : 0]);
+                               "waiting for the tensor core", "draining in-flight copies",
+                               "waiting for other ranks' shards of a gathered input"};
+  if (fv) return fail(MSQ_E_TIMEOUT, "decode GEMV kernel gave up %s", what[fv > 0 && fv < 6 ? fv : 0]);
+  if (fm) return fail(MSQ_E_TIMEOUT, "GEMM kernel gave up %s", what[fm > 0 && fm < 6 ? fm : 0]);
   return MSQ_OK;
+}
+
+int msq_xbuf_alloc(void* cu_ctx, int64_t bytes, void** d_ptr) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  if (!d_ptr || bytes <= 0) return fail(MSQ_E_INVALID, "msq_xbuf_alloc: need a positive size and an output pointer");
+  *d_ptr = nullptr;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, (size_t)bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "msq_xbuf_alloc");
+  e = cudaMemset(p, 0, (size_t)bytes);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "msq_xbuf_alloc zero fill");
+  }
+  *d_ptr = p;
+  return MSQ_OK;
+}
+
+int msq_xbuf_free(void* cu_ctx, void* d_ptr) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  if (d_ptr) MSQ_CUDA_TRY(cudaFree(d_ptr), "msq_xbuf_free");
+  return MSQ_OK;
+}
+
+int msq_ipc_handle(void* cu_ctx, void* d_ptr, void* handle) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == MSQ_IPC_HANDLE_BYTES, "IPC handle size");
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  if (!d_ptr || !handle) return fail(MSQ_E_INVALID, "msq_ipc_handle: NULL pointer");
+  cudaIpcMemHandle_t h;
+  MSQ_CUDA_TRY(cudaIpcGetMemHandle(&h, d_ptr), "cudaIpcGetMemHandle");
+  std::memcpy(handle, &h, sizeof h);
+  return MSQ_OK;
+}
+
+int msq_ipc_open(void* cu_ctx, const void* handle, void** d_ptr) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  if (!d_ptr || !handle) return fail(MSQ_E_INVALID, "msq_ipc_open: NULL pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof h);
+  *d_ptr = nullptr;
+  MSQ_CUDA_TRY(cudaIpcOpenMemHandle(d_ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+  return MSQ_OK;
+}
+
+int msq_ipc_close(void* cu_ctx, void* d_ptr) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  if (d_ptr) MSQ_CUDA_TRY(cudaIpcCloseMemHandle(d_ptr), "cudaIpcCloseMemHandle");
+  return MSQ_OK;
+}
+
+namespace {
+int check_wait(const msq_wait_t* wt, const char* fn) {
+  if (!wt) return MSQ_OK;
+  if (!wt->arrivals || !wt->produced) return fail(MSQ_E_INVALID, "%s: wait counters are NULL", fn);
+  if (wt->nranks < 1 || wt->nranks > MSQ_MAX_RANKS)
+    return fail(MSQ_E_INVALID, "%s: wait over %d ranks (1..%d)", fn, wt->nranks, MSQ_MAX_RANKS);
+  return MSQ_OK;
+}
+}  // namespace
+
+int msq_matmul_gather(void* cu_ctx, void* stream, msq_weights_t h, const void* d_a, int a_dtype, int64_t M,
+                      const msq_wait_t* wait, const msq_gather_t* gather) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  Weights* w = reinterpret_cast<Weights*>(h);
+  if (!w) return fail(MSQ_E_INVALID, "msq_matmul_gather: NULL weights handle");
+  if (!w->fast4) return fail(MSQ_E_UNSUPPORTED, "msq_matmul_gather needs bits=4 and a power-of-two block_size >= 32");
+  if (!is_float_act(a_dtype))
+    return fail(MSQ_E_INVALID, "MatMulNBits A must be Float32 or Float16; got %s.", dtype_name(a_dtype));
+  if (M < 1 || M > 4) return fail(MSQ_E_UNSUPPORTED, "msq_matmul_gather takes 1..4 A rows; got %lld", (long long)M);
+  if (!d_a || !gather) return fail(MSQ_E_INVALID, "msq_matmul_gather: NULL pointer");
+  if (gather->nranks < 1 || gather->nranks > MSQ_MAX_RANKS || gather->rank < 0 || gather->rank >= gather->nranks)
+    return fail(MSQ_E_INVALID, "msq_matmul_gather: rank %d of %d ranks", gather->rank, gather->nranks);
+  for (int r = 0; r < gather->nranks; ++r)
+    if (!gather->y[r] || !gather->arrivals[r])
+      return fail(MSQ_E_INVALID, "msq_matmul_gather: rank %d's buffer or counter is NULL", r);
+  if (!gather->done || !gather->produced) return fail(MSQ_E_INVALID, "msq_matmul_gather: NULL counter");
+  if (gather->col0 < 0 || gather->ldy < gather->col0 + w->n_rows)
+    return fail(MSQ_E_INVALID, "msq_matmul_gather: columns [%lld, %lld) do not fit a row of %lld",
+                (long long)gather->col0, (long long)(gather->col0 + w->n_rows), (long long)gather->ldy);
+  int rc = check_wait(wait, "msq_matmul_gather");
+  if (rc != MSQ_OK) return rc;
+  int dev;
+  rc = current_device(&dev);
+  if (rc != MSQ_OK) return rc;
+  if (dev != w->device)
+    return fail(MSQ_E_INVALID, "weights handle lives on device %d but the current device is %d", w->device, dev);
+  refresh_settled(*w, static_cast<cudaStream_t>(stream));
+  return run_gemv_gather(static_cast<cudaStream_t>(stream), *w, d_a, a_dtype, M, wait, gather);
+}
+
+int msq_wait_gathered(void* cu_ctx, void* stream, const msq_wait_t* wait) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  if (!wait) return fail(MSQ_E_INVALID, "msq_wait_gathered: NULL wait");
+  int rc = check_wait(wait, "msq_wait_gathered");
+  if (rc != MSQ_OK) return rc;
+  return run_wait_gathered(static_cast<cudaStream_t>(stream), wait);
 }
 
 int msq_qgemm_nbits(const float* a, const uint8_t* bq, const float* scales, const uint8_t* zero_points, float* y,

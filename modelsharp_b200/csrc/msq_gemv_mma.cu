@@ -54,7 +54,38 @@ struct Args {
   int a_vec;  // rows of A may be read 4 elements at a time
   int prefetch;  // weights settled: stream them before the programmatic-dependency wait
   int off_dig, off_s, off_ysum, off_bar, off_ring;  // shared-memory offsets (bytes)
+  // column-split exchange (the XG kernels): outputs to every rank's full-Y buffer
+  int nranks;
+  float* gy[MSQ_MAX_RANKS];
+  unsigned long long* garr[MSQ_MAX_RANKS];
+  int64_t gldy, gcol0;
+  unsigned long long* gprod;
+  unsigned int* gdone;
+  const unsigned long long* warr;  // gathered input to wait for (nullptr: none)
+  const unsigned long long* wprod;
+  int wranks;
 };
+
+constexpr int kErrTimeoutPeer = 5;  // waiting for other ranks' shards of a gathered input
+
+// Waits until every rank's shard of the latest gathered output has arrived on this rank:
+// arrivals >= produced * nranks (acquire at system scope). Bounded; false on timeout.
+__device__ __forceinline__ bool wait_arrivals(const unsigned long long* arr, const unsigned long long* prod,
+                                              int nranks) {
+  const unsigned long long target =
+      *reinterpret_cast<const volatile unsigned long long*>(prod) * (unsigned long long)nranks;
+  const unsigned long long t0 = ptx::globaltimer();
+  for (;;) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(arr) : "memory");
+    if (v >= target) return true;
+    if (ptx::globaltimer() - t0 > ptx::kWaitBudgetNs) {
+      atomicCAS(&g_mma_err, 0, kErrTimeoutPeer);
+      return false;
+    }
+    __nanosleep(64);
+  }
+}
 
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code) {
   if (*abort_flag) return false;
@@ -151,9 +182,11 @@ __device__ __forceinline__ int frexp_exponent(float x) {
 }
 __device__ __forceinline__ float exp2i(int s) { return __int_as_float((s + 127) << 23); }
 
-// BS = quantisation block size (32 / 64 / 128); NT = n8 tiles of B (1: M <= 2, 2: M <= 4).
-// A "unit" is max(BS, 64) k: one or two 64-k chunks (a uint4 of code words per lane each).
-template <int BS, int NT>
+// BS = quantisation block size (32 / 64 / 128); NT = n8 tiles of B (1: M <= 2, 2: M <= 4);
+// XG = the column-split form (outputs to every rank's full-Y buffer, optional wait for a
+// gathered input). A "unit" is max(BS, 64) k: one or two 64-k chunks (a uint4 of code words
+// per lane each).
+template <int BS, int NT, bool XG>
 __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
   constexpr int UNIT = BS > 64 ? BS : 64;
   constexpr int CH = UNIT / 64;     // 64-k chunks per unit
@@ -230,6 +263,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
   const int mc = p.mc;
   for (int i = tid; i < p.rows_cta * mc * kYPitch; i += kConsumers * 32) ysum[i] = 0.f;
   griddep_wait();  // A may come from the previous kernel, and Y may still be read by it
+  if constexpr (XG) {
+    if (p.warr) {  // a gathered input: every rank's shard of it must have arrived
+      if (tid == 0 && !wait_arrivals(p.warr, p.wprod, p.wranks)) *abort_flag = 1;
+      ptx::named_bar_sync(1, kConsumers * 32);
+    }
+  }
 
   // ---- activations: one pass. Loads in flight at once (float4, U deep); per quantisation
   // block (GL consecutive lanes) a shuffle max picks 2^sigma_b, the digits are written and a
@@ -452,14 +491,43 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
       const int r = o / mc, m = o - r * mc;
       const int b = blockIdx.x + (r >> 4) * grid;
       const int64_t row = (int64_t)b * 16 + (r & 15);
-      if (b < p.nblk && row < p.n_rows) p.y[(p.m0 + m) * p.ldy + row] = acc;
+      if (b < p.nblk && row < p.n_rows) {
+        if constexpr (XG) {
+          for (int r = 0; r < p.nranks; ++r) p.gy[r][(p.m0 + m) * p.gldy + p.gcol0 + row] = acc;
+        } else {
+          p.y[(p.m0 + m) * p.ldy + row] = acc;
+        }
+      }
+    }
+  }
+  if constexpr (XG) {
+    // The CTA's stores are ordered before its completion count by the barrier and a GPU-scope
+    // acquire-release count; the last CTA, having acquired every CTA's count, fences at system
+    // scope (cumulative over all those stores) and releases one arrival to every rank.
+    ptx::named_bar_sync(1, kConsumers * 32);
+    if (tid == 0) {
+      unsigned int prev;
+      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(p.gdone) : "memory");
+      if (prev == gridDim.x - 1) {
+        asm volatile("fence.sc.sys;" ::: "memory");
+        *p.gdone = 0u;  // the next launch of this layer is stream-ordered after this one
+        atomicAdd(p.gprod, 1ull);
+        for (int r = 0; r < p.nranks; ++r)
+          asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(p.garr[r]) : "memory");
+      }
     }
   }
 }
 
-template <int BS, int NT>
+// One thread: waits like a consuming launch for the latest gathered output.
+__global__ void wait_gathered_kernel(const unsigned long long* arr, const unsigned long long* prod, int nranks) {
+  griddep_wait();
+  if (threadIdx.x == 0) wait_arrivals(arr, prod, nranks);
+}
+
+template <int BS, int NT, bool XG>
 int launch(cudaStream_t st, const Args& a, int grid, size_t smem) {
-  auto kern = gemv_mma_kernel<BS, NT>;
+  auto kern = gemv_mma_kernel<BS, NT, XG>;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -507,15 +575,19 @@ size_t plan_smem(const Weights& w, int mc, int grid, Args& a) {
   return (size_t)a.off_ring + (size_t)slots * w.stage_bytes;
 }
 
-template <int BS>
+template <int BS, bool XG>
 int launch_nt(cudaStream_t st, const Args& a, int grid, size_t smem) {
-  return a.mc <= 2 ? launch<BS, 1>(st, a, grid, smem) : launch<BS, 2>(st, a, grid, smem);
+  return a.mc <= 2 ? launch<BS, 1, XG>(st, a, grid, smem) : launch<BS, 2, XG>(st, a, grid, smem);
 }
 
 }  // namespace
 
-int run_gemv_mma(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M, float* d_y,
-                 int64_t ldy) {
+namespace {
+
+// One decode GEMV call: passes of up to 4 A rows; with `g` (column split) a single pass
+// whose outputs go to every rank's full-Y buffer, after waiting for `wt` (or nothing).
+int gemv_impl(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M, float* d_y,
+              int64_t ldy, const msq_wait_t* wt, const msq_gather_t* g) {
   if (!w.strm || (w.block_size != 32 && w.block_size != 64 && w.block_size != 128)) return MSQ_E_UNSUPPORTED;
   const int unit = w.block_size > 64 ? w.block_size : 64;
   if (w.kt / unit > kUpw * kConsumers) return MSQ_E_UNSUPPORTED;
@@ -546,6 +618,22 @@ int run_gemv_mma(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype
       const int align = a_dtype == MSQ_DT_F32 ? 16 : 8;
       a.a_vec = (w.K % 4 == 0) && (ap % align == 0);
     }
+    if (g) {
+      a.nranks = g->nranks;
+      for (int r = 0; r < g->nranks; ++r) {
+        a.gy[r] = g->y[r];
+        a.garr[r] = g->arrivals[r];
+      }
+      a.gldy = g->ldy;
+      a.gcol0 = g->col0;
+      a.gprod = g->produced;
+      a.gdone = g->done;
+      if (wt) {
+        a.warr = wt->arrivals;
+        a.wprod = wt->produced;
+        a.wranks = wt->nranks;
+      }
+    }
     // the widest pass whose digits, row sums and ring fit in shared memory
     int mc = (int)std::min<int64_t>(kMaxM, M - m0);
     int grid = std::min(w.nblk, sms);
@@ -562,17 +650,45 @@ int run_gemv_mma(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype
         return MSQ_E_UNSUPPORTED;
       }
     }
+    if (g && mc < M) return fail(MSQ_E_UNSUPPORTED, "msq_matmul_gather: %lld A rows do not fit one pass", (long long)M);
     a.mc = mc;
     int rc;
-    switch (w.block_size) {
-      case 32: rc = launch_nt<32>(st, a, grid, smem); break;
-      case 64: rc = launch_nt<64>(st, a, grid, smem); break;
-      default: rc = launch_nt<128>(st, a, grid, smem); break;
+    if (g) {
+      switch (w.block_size) {
+        case 32: rc = launch_nt<32, true>(st, a, grid, smem); break;
+        case 64: rc = launch_nt<64, true>(st, a, grid, smem); break;
+        default: rc = launch_nt<128, true>(st, a, grid, smem); break;
+      }
+    } else {
+      switch (w.block_size) {
+        case 32: rc = launch_nt<32, false>(st, a, grid, smem); break;
+        case 64: rc = launch_nt<64, false>(st, a, grid, smem); break;
+        default: rc = launch_nt<128, false>(st, a, grid, smem); break;
+      }
     }
     if (rc != MSQ_OK) return rc;
     m0 += mc;
   }
-  note_path(M <= 4 ? "gemv_imma" : "gemv_imma_multipass");
+  note_path(g ? "gemv_imma_gather" : M <= 4 ? "gemv_imma" : "gemv_imma_multipass");
+  return MSQ_OK;
+}
+
+}  // namespace
+
+int run_gemv_mma(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M, float* d_y,
+                 int64_t ldy) {
+  return gemv_impl(st, w, d_a, a_dtype, M, d_y, ldy, nullptr, nullptr);
+}
+
+int run_gemv_gather(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M,
+                    const msq_wait_t* wt, const msq_gather_t* g) {
+  return gemv_impl(st, w, d_a, a_dtype, M, nullptr, 0, wt, g);
+}
+
+int run_wait_gathered(cudaStream_t st, const msq_wait_t* wt) {
+  wait_gathered_kernel<<<1, 32, 0, st>>>(wt->arrivals, wt->produced, wt->nranks);
+  note_launch();
+  MSQ_CUDA_TRY(cudaGetLastError(), "wait kernel launch");
   return MSQ_OK;
 }
 

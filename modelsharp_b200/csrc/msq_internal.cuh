@@ -100,6 +100,10 @@ int run_gemv(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, in
              float* d_y, int64_t ldy);
 int run_gemv_mma(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M,
                  float* d_y, int64_t ldy);
+// The column-split decode GEMV (outputs to every rank's full-Y buffer) and the wait kernel.
+int run_gemv_gather(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M,
+                    const msq_wait_t* wt, const msq_gather_t* g);
+int run_wait_gathered(cudaStream_t st, const msq_wait_t* wt);
 int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t M,
              float* d_y, int64_t ldy);
 void release_gemm_state(Weights& w);

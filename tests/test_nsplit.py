@@ -93,3 +93,71 @@ def test_nsplit_one_rank_cuda_matches_unsplit(cuda_device):
     assert torch.equal(y, ref)
     sh.free()
     full.free()
+
+
+def _p2p_chain_check(dev, rank=0, world=1):
+    """Up-proj then down-proj through the p2p gather, eager and as CUDA-graph replays with new
+    inputs, against the unsplit kernel on the same device (bit-exact: same kernel per row)."""
+    from modelsharp_b200 import QuantizedWeights
+    up_c = synth.make_case(71, 2, 1024, 512, 4, 128, "packed", scale_lo=0.001, scale_hi=0.01)
+    dn_c = synth.make_case(72, 2, 640, 1024, 4, 32, "none", scale_lo=0.001, scale_hi=0.01)
+    up = ShardedMatMulNBits(up_c["b"], up_c["scales"], up_c["zp"], 1024, 512, 4, 128, device=dev, gather="p2p")
+    dn = ShardedMatMulNBits(dn_c["b"], dn_c["scales"], dn_c["zp"], 640, 1024, 4, 32, device=dev, gather="p2p")
+    up_full = QuantizedWeights(up_c["b"], up_c["scales"], up_c["zp"], 1024, 512, 4, 128, device=dev)
+    dn_full = QuantizedWeights(dn_c["b"], dn_c["scales"], dn_c["zp"], 640, 1024, 4, 32, device=dev)
+    gen = torch.Generator().manual_seed(5)
+    a = torch.randn(2, 512, generator=gen).to(dev)
+
+    def chain():
+        return dn(up(a), wait=up.out_wait)
+
+    def reference():
+        return dn_full.matmul(up_full.matmul(a))
+
+    for _ in range(3):  # eager, both buffer parities
+        y = chain()
+        dn.wait_gathered()
+        assert torch.equal(y, reference())
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            y_g = chain()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    for _ in range(4):  # replays: the device counters keep every rank in step
+        a.copy_(torch.randn(2, 512, generator=gen).to(dev))
+        g.replay()
+        dn.wait_gathered()
+        assert torch.equal(y_g, reference())
+    torch.cuda.synchronize(dev)
+    from modelsharp_b200 import _native as NAT
+    assert NAT.lib().msq_device_status(None, None) == NAT.MSQ_OK, NAT.last_error()
+    del g
+    for x in (up, dn, up_full, dn_full):
+        x.free()
+
+
+@pytest.mark.gpu
+def test_nsplit_p2p_one_rank(cuda_device):
+    _p2p_chain_check(cuda_device)
+
+
+def _p2p_worker(rank: int, world: int, port: int):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    import datetime
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        _p2p_chain_check(torch.device("cuda", rank), rank, world)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_nsplit_p2p_two_ranks(cuda_device):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mp.start_processes(_p2p_worker, args=(2, _free_port()), nprocs=2, join=True, start_method="spawn")
