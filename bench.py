@@ -519,6 +519,180 @@ def run_nsplit(args, rank: int, world: int, local_rank: int):
             sh.free()
 
 
+# ---------------------------------------------------------------- prefill GEMM workload
+PREFILL_MS = (512, 2048, 8192)
+PREFILL_K, PREFILL_N, PREFILL_BS = 4096, 14336, 32
+PREFILL_WORKLOAD = ("prefill tensor-core GEMM (BASELINE configs[2]): M in {512, 2048, 8192}, K=4096, N=14336, "
+                    "bits=4, block_size=32, packed zero points, fp16 A ~N(0,1), fp16 scales U[0.001, 0.01]")
+
+
+def run_prefill(args, rank: int, world: int, local_rank: int):
+    """One step = the three GEMMs (one CUDA graph); value = 2*M*N*K summed over the three / step
+    time. Weight replicas rotate so weights + activations exceed L2 every step."""
+    import torch
+    import torch.distributed as dist
+
+    from modelsharp_b200 import QuantizedWeights, synth
+    from modelsharp_b200 import _native as N
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    lib = N.lib()
+    cases = [synth.make_case(200 + i, m, PREFILL_N, PREFILL_K, 4, PREFILL_BS, "packed", a_dtype="f16",
+                             scale_dtype="f16", scale_lo=SCALE_LO, scale_hi=SCALE_HI) for i, m in enumerate(PREFILL_MS)]
+    flops = sum(2.0 * m * PREFILL_N * PREFILL_K for m in PREFILL_MS)
+    reps_n = 4
+    wb = cases[0]
+    reps = [QuantizedWeights(wb["b"], wb["scales"], wb["zp"], PREFILL_N, PREFILL_K, 4, PREFILL_BS, device=dev)
+            for _ in range(reps_n)]
+    a_dev = [torch.from_numpy(c["a"]).to(dev) for c in cases]
+    y_dev = [torch.empty(c["M"], PREFILL_N, device=dev) for c in cases]
+    stream = torch.cuda.Stream(dev)
+    sptr = stream.cuda_stream
+
+    def launch_step(r: int):
+        for a, y in zip(a_dev, y_dev):
+            rc = lib.msq_matmul_ex(None, sptr, reps[r].handle, a.data_ptr(), N.DT_F16, a.shape[0], y.data_ptr(),
+                                   PREFILL_N, N.PATH_GEMM)
+            if rc:
+                N.check(rc)
+
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            launch_step(i % reps_n)
+    stream.synchronize()
+    path = N.last_path()
+    before = N.launch_count()
+    graphs = []
+    for r in range(reps_n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            launch_step(r)
+        graphs.append(g)
+    launches_per_step = (N.launch_count() - before) // reps_n
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            graphs[i % reps_n].replay()
+    stream.synchronize()
+    # per-M duration: one graph per M of reps_n launches
+    per_m = []
+    for mi, (a, y) in enumerate(zip(a_dev, y_dev)):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for r in range(reps_n):
+                lib.msq_matmul_ex(None, sptr, reps[r].handle, a.data_ptr(), N.DT_F16, a.shape[0], y.data_ptr(),
+                                  PREFILL_N, N.PATH_GEMM)
+        with torch.cuda.stream(stream):
+            g.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            nrep = 5
+            for _ in range(nrep):
+                g.replay()
+            e1.record(stream)
+        stream.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (nrep * reps_n)
+        per_m.append({"M": PREFILL_MS[mi], "us": us, "TFLOP/s": 2.0 * PREFILL_MS[mi] * PREFILL_N * PREFILL_K / us / 1e6})
+        del g
+
+    dist.barrier() if world > 1 else None
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        ev0.record(stream)
+        with torch.cuda.stream(stream):
+            for i in range(args.steps):
+                graphs[i % reps_n].replay()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    dist.barrier() if world > 1 else None
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * flops * args.steps / (ms * 1e-3) / 1e12
+
+    # e2e: host A in (fp16), Y out (fp32) through msq_matmul_host, every step
+    a_host = [torch.from_numpy(c["a"]).pin_memory() for c in cases]
+    y_host = [torch.empty(c["M"], PREFILL_N).pin_memory() for c in cases]
+    e2e_steps = max(1, min(args.steps, 5))
+
+    def e2e_step(r: int):
+        for a, y in zip(a_host, y_host):
+            rc = lib.msq_matmul_host(None, sptr, reps[r].handle, a.data_ptr(), N.DT_F16, a.shape[0], y.data_ptr())
+            if rc:
+                N.check(rc)
+
+    e2e_step(0)
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(e2e_steps):
+        e2e_step(i % reps_n)
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = t0.elapsed_time(t1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = world * flops * e2e_steps / (e2e_ms * 1e-3) / 1e12
+
+    if rank == 0:
+        from oracle import oracle
+        par = []
+        for c, y in zip(cases, y_dev):
+            m = c["M"]
+            rows = [slice(0, 16), slice(m // 2, m // 2 + 16), slice(m - 16, m)]
+            yy = y.cpu().numpy()
+            cw = dict(wb, a=c["a"], M=m)  # every GEMM runs on the first case's weights
+            par.append(oracle.rel_l2(np.concatenate([yy[r] for r in rows]),
+                                     np.concatenate([oracle.managed(cw, rows=r) for r in rows])))
+        pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+        peak = float(pk.get("bf16_tflops_sustained", 1400.0))
+        cpu = None
+        if world == 1:
+            c = cases[0]
+            sample = dict(c, a=c["a"][:64].astype(np.float32), M=64)
+            fn = oracle.reference_native if oracle.reference_available() else oracle.managed
+            fn(sample)
+            t_0 = time.perf_counter()
+            n = 0
+            while time.perf_counter() - t_0 < max(args.cpu_seconds, 0.1) or n < 1:
+                fn(sample)
+                n += 1
+            dt = (time.perf_counter() - t_0) / n
+            cpu = {"value": 2.0 * 64 * PREFILL_N * PREFILL_K / dt / 1e12, "unit": "TFLOP/s", "cores": os.cpu_count(),
+                   "kind": "reference" if oracle.reference_available() else "port",
+                   "sample": f"{n} calls of M=64 rows of the M=512 case (fp16 widened to fp32), mean, all host threads"}
+        out = {
+            "metric": "MatMulNBits INT4 prefill TFLOPS", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16 operands, f32 accumulate", "data": "synthetic",
+            "config": {"workload": PREFILL_WORKLOAD, "flops_per_step": flops, "parallelism": f"replicas{world}",
+                       "l2": f"{reps_n} weight replicas rotate; A up to {8192 * PREFILL_K * 2 / 1e6:.0f} MB",
+                       "launch": "one CUDA graph replay per step", "kernel_path": path,
+                       "parity_rel_l2_sampled_rows": max(par)},
+            "roofline": {"bound": "tensor", "achieved": value / world, "peak": peak, "unit": "TFLOP/s",
+                         "frac": value / world / peak, "traffic": None,
+                         "peak_source": "measured cuBLAS bf16, sustained" if pk else "fallback",
+                         "per_M": per_m},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": sum(a.numel() * 2 for a in a_host),
+                    "d2h_bytes_per_step": sum(y.numel() * 4 for y in y_host), "steps": e2e_steps,
+                    "entry": "msq_matmul_host"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(out), flush=True)
+    graphs.clear()
+    for w in reps:
+        w.free()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -526,7 +700,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--workload", default="sweep7b", choices=["sweep7b", "nsplit70b"])
+    ap.add_argument("--workload", default="sweep7b", choices=["sweep7b", "nsplit70b", "prefill"])
     ap.add_argument("--m", type=int, default=1, help="A rows for the nsplit70b workload")
     ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
                     help="nsplit70b: fused peer-store gather (M <= 4) or NCCL all-gather")
@@ -557,6 +731,8 @@ def main():
     try:
         if args.workload == "nsplit70b":
             run_nsplit(args, rank, world, local_rank)
+        elif args.workload == "prefill":
+            run_prefill(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)
     finally:

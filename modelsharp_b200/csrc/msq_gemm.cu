@@ -4,14 +4,18 @@
 //
 // One CTA computes a BM x BN tile of Y (BM = 128 activation rows = TMEM lanes, BN = 128 or
 // 256 weight rows = TMEM columns) over k-stages of 64:
-//   warp 8      TMA producer: the fp16 activation tile (128 x 64, 128-byte swizzle) and the
-//               packed int4 weight tile (BN rows x 32 bytes) of each stage, no multicast;
-//   warps 0..7  dequantise the packed tile into fp16 (q - zp) * s, written straight into the
-//               K-major 128-byte-swizzled layout the tensor core reads, then release the stage;
-//   warp 9      allocates TMEM and, from one lane, issues 4 x tcgen05.mma (M=128, N=BN, K=16)
+//   TMA warp    per stage: the fp16 activation tile (128 x 64, 128-byte swizzle), the packed
+//               int4 weight tile (BN rows x 32 bytes) and a 16-byte column of scales and of
+//               zero points per weight row covering the stage's blocks, no multicast;
+//   dequant     one thread per half row (32 codes, one block at block_size 32): reads its
+//   warps       16 bytes of codes and its scale / zero point from shared memory, writes fp16
+//               (q - zp) * s straight into the K-major 128-byte-swizzled layout the tensor
+//               core reads, then releases the stage;
+//   MMA warp    allocates TMEM and, from one lane, issues 4 x tcgen05.mma (M=128, N=BN, K=16)
 //               per stage with the fp32 accumulator in TMEM, committing each stage back to
 //               the producer;
-//   warps 0..7  finally read the accumulator with tcgen05.ld and store fp32 Y.
+//   dequant     finally read the accumulator with tcgen05.ld and store fp32 Y.
+//   warps
 // The dequantised operand is exact up to one fp16 rounding of (q - zp) * s; products and
 // sums are fp32 in the tensor core (parity bar: rel-L2 <= 5e-3 against the fp32 reference).
 // fp32 / bf16 activations are converted to fp16 into a stream-ordered scratch buffer first.
@@ -28,23 +32,27 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kDeqWarps = 8;
-constexpr int kThreads = (kDeqWarps + 2) * 32;  // + TMA warp + MMA warp
-constexpr int kTmaWarp = kDeqWarps;
-constexpr int kMmaWarp = kDeqWarps + 1;
 
 __device__ int g_gemm_err;
 
 template <int BN>
 struct Plan {
+  static constexpr int kDeq = BN / 16;                // dequant warps: one thread per half row
+  static constexpr int kThreads = (kDeq + 2) * 32;    // + TMA warp + MMA warp
+  static constexpr int kTmaWarp = kDeq;
+  static constexpr int kMmaWarp = kDeq + 1;
   static constexpr int kStages = BN == 256 ? 3 : 4;
   static constexpr int kABytes = BM * BK * 2;         // 16 KB
   static constexpr int kBBytes = BN * BK * 2;         // dequantised fp16 weights
   static constexpr int kPBytes = BN * BK / 2;         // packed int4 weights
+  static constexpr int kSBytes = BN * 16;             // 8 fp16 scales per row
+  static constexpr int kZBytes = BN * 16;             // 32 packed or 4 fp32 zero points per row
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kOffA + kStages * kABytes;
   static constexpr int kOffP = kOffB + kStages * kBBytes;
-  static constexpr int kOffBar = kOffP + kStages * kPBytes;
+  static constexpr int kOffS = kOffP + kStages * kPBytes;
+  static constexpr int kOffZ = kOffS + kStages * kSBytes;
+  static constexpr int kOffBar = kOffZ + kStages * kZBytes;
   static constexpr int kBarBytes = (3 * kStages + 1) * 8 + 16;
   static constexpr int kSmem = kOffBar + kBarBytes + 1024;  // + alignment slack
 };
@@ -53,12 +61,6 @@ struct GemmArgs {
   float* y;
   int64_t ldy;
   int M, n_rows, K, ksteps;
-  const float* unused;
-  const __half* sc16;
-  int64_t sc_pitch;
-  const uint8_t* zp4;
-  int64_t zp_pitch;
-  const float* zpf;
   int bs_shift;
   int vec_store;
 };
@@ -100,11 +102,15 @@ __device__ __forceinline__ uint32_t deq_pair_f32(uint32_t bits, float z, float s
 }
 
 template <int BN, int ZPK>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Plan<BN>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmP,
+                   const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmZ,
                    const GemmArgs p) {
   using PL = Plan<BN>;
   constexpr int S = PL::kStages;
+  constexpr int kDeqWarps = PL::kDeq;
+  constexpr int kTmaWarp = PL::kTmaWarp;
+  constexpr int kMmaWarp = PL::kMmaWarp;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -135,6 +141,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kTmaWarp && lane == 0) {
     ptx::prefetch_tmap(&tmA);
     ptx::prefetch_tmap(&tmP);
+    ptx::prefetch_tmap(&tmS);
+    if (ZPK != ZP_NONE) ptx::prefetch_tmap(&tmZ);
   }
   ptx::tc_fence_before();
   __syncthreads();
@@ -148,9 +156,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = kt % S;
         const uint32_t u = kt / S;
         if (kt >= S && !wait_abort(&empty[s], (u - 1) & 1, abort_flag, ptx::kErrTimeoutEmpty)) break;
-        ptx::mbar_arrive_expect_tx(&full[s], PL::kABytes + PL::kPBytes);
+        // scales / zero points: the 16-byte-aligned column holding the stage's block(s)
+        const int blk0 = (kt * BK) >> p.bs_shift;
+        ptx::mbar_arrive_expect_tx(&full[s],
+                                   PL::kABytes + PL::kPBytes + PL::kSBytes + (ZPK != ZP_NONE ? PL::kZBytes : 0));
         ptx::tma_load_2d(smem + PL::kOffA + s * PL::kABytes, &tmA, &full[s], kt * BK, m0);
         ptx::tma_load_2d(smem + PL::kOffP + s * PL::kPBytes, &tmP, &full[s], kt * (BK / 2), n0);
+        ptx::tma_load_2d(smem + PL::kOffS + s * PL::kSBytes, &tmS, &full[s], blk0 & ~7, n0);
+        if (ZPK == ZP_PACKED)
+          ptx::tma_load_2d(smem + PL::kOffZ + s * PL::kZBytes, &tmZ, &full[s], (blk0 >> 1) & ~15, n0);
+        else if (ZPK == ZP_F32)
+          ptx::tma_load_2d(smem + PL::kOffZ + s * PL::kZBytes, &tmZ, &full[s], blk0 & ~3, n0);
         ++issued;
       }
       for (int s = 0; s < S && s < issued; ++s) {  // drain copies in flight
@@ -193,59 +209,50 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- dequantisation warps 0..7
-    const int tid = threadIdx.x;                 // 0..255
+    // ---------------- dequantisation warps: thread t takes half row t (codes 16t..16t+15 of
+    // the packed tile: row t/2, k 32(t%2)..+31), so a warp's code loads are one contiguous
+    // 512-byte run and its swizzled stores hit every bank group once per 128 bytes
+    const int tid = threadIdx.x;  // 0 .. 2*BN-1
+    const int r = tid >> 1, c = tid & 1;
+    uint8_t* brow_base = smem + PL::kOffB + (r >> 3) * 1024 + (r & 7) * 128;
     for (int kt = 0; kt < p.ksteps; ++kt) {
       const int s = kt % S;
       const uint32_t u = kt / S;
       const bool ok = wait_abort(&full[s], u & 1, abort_flag, ptx::kErrTimeoutFull);
       if (ok) {
-        const uint8_t* ptile = smem + PL::kOffP + s * PL::kPBytes;
-        uint8_t* btile = smem + PL::kOffB + s * PL::kBBytes;
-        for (int r = tid; r < BN; r += kDeqWarps * 32) {
-          const int n = n0 + r;
-          const bool valid = n < p.n_rows;
-          const uint4 w0 = *reinterpret_cast<const uint4*>(ptile + r * 32);
-          const uint4 w1 = *reinterpret_cast<const uint4*>(ptile + r * 32 + 16);
-          const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-          // the stage's block(s): one block for bs >= 64, two (words 0-3 / 4-7) for bs = 32
-          const int blk0 = (kt * BK) >> p.bs_shift;
-          const int blk1 = (kt * BK + 32) >> p.bs_shift;
-          float s0 = 0.f, s1 = 0.f, z0 = 8.f, z1 = 8.f;
-          if (valid) {
-            s0 = __half2float(p.sc16[(int64_t)n * p.sc_pitch + blk0]);
-            s1 = __half2float(p.sc16[(int64_t)n * p.sc_pitch + blk1]);
-            if (ZPK == ZP_PACKED) {
-              const uint8_t* zr = p.zp4 + (int64_t)n * p.zp_pitch;
-              z0 = (float)((zr[blk0 >> 1] >> ((blk0 & 1) * 4)) & 0xF);
-              z1 = (float)((zr[blk1 >> 1] >> ((blk1 & 1) * 4)) & 0xF);
-            } else if (ZPK == ZP_F32) {
-              z0 = p.zpf[(int64_t)n * p.sc_pitch + blk0];
-              z1 = p.zpf[(int64_t)n * p.sc_pitch + blk1];
-            }
-          }
-          uint8_t* brow = btile + (r >> 3) * 1024 + (r & 7) * 128;
+        const uint4 w4 = *reinterpret_cast<const uint4*>(smem + PL::kOffP + s * PL::kPBytes + tid * 16);
+        const int blk0 = (kt * BK) >> p.bs_shift;
+        const int blk = (kt * BK + c * 32) >> p.bs_shift;
+        const float sf = __half2float(
+            reinterpret_cast<const __half*>(smem + PL::kOffS + s * PL::kSBytes + r * 16)[blk - (blk0 & ~7)]);
+        float zf = 8.f;
+        if (ZPK == ZP_PACKED) {
+          const uint8_t zb = (smem + PL::kOffZ + s * PL::kZBytes + r * 16)[(blk >> 1) - ((blk0 >> 1) & ~15)];
+          zf = (float)((zb >> ((blk & 1) * 4)) & 0xF);
+        } else if (ZPK == ZP_F32) {
+          zf = reinterpret_cast<const float*>(smem + PL::kOffZ + s * PL::kZBytes + r * 16)[blk - (blk0 & ~3)];
+        }
+        uint8_t* brow = brow_base + s * PL::kBBytes;
+        const uint32_t words[4] = {w4.x, w4.y, w4.z, w4.w};
+        const __half2 zc = __float2half2_rn(1024.f + zf);
+        const __half2 s2 = __float2half2_rn(sf);
 #pragma unroll
-          for (int wi = 0; wi < 8; ++wi) {
-            const uint32_t x = words[wi];
-            const float sf = wi < 4 ? s0 : s1;
-            const float zf = wi < 4 ? z0 : z1;
-            uint4 o;
-            if (ZPK == ZP_F32) {
-              o.x = deq_pair_f32(x, zf, sf);
-              o.y = deq_pair_f32(x >> 4, zf, sf);
-              o.z = deq_pair_f32(x >> 8, zf, sf);
-              o.w = deq_pair_f32(x >> 12, zf, sf);
-            } else {
-              const __half2 zc = __float2half2_rn(1024.f + zf);
-              const __half2 s2 = __float2half2_rn(sf);
-              o.x = deq_pair(x, zc, s2);
-              o.y = deq_pair(x >> 4, zc, s2);
-              o.z = deq_pair(x >> 8, zc, s2);
-              o.w = deq_pair(x >> 12, zc, s2);
-            }
-            *reinterpret_cast<uint4*>(brow + ((wi ^ (r & 7)) << 4)) = o;
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t x = words[j];
+          uint4 o;
+          if (ZPK == ZP_F32) {
+            o.x = deq_pair_f32(x, zf, sf);
+            o.y = deq_pair_f32(x >> 4, zf, sf);
+            o.z = deq_pair_f32(x >> 8, zf, sf);
+            o.w = deq_pair_f32(x >> 12, zf, sf);
+          } else {
+            o.x = deq_pair(x, zc, s2);
+            o.y = deq_pair(x >> 4, zc, s2);
+            o.z = deq_pair(x >> 8, zc, s2);
+            o.w = deq_pair(x >> 12, zc, s2);
           }
+          const int wi = 4 * c + j;  // 8-k group of the row
+          *reinterpret_cast<uint4*>(brow + ((wi ^ (r & 7)) << 4)) = o;
         }
       }
       ptx::fence_proxy_async_smem();
@@ -259,12 +266,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::tc_fence_after();
     if (ok) {
       const int q = warp & 3;                 // TMEM lane quarter of this warp
-      const int half = warp >> 2;             // column half
+      const int cg = warp >> 2;               // column group
       const int m = m0 + q * 32 + lane;
-      constexpr int kCols = BN / 2;
+      constexpr int kCols = BN / (kDeqWarps / 4);
 #pragma unroll 1
-      for (int c = 0; c < kCols; c += 32) {
-        const int col = half * kCols + c;
+      for (int cc = 0; cc < kCols; cc += 32) {
+        const int col = cg * kCols + cc;
         uint32_t v[32];
         ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)col, v);
         ptx::tmem_ld_wait();
@@ -338,12 +345,17 @@ int make_map_2d(CUtensorMap* map, CUtensorMapDataType dt, void* base, uint64_t i
   return MSQ_OK;
 }
 
+// Tensor maps of one weight handle for one tile width: packed codes, scales, zero points.
+struct WeightMaps {
+  CUtensorMap p, s, z;
+};
+
 struct GemmState {
-  CUtensorMap tmP128, tmP256;
+  WeightMaps m128, m256;
 };
 
 template <int BN, int ZPK>
-int launch(cudaStream_t st, const CUtensorMap& tmA, const CUtensorMap& tmP, const GemmArgs& a, dim3 grid) {
+int launch(cudaStream_t st, const CUtensorMap& tmA, const WeightMaps& wm, const GemmArgs& a, dim3 grid) {
   auto kern = gemm_tc_kernel<BN, ZPK>;
   static bool configured[64] = {false};
   int dev = 0;
@@ -353,19 +365,19 @@ int launch(cudaStream_t st, const CUtensorMap& tmA, const CUtensorMap& tmP, cons
                  "gemm smem attribute");
     configured[dev] = true;
   }
-  kern<<<grid, kThreads, Plan<BN>::kSmem, st>>>(tmA, tmP, a);
+  kern<<<grid, Plan<BN>::kThreads, Plan<BN>::kSmem, st>>>(tmA, wm.p, wm.s, wm.z, a);
   note_launch();
   MSQ_CUDA_TRY(cudaGetLastError(), "gemm launch");
   return MSQ_OK;
 }
 
 template <int BN>
-int launch_zp(cudaStream_t st, int zp_kind, const CUtensorMap& tmA, const CUtensorMap& tmP, const GemmArgs& a,
+int launch_zp(cudaStream_t st, int zp_kind, const CUtensorMap& tmA, const WeightMaps& wm, const GemmArgs& a,
               dim3 grid) {
   switch (zp_kind) {
-    case ZP_PACKED: return launch<BN, ZP_PACKED>(st, tmA, tmP, a, grid);
-    case ZP_F32: return launch<BN, ZP_F32>(st, tmA, tmP, a, grid);
-    default: return launch<BN, ZP_NONE>(st, tmA, tmP, a, grid);
+    case ZP_PACKED: return launch<BN, ZP_PACKED>(st, tmA, wm, a, grid);
+    case ZP_F32: return launch<BN, ZP_F32>(st, tmA, wm, a, grid);
+    default: return launch<BN, ZP_NONE>(st, tmA, wm, a, grid);
   }
 }
 
@@ -374,7 +386,7 @@ int launch_zp(cudaStream_t st, int zp_kind, const CUtensorMap& tmA, const CUtens
 namespace {
 
 // Builds the activation map over fp16 rows of stride lda and launches the tile kernel.
-int launch_gemm(cudaStream_t st, const Weights& w, const CUtensorMap& tmP128, const CUtensorMap& tmP256,
+int launch_gemm(cudaStream_t st, const Weights& w, const WeightMaps& m128, const WeightMaps& m256,
                 const void* a16, int64_t lda, int64_t M, float* d_y, int64_t ldy) {
   CUtensorMap tmA;
   int rc = make_map_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, const_cast<void*>(a16), (uint64_t)w.K, (uint64_t)M,
@@ -387,11 +399,6 @@ int launch_gemm(cudaStream_t st, const Weights& w, const CUtensorMap& tmP128, co
   g.n_rows = w.n_rows;
   g.K = w.K;
   g.ksteps = (w.K + BK - 1) / BK;
-  g.sc16 = w.sc16;
-  g.sc_pitch = w.sc_pitch;
-  g.zp4 = w.zp4;
-  g.zp_pitch = w.zp_pitch;
-  g.zpf = w.zpf;
   int sh = 0;
   while ((1 << sh) < w.block_size) ++sh;
   g.bs_shift = sh;
@@ -400,21 +407,36 @@ int launch_gemm(cudaStream_t st, const Weights& w, const CUtensorMap& tmP128, co
   const int64_t tiles256 = (w.n_rows + 255) / 256 * mt;
   const bool big = tiles256 >= 2 * num_sms(w.device);
   if (big) {
-    rc = launch_zp<256>(st, w.zp_kind, tmA, tmP256, g, dim3((w.n_rows + 255) / 256, (unsigned)mt));
+    rc = launch_zp<256>(st, w.zp_kind, tmA, m256, g, dim3((w.n_rows + 255) / 256, (unsigned)mt));
   } else {
-    rc = launch_zp<128>(st, w.zp_kind, tmA, tmP128, g, dim3((w.n_rows + 127) / 128, (unsigned)mt));
+    rc = launch_zp<128>(st, w.zp_kind, tmA, m128, g, dim3((w.n_rows + 127) / 128, (unsigned)mt));
   }
   if (rc == MSQ_OK) note_path(big ? "gemm_tc_n256" : "gemm_tc_n128");
   return rc;
 }
 
-int make_weight_maps(const Weights& w, CUtensorMap* tmP128, CUtensorMap* tmP256) {
-  int rc = make_map_2d(tmP128, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.nib, (uint64_t)w.nib_pitch, (uint64_t)w.n_rows,
-                       (uint64_t)w.nib_pitch, BK / 2, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+// Codes [n_rows][KP/2] in boxes of 32 bytes x BN rows; scales [n_rows][sc_pitch] fp16 and zero
+// points (packed [n_rows][zp_pitch] bytes or fp32 [n_rows][sc_pitch]) in 16-byte x BN boxes.
+int make_maps(const Weights& w, int bn, WeightMaps* m) {
+  int rc = make_map_2d(&m->p, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.nib, (uint64_t)w.nib_pitch, (uint64_t)w.n_rows,
+                       (uint64_t)w.nib_pitch, BK / 2, bn, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc == MSQ_OK)
-    rc = make_map_2d(tmP256, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.nib, (uint64_t)w.nib_pitch, (uint64_t)w.n_rows,
-                     (uint64_t)w.nib_pitch, BK / 2, 256, CU_TENSOR_MAP_SWIZZLE_NONE);
-  return rc;
+    rc = make_map_2d(&m->s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, w.sc16, (uint64_t)w.sc_pitch, (uint64_t)w.n_rows,
+                     (uint64_t)w.sc_pitch * 2, 8, bn, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc != MSQ_OK) return rc;
+  if (w.zp_kind == ZP_PACKED)
+    return make_map_2d(&m->z, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.zp4, (uint64_t)w.zp_pitch, (uint64_t)w.n_rows,
+                       (uint64_t)w.zp_pitch, 16, bn, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (w.zp_kind == ZP_F32)
+    return make_map_2d(&m->z, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w.zpf, (uint64_t)w.sc_pitch, (uint64_t)w.n_rows,
+                       (uint64_t)w.sc_pitch * 4, 4, bn, CU_TENSOR_MAP_SWIZZLE_NONE);
+  m->z = m->s;  // not read without zero points
+  return MSQ_OK;
+}
+
+int make_weight_maps(const Weights& w, WeightMaps* m128, WeightMaps* m256) {
+  const int rc = make_maps(w, 128, m128);
+  return rc == MSQ_OK ? make_maps(w, 256, m256) : rc;
 }
 
 // fp16 activations with 16-byte rows feed TMA directly; anything else is staged as fp16.
@@ -433,7 +455,7 @@ int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t 
   GemmState* gs = static_cast<GemmState*>(w.gemm_state);
   if (!gs) {
     gs = new GemmState();
-    int rc = make_weight_maps(w, &gs->tmP128, &gs->tmP256);
+    int rc = make_weight_maps(w, &gs->m128, &gs->m256);
     if (rc != MSQ_OK) {
       delete gs;
       return rc;
@@ -451,7 +473,7 @@ int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t 
     note_launch();
     a16 = scratch;
   }
-  const int rc = launch_gemm(st, w, gs->tmP128, gs->tmP256, a16, lda, M, d_y, ldy);
+  const int rc = launch_gemm(st, w, gs->m128, gs->m256, a16, lda, M, d_y, ldy);
   scratch_free(scratch, st);
   return rc;
 }
@@ -466,8 +488,8 @@ int run_gemm_staged(cudaStream_t st, const Weights& w, const void* d_a, int a_dt
   if (!w.fast4) return fail(MSQ_E_UNSUPPORTED, "GEMM path needs bits=4 and a power-of-two block_size >= 32");
   if (M <= 0) return MSQ_OK;
   if (M > 0x7fffffff) return fail(MSQ_E_INVALID, "GEMM: M too large");
-  CUtensorMap tmP128, tmP256;
-  int rc = make_weight_maps(w, &tmP128, &tmP256);
+  WeightMaps m128, m256;
+  int rc = make_weight_maps(w, &m128, &m256);
   if (rc != MSQ_OK) return rc;
   const void* a16 = d_a;
   int64_t lda = w.K;
@@ -481,7 +503,7 @@ int run_gemm_staged(cudaStream_t st, const Weights& w, const void* d_a, int a_dt
     MSQ_CUDA_TRY(cudaGetLastError(), "staging launch");
     a16 = staging;
   }
-  return launch_gemm(st, w, tmP128, tmP256, a16, lda, M, d_y, ldy);
+  return launch_gemm(st, w, m128, m256, a16, lda, M, d_y, ldy);
 }
 
 void release_gemm_state(Weights& w) {
