@@ -2,8 +2,10 @@
 //
 //   Y[m, n] = sum_k A[m, k] * W[n, k],  W[n, k] = fp16((q[n,k] - zp[n,b]) * s[n,b])
 //
-// One CTA computes a BM x BN tile of Y (BM = 128 activation rows = TMEM lanes, BN = 128 or
-// 256 weight rows = TMEM columns) over k-stages of 64:
+// One CTA computes a (128 TM) x BN tile of Y over k-stages of 64: TM accumulators of 128
+// activation rows (TMEM lanes) x BN weight rows (TMEM columns) that share one dequantised
+// weight tile, so each dequantised weight feeds 128 TM rows (TM = 2, BN = 128 for M > 128;
+// TM = 1, BN = 128 for small M):
 //   TMA warp    per stage: the fp16 activation tile (128 x 64, 128-byte swizzle), the packed
 //               int4 weight tile (BN rows x 32 bytes) and a 16-byte column of scales and of
 //               zero points per weight row covering the stage's blocks, no multicast;
@@ -11,9 +13,9 @@
 //   warps       16 bytes of codes and its scale / zero point from shared memory, writes fp16
 //               (q - zp) * s straight into the K-major 128-byte-swizzled layout the tensor
 //               core reads, then releases the stage;
-//   MMA warp    allocates TMEM and, from one lane, issues 4 x tcgen05.mma (M=128, N=BN, K=16)
-//               per stage with the fp32 accumulator in TMEM, committing each stage back to
-//               the producer;
+//   MMA warp    allocates TMEM and, from one lane, issues 4 TM x tcgen05.mma (M=128, N=BN,
+//               K=16) per stage into the fp32 accumulators in TMEM, committing each stage
+//               back to the producer;
 //   dequant     finally read the accumulator with tcgen05.ld and store fp32 Y.
 //   warps
 // The dequantised operand is exact up to one fp16 rounding of (q - zp) * s; products and
@@ -35,14 +37,16 @@ constexpr int BK = 64;
 
 __device__ int g_gemm_err;
 
-template <int BN>
+template <int TM, int BN>
 struct Plan {
+  static constexpr int kRows = BM * TM;               // activation rows of a tile
+  static constexpr int kCols = TM * BN;               // TMEM columns (the TM accumulators)
   static constexpr int kDeq = BN / 16;                // dequant warps: one thread per half row
   static constexpr int kThreads = (kDeq + 2) * 32;    // + TMA warp + MMA warp
   static constexpr int kTmaWarp = kDeq;
   static constexpr int kMmaWarp = kDeq + 1;
-  static constexpr int kStages = BN == 256 ? 3 : 4;
-  static constexpr int kABytes = BM * BK * 2;         // 16 KB
+  static constexpr int kStages = (TM == 1 && BN == 128) ? 4 : 3;
+  static constexpr int kABytes = kRows * BK * 2;      // 16 or 32 KB
   static constexpr int kBBytes = BN * BK * 2;         // dequantised fp16 weights
   static constexpr int kPBytes = BN * BK / 2;         // packed int4 weights
   static constexpr int kSBytes = BN * 16;             // 8 fp16 scales per row
@@ -101,12 +105,12 @@ __device__ __forceinline__ uint32_t deq_pair_f32(uint32_t bits, float z, float s
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-template <int BN, int ZPK>
-__global__ void __launch_bounds__(Plan<BN>::kThreads, 1)
+template <int TM, int BN, int ZPK>
+__global__ void __launch_bounds__(Plan<TM, BN>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmP,
                    const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmZ,
                    const GemmArgs p) {
-  using PL = Plan<BN>;
+  using PL = Plan<TM, BN>;
   constexpr int S = PL::kStages;
   constexpr int kDeqWarps = PL::kDeq;
   constexpr int kTmaWarp = PL::kTmaWarp;
@@ -122,7 +126,7 @@ __global__ void __launch_bounds__(Plan<BN>::kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * PL::kRows;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -135,7 +139,7 @@ __global__ void __launch_bounds__(Plan<BN>::kThreads, 1)
     ptx::fence_mbar_init();
   }
   if (warp == kMmaWarp) {
-    ptx::tmem_alloc(tmem_slot, BN);
+    ptx::tmem_alloc(tmem_slot, PL::kCols);
     ptx::tmem_relinquish();
   }
   if (warp == kTmaWarp && lane == 0) {
@@ -191,11 +195,14 @@ __global__ void __launch_bounds__(Plan<BN>::kThreads, 1)
              wait_abort(&wready[s], u & 1, abort_flag, ptx::kErrTimeoutFull);
         if (!ok) break;
         ptx::tc_fence_after();
-        const uint64_t ad = sw128_desc(ptx::smem_u32(smem + PL::kOffA + s * PL::kABytes));
         const uint64_t bd = sw128_desc(ptx::smem_u32(smem + PL::kOffB + s * PL::kBBytes));
 #pragma unroll
-        for (int j = 0; j < BK / 16; ++j)
-          ptx::mma_f16(tmem, ad + 2 * j, bd + 2 * j, idesc, (kt | j) != 0);
+        for (int t = 0; t < TM; ++t) {  // accumulator t: activation rows 128t.. of the tile
+          const uint64_t ad = sw128_desc(ptx::smem_u32(smem + PL::kOffA + s * PL::kABytes + t * BM * 128));
+#pragma unroll
+          for (int j = 0; j < BK / 16; ++j)
+            ptx::mma_f16(tmem + (uint32_t)(t * BN), ad + 2 * j, bd + 2 * j, idesc, (kt | j) != 0);
+        }
         ptx::mma_commit(&empty[s]);
       }
       ptx::mma_commit(accum);
@@ -267,13 +274,14 @@ __global__ void __launch_bounds__(Plan<BN>::kThreads, 1)
     if (ok) {
       const int q = warp & 3;                 // TMEM lane quarter of this warp
       const int cg = warp >> 2;               // column group
-      const int m = m0 + q * 32 + lane;
-      constexpr int kCols = BN / (kDeqWarps / 4);
+      constexpr int kCols = PL::kCols / (kDeqWarps / 4);
 #pragma unroll 1
       for (int cc = 0; cc < kCols; cc += 32) {
-        const int col = cg * kCols + cc;
+        const int tcol = cg * kCols + cc;     // TMEM column: accumulator tcol / BN
+        const int col = tcol % BN;
+        const int m = m0 + (tcol / BN) * BM + q * 32 + lane;
         uint32_t v[32];
-        ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)col, v);
+        ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)tcol, v);
         ptx::tmem_ld_wait();
         if (m < p.M) {
           float* yrow = p.y + (int64_t)m * p.ldy + n0 + col;
@@ -296,7 +304,7 @@ __global__ void __launch_bounds__(Plan<BN>::kThreads, 1)
   __syncthreads();
   if (warp == kMmaWarp) {
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem, BN);
+    ptx::tmem_dealloc(tmem, PL::kCols);
   }
 }
 
@@ -351,33 +359,33 @@ struct WeightMaps {
 };
 
 struct GemmState {
-  WeightMaps m128, m256;
+  WeightMaps m128;
 };
 
-template <int BN, int ZPK>
+template <int TM, int BN, int ZPK>
 int launch(cudaStream_t st, const CUtensorMap& tmA, const WeightMaps& wm, const GemmArgs& a, dim3 grid) {
-  auto kern = gemm_tc_kernel<BN, ZPK>;
+  auto kern = gemm_tc_kernel<TM, BN, ZPK>;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !configured[dev]) {
-    MSQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Plan<BN>::kSmem),
+    MSQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Plan<TM, BN>::kSmem),
                  "gemm smem attribute");
     configured[dev] = true;
   }
-  kern<<<grid, Plan<BN>::kThreads, Plan<BN>::kSmem, st>>>(tmA, wm.p, wm.s, wm.z, a);
+  kern<<<grid, Plan<TM, BN>::kThreads, Plan<TM, BN>::kSmem, st>>>(tmA, wm.p, wm.s, wm.z, a);
   note_launch();
   MSQ_CUDA_TRY(cudaGetLastError(), "gemm launch");
   return MSQ_OK;
 }
 
-template <int BN>
+template <int TM, int BN>
 int launch_zp(cudaStream_t st, int zp_kind, const CUtensorMap& tmA, const WeightMaps& wm, const GemmArgs& a,
               dim3 grid) {
   switch (zp_kind) {
-    case ZP_PACKED: return launch<BN, ZP_PACKED>(st, tmA, wm, a, grid);
-    case ZP_F32: return launch<BN, ZP_F32>(st, tmA, wm, a, grid);
-    default: return launch<BN, ZP_NONE>(st, tmA, wm, a, grid);
+    case ZP_PACKED: return launch<TM, BN, ZP_PACKED>(st, tmA, wm, a, grid);
+    case ZP_F32: return launch<TM, BN, ZP_F32>(st, tmA, wm, a, grid);
+    default: return launch<TM, BN, ZP_NONE>(st, tmA, wm, a, grid);
   }
 }
 
@@ -385,12 +393,16 @@ int launch_zp(cudaStream_t st, int zp_kind, const CUtensorMap& tmA, const Weight
 
 namespace {
 
-// Builds the activation map over fp16 rows of stride lda and launches the tile kernel.
-int launch_gemm(cudaStream_t st, const Weights& w, const WeightMaps& m128, const WeightMaps& m256,
-                const void* a16, int64_t lda, int64_t M, float* d_y, int64_t ldy) {
+// Builds the activation map over fp16 rows of stride lda and launches the tile kernel:
+// 256 x 128 tiles (two accumulators sharing each dequantised weight tile) when M > 128,
+// else 128 x 128.
+int launch_gemm(cudaStream_t st, const Weights& w, const WeightMaps& m128, const void* a16, int64_t lda,
+                int64_t M, float* d_y, int64_t ldy) {
+  const bool two = M > BM;
+  const int rows = two ? 2 * BM : BM;
   CUtensorMap tmA;
   int rc = make_map_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, const_cast<void*>(a16), (uint64_t)w.K, (uint64_t)M,
-                       (uint64_t)lda * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+                       (uint64_t)lda * 2, BK, rows, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != MSQ_OK) return rc;
   GemmArgs g{};
   g.y = d_y;
@@ -403,15 +415,9 @@ int launch_gemm(cudaStream_t st, const Weights& w, const WeightMaps& m128, const
   while ((1 << sh) < w.block_size) ++sh;
   g.bs_shift = sh;
   g.vec_store = (ldy % 4 == 0) && ((reinterpret_cast<uintptr_t>(d_y) & 15) == 0);
-  const int64_t mt = (M + BM - 1) / BM;
-  const int64_t tiles256 = (w.n_rows + 255) / 256 * mt;
-  const bool big = tiles256 >= 2 * num_sms(w.device);
-  if (big) {
-    rc = launch_zp<256>(st, w.zp_kind, tmA, m256, g, dim3((w.n_rows + 255) / 256, (unsigned)mt));
-  } else {
-    rc = launch_zp<128>(st, w.zp_kind, tmA, m128, g, dim3((w.n_rows + 127) / 128, (unsigned)mt));
-  }
-  if (rc == MSQ_OK) note_path(big ? "gemm_tc_n256" : "gemm_tc_n128");
+  const dim3 grid((w.n_rows + 127) / 128, (unsigned)((M + rows - 1) / rows));
+  rc = two ? launch_zp<2, 128>(st, w.zp_kind, tmA, m128, g, grid) : launch_zp<1, 128>(st, w.zp_kind, tmA, m128, g, grid);
+  if (rc == MSQ_OK) note_path(two ? "gemm_tc_m256_n128" : "gemm_tc_m128_n128");
   return rc;
 }
 
@@ -434,9 +440,8 @@ int make_maps(const Weights& w, int bn, WeightMaps* m) {
   return MSQ_OK;
 }
 
-int make_weight_maps(const Weights& w, WeightMaps* m128, WeightMaps* m256) {
-  const int rc = make_maps(w, 128, m128);
-  return rc == MSQ_OK ? make_maps(w, 256, m256) : rc;
+int make_weight_maps(const Weights& w, WeightMaps* m128) {
+  return make_maps(w, 128, m128);
 }
 
 // fp16 activations with 16-byte rows feed TMA directly; anything else is staged as fp16.
@@ -455,7 +460,7 @@ int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t 
   GemmState* gs = static_cast<GemmState*>(w.gemm_state);
   if (!gs) {
     gs = new GemmState();
-    int rc = make_weight_maps(w, &gs->m128, &gs->m256);
+    int rc = make_weight_maps(w, &gs->m128);
     if (rc != MSQ_OK) {
       delete gs;
       return rc;
@@ -473,7 +478,7 @@ int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t 
     note_launch();
     a16 = scratch;
   }
-  const int rc = launch_gemm(st, w, gs->m128, gs->m256, a16, lda, M, d_y, ldy);
+  const int rc = launch_gemm(st, w, gs->m128, a16, lda, M, d_y, ldy);
   scratch_free(scratch, st);
   return rc;
 }
@@ -488,8 +493,8 @@ int run_gemm_staged(cudaStream_t st, const Weights& w, const void* d_a, int a_dt
   if (!w.fast4) return fail(MSQ_E_UNSUPPORTED, "GEMM path needs bits=4 and a power-of-two block_size >= 32");
   if (M <= 0) return MSQ_OK;
   if (M > 0x7fffffff) return fail(MSQ_E_INVALID, "GEMM: M too large");
-  WeightMaps m128, m256;
-  int rc = make_weight_maps(w, &m128, &m256);
+  WeightMaps m128;
+  int rc = make_weight_maps(w, &m128);
   if (rc != MSQ_OK) return rc;
   const void* a16 = d_a;
   int64_t lda = w.K;
@@ -503,7 +508,7 @@ int run_gemm_staged(cudaStream_t st, const Weights& w, const void* d_a, int a_dt
     MSQ_CUDA_TRY(cudaGetLastError(), "staging launch");
     a16 = staging;
   }
-  return launch_gemm(st, w, m128, m256, a16, lda, M, d_y, ldy);
+  return launch_gemm(st, w, m128, a16, lda, M, d_y, ldy);
 }
 
 void release_gemm_state(Weights& w) {
