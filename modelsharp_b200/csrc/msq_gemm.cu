@@ -4,8 +4,8 @@
 //
 // One CTA computes a (128 TM) x BN tile of Y over k-stages of 64: TM accumulators of 128
 // activation rows (TMEM lanes) x BN weight rows (TMEM columns) that share one dequantised
-// weight tile, so each dequantised weight feeds 128 TM rows (TM = 2, BN = 128 for M > 128;
-// TM = 1, BN = 128 for small M):
+// weight tile, so each dequantised weight feeds 128 TM rows (BN = 128; TM = 4 for M >= 512,
+// 2 for M > 128, 1 below):
 //   TMA warp    per stage: the fp16 activation tile (128 x 64, 128-byte swizzle), the packed
 //               int4 weight tile (BN rows x 32 bytes) and a 16-byte column of scales and of
 //               zero points per weight row covering the stage's blocks, no multicast;
@@ -45,8 +45,9 @@ struct Plan {
   static constexpr int kThreads = (kDeq + 2) * 32;    // + TMA warp + MMA warp
   static constexpr int kTmaWarp = kDeq;
   static constexpr int kMmaWarp = kDeq + 1;
-  static constexpr int kStages = (TM == 1 && BN == 128) ? 4 : 3;
+  static constexpr int kStages = TM == 1 ? 4 : TM == 2 ? 3 : 2;  // what fits in 227 KB
   static constexpr int kABytes = kRows * BK * 2;      // 16 or 32 KB
+  static constexpr int kABoxes = kRows > 256 ? kRows / 256 : 1;  // activation TMA boxes per stage
   static constexpr int kBBytes = BN * BK * 2;         // dequantised fp16 weights
   static constexpr int kPBytes = BN * BK / 2;         // packed int4 weights
   static constexpr int kSBytes = BN * 16;             // 8 fp16 scales per row
@@ -164,7 +165,10 @@ __global__ void __launch_bounds__(Plan<TM, BN>::kThreads, 1)
         const int blk0 = (kt * BK) >> p.bs_shift;
         ptx::mbar_arrive_expect_tx(&full[s],
                                    PL::kABytes + PL::kPBytes + PL::kSBytes + (ZPK != ZP_NONE ? PL::kZBytes : 0));
-        ptx::tma_load_2d(smem + PL::kOffA + s * PL::kABytes, &tmA, &full[s], kt * BK, m0);
+#pragma unroll
+        for (int h = 0; h < PL::kABoxes; ++h)  // a box is at most 256 rows
+          ptx::tma_load_2d(smem + PL::kOffA + s * PL::kABytes + h * (PL::kABytes / PL::kABoxes), &tmA, &full[s],
+                           kt * BK, m0 + h * (PL::kRows / PL::kABoxes));
         ptx::tma_load_2d(smem + PL::kOffP + s * PL::kPBytes, &tmP, &full[s], kt * (BK / 2), n0);
         ptx::tma_load_2d(smem + PL::kOffS + s * PL::kSBytes, &tmS, &full[s], blk0 & ~7, n0);
         if (ZPK == ZP_PACKED)
@@ -394,15 +398,15 @@ int launch_zp(cudaStream_t st, int zp_kind, const CUtensorMap& tmA, const Weight
 namespace {
 
 // Builds the activation map over fp16 rows of stride lda and launches the tile kernel:
-// 256 x 128 tiles (two accumulators sharing each dequantised weight tile) when M > 128,
-// else 128 x 128.
+// 512 x 128 tiles (four accumulators sharing each dequantised weight tile) for M >= 512,
+// 256 x 128 for M > 128, else 128 x 128.
 int launch_gemm(cudaStream_t st, const Weights& w, const WeightMaps& m128, const void* a16, int64_t lda,
                 int64_t M, float* d_y, int64_t ldy) {
-  const bool two = M > BM;
-  const int rows = two ? 2 * BM : BM;
+  const int tm = M >= 4 * BM ? 4 : M > BM ? 2 : 1;
+  const int rows = tm * BM;
   CUtensorMap tmA;
   int rc = make_map_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, const_cast<void*>(a16), (uint64_t)w.K, (uint64_t)M,
-                       (uint64_t)lda * 2, BK, rows, CU_TENSOR_MAP_SWIZZLE_128B);
+                       (uint64_t)lda * 2, BK, std::min(rows, 256), CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != MSQ_OK) return rc;
   GemmArgs g{};
   g.y = d_y;
@@ -416,8 +420,10 @@ int launch_gemm(cudaStream_t st, const Weights& w, const WeightMaps& m128, const
   g.bs_shift = sh;
   g.vec_store = (ldy % 4 == 0) && ((reinterpret_cast<uintptr_t>(d_y) & 15) == 0);
   const dim3 grid((w.n_rows + 127) / 128, (unsigned)((M + rows - 1) / rows));
-  rc = two ? launch_zp<2, 128>(st, w.zp_kind, tmA, m128, g, grid) : launch_zp<1, 128>(st, w.zp_kind, tmA, m128, g, grid);
-  if (rc == MSQ_OK) note_path(two ? "gemm_tc_m256_n128" : "gemm_tc_m128_n128");
+  rc = tm == 4   ? launch_zp<4, 128>(st, w.zp_kind, tmA, m128, g, grid)
+       : tm == 2 ? launch_zp<2, 128>(st, w.zp_kind, tmA, m128, g, grid)
+                 : launch_zp<1, 128>(st, w.zp_kind, tmA, m128, g, grid);
+  if (rc == MSQ_OK) note_path(tm == 4 ? "gemm_tc_m512_n128" : tm == 2 ? "gemm_tc_m256_n128" : "gemm_tc_m128_n128");
   return rc;
 }
 

@@ -34,7 +34,8 @@ def sampled_ref(c, rows):
     (64, 1000, 4160, 128, "packed"),   # ragged N tile and ragged last k-stage
     (128, 512, 1024, 32, "none"),
     (200, 384, 2048, 64, "float"),
-    (300, 4096, 4096, 128, "packed"),  # BN=256 tiles
+    (300, 4096, 4096, 128, "packed"),  # 256-row tiles (two accumulators)
+    (600, 640, 1024, 32, "float"),     # 512-row tiles (four accumulators), ragged last M tile
 ])
 def test_gemm_parity_fp32_activations(cuda_device, M, N_, K, bs, zp):
     c = synth.make_case(31, M, N_, K, 4, bs, zp, scale_lo=0.001, scale_hi=0.01)
