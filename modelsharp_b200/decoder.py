@@ -1,0 +1,205 @@
+"""A Llama-shaped INT4 decoder whose every projection is MatMulNBits on this backend.
+
+The end-to-end workload of the op (synthetic 7B shape: 32 layers, hidden 4096, 32 query /
+8 key-value heads of 128, SwiGLU 14336, vocabulary 32000, every projection bits=4 with
+block_size 32 and zero points): the q/k/v/o and gate/up/down projections and the LM head
+run on libms_cuda_nbits (the tensor-core GEMM for a prompt, the decode GEMV per token); the
+glue between them (RMSNorm, rotary embedding, causal grouped-query attention over a KV
+cache, SwiGLU, residual adds, greedy argmax) is plain torch in float32. Its semantics follow
+the reference's CPU kernels: SimplifiedLayerNormalizationKernel.cs:48-54 (RMSNorm),
+RotaryEmbeddingKernel.cs:96-114 (half-split rotary), GroupQueryAttentionKernel.cs:194-195,
+275-312 (causal GQA, 1/sqrt(d) scale).
+
+Weights are drawn on the device from a seeded torch generator (uniform codes and zero
+points, scales uniform in [scale_lo, scale_hi], an N(0, 1) embedding table).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _native as N
+from .weights import QuantizedWeights
+
+PROJ = ("q", "k", "v", "o", "gate", "up", "down")
+
+
+@dataclass(frozen=True)
+class DecoderConfig:
+    layers: int = 32
+    hidden: int = 4096
+    heads: int = 32
+    kv_heads: int = 8
+    head_dim: int = 128
+    inter: int = 14336
+    vocab: int = 32000
+    block_size: int = 32
+    rope_theta: float = 1e4
+    eps: float = 1e-5
+    max_seq: int = 640
+    scale_lo: float = 0.001
+    scale_hi: float = 0.01
+
+
+def proj_shapes(cfg: DecoderConfig) -> dict[str, tuple[int, int]]:
+    """(N, K) of every projection of a layer."""
+    h, kv, i = cfg.hidden, cfg.kv_heads * cfg.head_dim, cfg.inter
+    return {"q": (cfg.heads * cfg.head_dim, h), "k": (kv, h), "v": (kv, h), "o": (h, cfg.heads * cfg.head_dim),
+            "gate": (i, h), "up": (i, h), "down": (h, i)}
+
+
+def weight_bytes_per_token(cfg: DecoderConfig) -> int:
+    """Algorithmic MatMulNBits bytes one decode step reads: codes, fp32 scales, packed zp."""
+    from .synth import algorithmic_bytes
+    per_layer = sum(algorithmic_bytes(n, k, 4, cfg.block_size, "packed") for n, k in proj_shapes(cfg).values())
+    return cfg.layers * per_layer + algorithmic_bytes(cfg.vocab, cfg.hidden, 4, cfg.block_size, "packed")
+
+
+def _quant(n: int, k: int, cfg: DecoderConfig, g: torch.Generator, dev: torch.device) -> dict:
+    nb = -(-k // cfg.block_size)
+    return {"b": torch.randint(0, 256, (n, nb, cfg.block_size // 2), dtype=torch.uint8, device=dev, generator=g),
+            "scales": torch.empty(n * nb, device=dev).uniform_(cfg.scale_lo, cfg.scale_hi, generator=g),
+            "zp": torch.randint(0, 256, (n, -(-nb // 2)), dtype=torch.uint8, device=dev, generator=g)}
+
+
+def make_weights(cfg: DecoderConfig, seed: int, device: torch.device | str) -> dict:
+    """Every weight of the decoder in the op's reference layouts, on `device`."""
+    dev = torch.device(device)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    shapes = proj_shapes(cfg)
+    layers = []
+    for _ in range(cfg.layers):
+        lw = {name: _quant(*shapes[name], cfg, g, dev) for name in PROJ}
+        lw["norm_attn"] = torch.empty(cfg.hidden, device=dev).uniform_(0.8, 1.2, generator=g)
+        lw["norm_mlp"] = torch.empty(cfg.hidden, device=dev).uniform_(0.8, 1.2, generator=g)
+        layers.append(lw)
+    return {"layers": layers,
+            "embed": torch.randn(cfg.vocab, cfg.hidden, device=dev, generator=g),
+            "norm_final": torch.empty(cfg.hidden, device=dev).uniform_(0.8, 1.2, generator=g),
+            "lm_head": _quant(cfg.vocab, cfg.hidden, cfg, g, dev)}
+
+
+def weights_to_host(w: dict) -> dict:
+    """numpy copy (for the parity checker)."""
+    if isinstance(w, dict):
+        return {k: weights_to_host(v) for k, v in w.items()}
+    if isinstance(w, list):
+        return [weights_to_host(v) for v in w]
+    return w.cpu().numpy()
+
+
+class CudaDecoder:
+    """Greedy decoding with the projections on libms_cuda_nbits."""
+
+    def __init__(self, cfg: DecoderConfig, weights: dict, device: torch.device | str):
+        self.cfg = cfg
+        self.device = dev = torch.device(device)
+        shapes = proj_shapes(cfg)
+
+        def pack(w, n, k):
+            return QuantizedWeights(w["b"], w["scales"], w["zp"], n, k, 4, cfg.block_size, device=dev)
+
+        self.layers = []
+        for lw in weights["layers"]:
+            self.layers.append({**{name: pack(lw[name], *shapes[name]) for name in PROJ},
+                                "norm_attn": lw["norm_attn"], "norm_mlp": lw["norm_mlp"]})
+        self.lm_head = pack(weights["lm_head"], cfg.vocab, cfg.hidden)
+        self.embed = weights["embed"]
+        self.norm_final = weights["norm_final"]
+        half = cfg.head_dim // 2
+        inv = cfg.rope_theta ** (-np.arange(half, dtype=np.float64) * 2.0 / cfg.head_dim)
+        ang = np.arange(cfg.max_seq, dtype=np.float64)[:, None] * inv[None, :]
+        self.cos = torch.from_numpy(np.cos(ang).astype(np.float32)).to(dev)
+        self.sin = torch.from_numpy(np.sin(ang).astype(np.float32)).to(dev)
+        shape = (cfg.layers, cfg.kv_heads, cfg.max_seq, cfg.head_dim)
+        self.kc = torch.zeros(shape, device=dev)
+        self.vc = torch.zeros(shape, device=dev)
+        self.keys = torch.arange(cfg.max_seq, device=dev)
+
+    # ---- glue
+    def _norm(self, x, gamma):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.cfg.eps) * gamma
+
+    def _rope(self, x, heads, cos, sin):
+        s, d = x.shape[0], self.cfg.head_dim
+        v = x.view(s, heads, d)
+        a, b = v[..., : d // 2], v[..., d // 2:]
+        c, sn = cos[:, None, :], sin[:, None, :]
+        return torch.cat((a * c - b * sn, b * c + a * sn), dim=-1).reshape(s, heads * d)
+
+    def _attend(self, q, li, mask):
+        """q [S, H*d] against the layer's cache; mask [S, max_seq] True where a key is visible."""
+        cfg = self.cfg
+        s, d, hkv = q.shape[0], cfg.head_dim, cfg.kv_heads
+        qv = q.view(s, hkv, cfg.heads // hkv, d).permute(1, 2, 0, 3)           # [Hkv, G, S, d]
+        sc = torch.matmul(qv, self.kc[li].unsqueeze(1).transpose(-1, -2)) / float(np.sqrt(d))  # [Hkv, G, S, T]
+        sc = sc.masked_fill(~mask, float("-inf"))
+        p = torch.softmax(sc, dim=-1)
+        out = torch.matmul(p, self.vc[li].unsqueeze(1))                          # [Hkv, G, S, d]
+        return out.permute(2, 0, 1, 3).reshape(s, cfg.heads * d)
+
+    def _block(self, x, li, cos, sin, write, mask, path):
+        cfg, lw = self.cfg, self.layers[li]
+        h = self._norm(x, lw["norm_attn"])
+        q = self._rope(lw["q"].matmul(h, path=path), cfg.heads, cos, sin)
+        k = self._rope(lw["k"].matmul(h, path=path), cfg.kv_heads, cos, sin)
+        v = lw["v"].matmul(h, path=path)
+        s = x.shape[0]
+        write(self.kc[li], k.view(s, cfg.kv_heads, cfg.head_dim).transpose(0, 1))
+        write(self.vc[li], v.view(s, cfg.kv_heads, cfg.head_dim).transpose(0, 1))
+        x = x + lw["o"].matmul(self._attend(q, li, mask), path=path)
+        h = self._norm(x, lw["norm_mlp"])
+        act = torch.nn.functional.silu(lw["gate"].matmul(h, path=path)) * lw["up"].matmul(h, path=path)
+        return x + lw["down"].matmul(act, path=path)
+
+    # ---- passes
+    def prefill(self, tokens: torch.Tensor, path: int = N.PATH_AUTO) -> torch.Tensor:
+        """Runs the prompt from position 0; returns the last position's logits [vocab]."""
+        s = tokens.shape[0]
+        cos, sin = self.cos[:s], self.sin[:s]
+        mask = self.keys[None, :] <= torch.arange(s, device=self.device)[:, None]
+
+        def write(cache, kv):  # kv [Hkv, S, d] at positions 0..S-1
+            cache[:, :s].copy_(kv)
+
+        x = self.embed[tokens]
+        for li in range(self.cfg.layers):
+            x = self._block(x, li, cos, sin, write, mask, path)
+        return self.lm_head.matmul(self._norm(x[-1:], self.norm_final), path=path)[0]
+
+    def decode_step(self, tok: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        """One token: tok [1] (int64) at position pos [1] (int64), both on the device; writes
+        the argmax into tok, advances pos and returns the logits [vocab]. Only device tensors
+        change, so the step can be captured in a CUDA graph and replayed."""
+        cos, sin = self.cos[pos], self.sin[pos]
+        mask = (self.keys <= pos)[None, :]
+
+        def write(cache, kv):  # kv [Hkv, 1, d] at position pos
+            cache.index_copy_(1, pos, kv)
+
+        x = self.embed[tok]
+        for li in range(self.cfg.layers):
+            x = self._block(x, li, cos, sin, write, mask, N.PATH_GEMV)
+        logits = self.lm_head.matmul(self._norm(x, self.norm_final))[0]
+        tok.copy_(torch.argmax(logits).view(1))
+        pos.add_(1)
+        return logits
+
+    def generate(self, prompt: torch.Tensor, n_new: int, path: int = N.PATH_AUTO) -> torch.Tensor:
+        """Greedy: the prompt in one pass, then n_new - 1 decode steps; the new tokens [n_new]."""
+        logits = self.prefill(prompt, path)
+        tok = torch.argmax(logits).view(1)
+        pos = torch.tensor([prompt.shape[0]], device=self.device)
+        out = [tok.clone()]
+        for _ in range(n_new - 1):
+            self.decode_step(tok, pos)
+            out.append(tok.clone())
+        return torch.cat(out)
+
+    def free(self) -> None:
+        for lw in self.layers:
+            for name in PROJ:
+                lw[name].free()
+        self.lm_head.free()
