@@ -697,7 +697,9 @@ def run_prefill(args, rank: int, world: int, local_rank: int):
 DECODE_WORKLOAD = ("synthetic 7B-shaped INT4 decoder (BASELINE configs[4]): 32 layers, hidden 4096, 32 query / "
                    "8 key-value heads of 128, SwiGLU 14336, vocabulary 32000, every projection MatMulNBits bits=4 "
                    "block_size=32 with zero points; greedy decode of 128 tokens after a 512-token prompt of uniform "
-                   "random ids; glue (RMSNorm, rotary, GQA, SwiGLU) in torch fp32")
+                   "random ids; q/k/v and gate/up packed into one MatMulNBits each; fp32 glue: the library's "
+                   "fused decode kernels (add+RMSNorm, rotary+KV append, split-K GQA, SwiGLU, argmax), torch for "
+                   "the prompt pass")
 
 
 def run_decode(args, rank: int, world: int, local_rank: int):

@@ -212,6 +212,40 @@ int msq_matmul_gather(void* cu_ctx, void* stream, msq_weights_t w,
  * copy to the host.                                                                      */
 int msq_wait_gathered(void* cu_ctx, void* stream, const msq_wait_t* wait);
 
+/* ---- decoder glue for one decode token (fp32, device pointers, enqueue-only) ----------
+ * The kernels a Llama-shaped decode step needs between its MatMulNBits projections, so that
+ * a step is a short chain of launches that a CUDA graph can replay (positions are read from
+ * device memory). Not part of the reference's C ABI: each restates one of the reference's CPU
+ * graph kernels (cited per entry).                                                      */
+
+/* x[r] <- x[r] + delta[r] (delta may be NULL); y[r] <- x[r] / sqrt(mean(x[r]^2) + eps) * gamma,
+ * for rows r < rows of n floats (SkipSimplifiedLayerNormalizationKernel.cs:64-67,
+ * SimplifiedLayerNormalizationKernel.cs:48-54).                                         */
+int msq_add_rmsnorm(void* cu_ctx, void* stream, float* x, const float* delta, const float* gamma,
+                    float* y, int64_t rows, int64_t n, float eps);
+
+/* One token's qkv = [q (heads*d) | k (kv_heads*d) | v (kv_heads*d)]: half-split rotary of q and
+ * k in place with cos/sin [max_seq][d/2] at position *d_pos, then k and v written to row
+ * *d_pos of the caches [kv_heads][max_seq][d] (RotaryEmbeddingKernel.cs:96-114).        */
+int msq_rope_append(void* cu_ctx, void* stream, float* qkv, int heads, int kv_heads, int d,
+                    const float* cos_t, const float* sin_t, const int64_t* d_pos,
+                    float* kcache, float* vcache, int64_t max_seq);
+
+/* out[h] = softmax(q[h] . K[g]^T / sqrt(d)) . V[g] over cache rows 0..*d_pos, g = h / (heads /
+ * kv_heads) (GroupQueryAttentionKernel.cs:194-195, 275-312). A position past the cache reads
+ * all max_seq rows. MSQ_E_UNSUPPORTED unless heads / kv_heads <= 8, d <= 256 with d % 4 == 0,
+ * q and the caches 16-byte aligned, and max_seq fits the shared-memory plan (max_seq 2^15
+ * at 4 query heads per kv head).                                                           */
+int msq_gqa_decode(void* cu_ctx, void* stream, const float* q, const float* kcache,
+                   const float* vcache, const int64_t* d_pos, float* out, int heads, int kv_heads,
+                   int d, int64_t max_seq);
+
+/* gate_up = [gate (n) | up (n)]: out = gate / (1 + exp(-gate)) * up.                     */
+int msq_swiglu(void* cu_ctx, void* stream, const float* gate_up, float* out, int64_t n);
+
+/* *d_idx = the first index of the maximum of x[0..n); *d_pos += 1 when d_pos is not NULL.  */
+int msq_argmax(void* cu_ctx, void* stream, const float* x, int64_t n, int64_t* d_idx, int64_t* d_pos);
+
 /* ---- one-shot drop-in for ms_qgemm_nbits (native/ms_kernels.h:42-44) -----------------
  * Host pointers, fp32 A / scales, packed or NULL zero points; uploads, runs on the
  * current device and downloads per call. Returns a status where the original is void. */

@@ -645,6 +645,60 @@ int msq_wait_gathered(void* cu_ctx, void* stream, const msq_wait_t* wait) {
   return run_wait_gathered(static_cast<cudaStream_t>(stream), wait);
 }
 
+int msq_add_rmsnorm(void* cu_ctx, void* stream, float* x, const float* delta, const float* gamma, float* y,
+                    int64_t rows, int64_t n, float eps) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  if (!x || !gamma || !y) return fail(MSQ_E_INVALID, "msq_add_rmsnorm: NULL pointer");
+  if (rows < 1 || n < 1 || rows > 0x7fffffff || n > 0x7fffffff)
+    return fail(MSQ_E_INVALID, "msq_add_rmsnorm: bad shape [%lld, %lld]", (long long)rows, (long long)n);
+  return run_add_rmsnorm(static_cast<cudaStream_t>(stream), x, delta, gamma, y, rows, n, eps);
+}
+
+int msq_rope_append(void* cu_ctx, void* stream, float* qkv, int heads, int kv_heads, int d, const float* cos_t,
+                    const float* sin_t, const int64_t* d_pos, float* kcache, float* vcache, int64_t max_seq) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  if (!qkv || !cos_t || !sin_t || !d_pos || !kcache || !vcache) return fail(MSQ_E_INVALID, "msq_rope_append: NULL pointer");
+  if (heads < 1 || kv_heads < 1 || heads % kv_heads || d < 2 || (d & 1) || max_seq < 1 ||
+      ((int64_t)heads + 2 * (int64_t)kv_heads) * d > 0x7fffffff)
+    return fail(MSQ_E_INVALID, "msq_rope_append: heads %d, kv_heads %d, d %d, max_seq %lld", heads, kv_heads, d,
+                (long long)max_seq);
+  return run_rope_append(static_cast<cudaStream_t>(stream), qkv, heads, kv_heads, d, cos_t, sin_t, d_pos, kcache,
+                         vcache, max_seq);
+}
+
+int msq_gqa_decode(void* cu_ctx, void* stream, const float* q, const float* kcache, const float* vcache,
+                   const int64_t* d_pos, float* out, int heads, int kv_heads, int d, int64_t max_seq) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  if (!q || !kcache || !vcache || !d_pos || !out) return fail(MSQ_E_INVALID, "msq_gqa_decode: NULL pointer");
+  if (heads < 1 || kv_heads < 1 || heads % kv_heads || d < 1 || max_seq < 1)
+    return fail(MSQ_E_INVALID, "msq_gqa_decode: heads %d, kv_heads %d, d %d", heads, kv_heads, d);
+  if (heads / kv_heads > 8 || d > 256 || (d & 3) || ((uintptr_t)q | (uintptr_t)kcache | (uintptr_t)vcache) & 15)
+    return fail(MSQ_E_UNSUPPORTED,
+                "msq_gqa_decode: needs heads / kv_heads <= 8, d <= 256 and a multiple of 4, 16-byte aligned q and "
+                "caches (heads %d, kv_heads %d, d %d)", heads, kv_heads, d);
+  if (gqa_decode_smem(heads, kv_heads, d, max_seq) > 200 * 1024)
+    return fail(MSQ_E_UNSUPPORTED, "msq_gqa_decode: max_seq %lld with d %d exceeds the shared-memory plan",
+                (long long)max_seq, d);
+  return run_gqa_decode(static_cast<cudaStream_t>(stream), q, kcache, vcache, d_pos, out, heads, kv_heads, d, max_seq);
+}
+
+int msq_swiglu(void* cu_ctx, void* stream, const float* gate_up, float* out, int64_t n) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  if (!gate_up || !out || n < 1) return fail(MSQ_E_INVALID, "msq_swiglu: NULL pointer or empty");
+  return run_swiglu(static_cast<cudaStream_t>(stream), gate_up, out, n);
+}
+
+int msq_argmax(void* cu_ctx, void* stream, const float* x, int64_t n, int64_t* d_idx, int64_t* d_pos) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  if (!x || !d_idx || n < 1) return fail(MSQ_E_INVALID, "msq_argmax: NULL pointer or empty");
+  return run_argmax(static_cast<cudaStream_t>(stream), x, n, d_idx, d_pos);
+}
+
 int msq_qgemm_nbits(const float* a, const uint8_t* bq, const float* scales, const uint8_t* zero_points, float* y,
                     int M, int N, int K, int bits, int block_size) {
   if (N <= 0 || K <= 0 || block_size <= 0 || (bits != 4 && bits != 8) || M < 0)

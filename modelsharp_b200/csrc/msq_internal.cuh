@@ -117,6 +117,18 @@ int run_gemm_staged(cudaStream_t st, const Weights& w, const void* d_a, int a_dt
 int run_gemm_noalloc(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M,
                      float* d_y, int64_t ldy);
 
+// ---- decoder glue (msq_decoder.cu) ----
+int run_add_rmsnorm(cudaStream_t st, float* x, const float* delta, const float* gamma, float* y, int64_t rows,
+                    int64_t n, float eps);
+int run_rope_append(cudaStream_t st, float* qkv, int heads, int kv, int d, const float* cos_t, const float* sin_t,
+                    const int64_t* pos, float* kc, float* vc, int64_t max_seq);
+int run_gqa_decode(cudaStream_t st, const float* q, const float* kc, const float* vc, const int64_t* pos, float* out,
+                   int heads, int kv, int d, int64_t max_seq);
+// Dynamic shared memory of one gqa_decode block (heads / kv <= 8, d <= 256).
+size_t gqa_decode_smem(int heads, int kv, int d, int64_t max_seq);
+int run_swiglu(cudaStream_t st, const float* gu, float* out, int64_t n);
+int run_argmax(cudaStream_t st, const float* x, int64_t n, int64_t* idx, int64_t* pos);
+
 // Loads element idx of an activation tensor of dtype dt (f32 / f16 / bf16) as fp32.
 __device__ __forceinline__ float load_act(const void* a, int dt, int64_t idx) {
   if (dt == MSQ_DT_F32) return static_cast<const float*>(a)[idx];

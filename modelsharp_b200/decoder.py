@@ -2,13 +2,13 @@
 
 The end-to-end workload of the op (synthetic 7B shape: 32 layers, hidden 4096, 32 query /
 8 key-value heads of 128, SwiGLU 14336, vocabulary 32000, every projection bits=4 with
-block_size 32 and zero points): the q/k/v/o and gate/up/down projections and the LM head
-run on libms_cuda_nbits (the tensor-core GEMM for a prompt, the decode GEMV per token); the
-glue between them (RMSNorm, rotary embedding, causal grouped-query attention over a KV
-cache, SwiGLU, residual adds, greedy argmax) is plain torch in float32. Its semantics follow
-the reference's CPU kernels: SimplifiedLayerNormalizationKernel.cs:48-54 (RMSNorm),
-RotaryEmbeddingKernel.cs:96-114 (half-split rotary), GroupQueryAttentionKernel.cs:194-195,
-275-312 (causal GQA, 1/sqrt(d) scale).
+block_size 32 and zero points): the packed q/k/v, o, packed gate/up and down projections and
+the LM head run on libms_cuda_nbits (the tensor-core GEMM for a prompt, the decode GEMV per
+token). The glue between them (RMSNorm, rotary embedding, causal grouped-query attention over
+a KV cache, SwiGLU, residual adds, greedy argmax) is float32: torch for the prompt pass, the
+library's fused glue kernels for a decode step. Its semantics follow the reference's CPU
+kernels: SimplifiedLayerNormalizationKernel.cs:48-54 (RMSNorm), RotaryEmbeddingKernel.cs:96-114
+(half-split rotary), GroupQueryAttentionKernel.cs:194-195, 275-312 (causal GQA, 1/sqrt(d) scale).
 
 Weights are drawn on the device from a seeded torch generator (uniform codes and zero
 points, scales uniform in [scale_lo, scale_hi], an N(0, 1) embedding table).
@@ -90,21 +90,37 @@ def weights_to_host(w: dict) -> dict:
     return w.cpu().numpy()
 
 
+def _cat(ws: list[dict]) -> dict:
+    """Weights stacked along N (the output rows): one projection computing several at once."""
+    return {"b": torch.cat([w["b"] for w in ws]), "scales": torch.cat([w["scales"].reshape(-1) for w in ws]),
+            "zp": torch.cat([w["zp"] for w in ws])}
+
+
 class CudaDecoder:
-    """Greedy decoding with the projections on libms_cuda_nbits."""
+    """Greedy decoding with the projections on libms_cuda_nbits.
+
+    q/k/v are packed into one weight (N = (H + 2 Hkv) d) and gate/up into another (N = 2 I), as
+    packed-QKV exports do, so a layer runs four MatMulNBits. The prompt pass uses torch glue;
+    a decode step uses the library's fused glue (add + RMSNorm, rotary + KV append, GQA decode,
+    SwiGLU, argmax), every launch chained with programmatic dependent launch."""
 
     def __init__(self, cfg: DecoderConfig, weights: dict, device: torch.device | str):
         self.cfg = cfg
         self.device = dev = torch.device(device)
         shapes = proj_shapes(cfg)
+        self.n_q, self.n_kv = cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
 
         def pack(w, n, k):
             return QuantizedWeights(w["b"], w["scales"], w["zp"], n, k, 4, cfg.block_size, device=dev)
 
         self.layers = []
         for lw in weights["layers"]:
-            self.layers.append({**{name: pack(lw[name], *shapes[name]) for name in PROJ},
-                                "norm_attn": lw["norm_attn"], "norm_mlp": lw["norm_mlp"]})
+            self.layers.append({
+                "qkv": pack(_cat([lw["q"], lw["k"], lw["v"]]), self.n_q + 2 * self.n_kv, cfg.hidden),
+                "o": pack(lw["o"], *shapes["o"]),
+                "gate_up": pack(_cat([lw["gate"], lw["up"]]), 2 * cfg.inter, cfg.hidden),
+                "down": pack(lw["down"], *shapes["down"]),
+                "norm_attn": lw["norm_attn"], "norm_mlp": lw["norm_mlp"]})
         self.lm_head = pack(weights["lm_head"], cfg.vocab, cfg.hidden)
         self.embed = weights["embed"]
         self.norm_final = weights["norm_final"]
@@ -117,14 +133,21 @@ class CudaDecoder:
         self.kc = torch.zeros(shape, device=dev)
         self.vc = torch.zeros(shape, device=dev)
         self.keys = torch.arange(cfg.max_seq, device=dev)
+        # decode-step buffers (fixed addresses, so a captured step can be replayed)
+        f = dict(device=dev, dtype=torch.float32)
+        self.bx, self.bh = torch.empty(1, cfg.hidden, **f), torch.empty(1, cfg.hidden, **f)
+        self.bqkv = torch.empty(1, self.n_q + 2 * self.n_kv, **f)
+        self.battn, self.bo = torch.empty(1, self.n_q, **f), torch.empty(1, cfg.hidden, **f)
+        self.bgu, self.bact = torch.empty(1, 2 * cfg.inter, **f), torch.empty(1, cfg.inter, **f)
+        self.bdown, self.blogits = torch.empty(1, cfg.hidden, **f), torch.empty(1, cfg.vocab, **f)
 
-    # ---- glue
+    # ---- torch glue (prompt pass)
     def _norm(self, x, gamma):
         return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.cfg.eps) * gamma
 
     def _rope(self, x, heads, cos, sin):
         s, d = x.shape[0], self.cfg.head_dim
-        v = x.view(s, heads, d)
+        v = x.contiguous().view(s, heads, d)
         a, b = v[..., : d // 2], v[..., d // 2:]
         c, sn = cos[:, None, :], sin[:, None, :]
         return torch.cat((a * c - b * sn, b * c + a * sn), dim=-1).reshape(s, heads * d)
@@ -133,59 +156,71 @@ class CudaDecoder:
         """q [S, H*d] against the layer's cache; mask [S, max_seq] True where a key is visible."""
         cfg = self.cfg
         s, d, hkv = q.shape[0], cfg.head_dim, cfg.kv_heads
-        qv = q.view(s, hkv, cfg.heads // hkv, d).permute(1, 2, 0, 3)           # [Hkv, G, S, d]
+        qv = q.reshape(s, hkv, cfg.heads // hkv, d).permute(1, 2, 0, 3)         # [Hkv, G, S, d]
         sc = torch.matmul(qv, self.kc[li].unsqueeze(1).transpose(-1, -2)) / float(np.sqrt(d))  # [Hkv, G, S, T]
         sc = sc.masked_fill(~mask, float("-inf"))
         p = torch.softmax(sc, dim=-1)
         out = torch.matmul(p, self.vc[li].unsqueeze(1))                          # [Hkv, G, S, d]
         return out.permute(2, 0, 1, 3).reshape(s, cfg.heads * d)
 
-    def _block(self, x, li, cos, sin, write, mask, path):
-        cfg, lw = self.cfg, self.layers[li]
-        h = self._norm(x, lw["norm_attn"])
-        q = self._rope(lw["q"].matmul(h, path=path), cfg.heads, cos, sin)
-        k = self._rope(lw["k"].matmul(h, path=path), cfg.kv_heads, cos, sin)
-        v = lw["v"].matmul(h, path=path)
-        s = x.shape[0]
-        write(self.kc[li], k.view(s, cfg.kv_heads, cfg.head_dim).transpose(0, 1))
-        write(self.vc[li], v.view(s, cfg.kv_heads, cfg.head_dim).transpose(0, 1))
-        x = x + lw["o"].matmul(self._attend(q, li, mask), path=path)
-        h = self._norm(x, lw["norm_mlp"])
-        act = torch.nn.functional.silu(lw["gate"].matmul(h, path=path)) * lw["up"].matmul(h, path=path)
-        return x + lw["down"].matmul(act, path=path)
-
-    # ---- passes
     def prefill(self, tokens: torch.Tensor, path: int = N.PATH_AUTO) -> torch.Tensor:
         """Runs the prompt from position 0; returns the last position's logits [vocab]."""
+        cfg = self.cfg
         s = tokens.shape[0]
         cos, sin = self.cos[:s], self.sin[:s]
         mask = self.keys[None, :] <= torch.arange(s, device=self.device)[:, None]
-
-        def write(cache, kv):  # kv [Hkv, S, d] at positions 0..S-1
-            cache[:, :s].copy_(kv)
-
         x = self.embed[tokens]
-        for li in range(self.cfg.layers):
-            x = self._block(x, li, cos, sin, write, mask, path)
+        for li, lw in enumerate(self.layers):
+            h = self._norm(x, lw["norm_attn"])
+            qkv = lw["qkv"].matmul(h, path=path)
+            q = self._rope(qkv[:, :self.n_q], cfg.heads, cos, sin)
+            k = self._rope(qkv[:, self.n_q:self.n_q + self.n_kv], cfg.kv_heads, cos, sin)
+            v = qkv[:, self.n_q + self.n_kv:]
+            self.kc[li][:, :s].copy_(k.reshape(s, cfg.kv_heads, cfg.head_dim).transpose(0, 1))
+            self.vc[li][:, :s].copy_(v.reshape(s, cfg.kv_heads, cfg.head_dim).transpose(0, 1))
+            x = x + lw["o"].matmul(self._attend(q, li, mask), path=path)
+            h = self._norm(x, lw["norm_mlp"])
+            gu = lw["gate_up"].matmul(h, path=path)
+            act = torch.nn.functional.silu(gu[:, :cfg.inter]) * gu[:, cfg.inter:]
+            x = x + lw["down"].matmul(act, path=path)
         return self.lm_head.matmul(self._norm(x[-1:], self.norm_final), path=path)[0]
 
+    # ---- fused decode step
     def decode_step(self, tok: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
         """One token: tok [1] (int64) at position pos [1] (int64), both on the device; writes
-        the argmax into tok, advances pos and returns the logits [vocab]. Only device tensors
-        change, so the step can be captured in a CUDA graph and replayed."""
-        cos, sin = self.cos[pos], self.sin[pos]
-        mask = (self.keys <= pos)[None, :]
+        the argmax into tok, advances pos and returns the logits [vocab]. Only device memory
+        changes, so the step can be captured in a CUDA graph and replayed."""
+        cfg, lib = self.cfg, N.lib()
+        st = torch.cuda.current_stream(self.device).cuda_stream
 
-        def write(cache, kv):  # kv [Hkv, 1, d] at position pos
-            cache.index_copy_(1, pos, kv)
+        def ok(rc, what):
+            if rc:
+                N.check(rc, what)
 
-        x = self.embed[tok]
-        for li in range(self.cfg.layers):
-            x = self._block(x, li, cos, sin, write, mask, N.PATH_GEMV)
-        logits = self.lm_head.matmul(self._norm(x, self.norm_final))[0]
-        tok.copy_(torch.argmax(logits).view(1))
-        pos.add_(1)
-        return logits
+        torch.index_select(self.embed, 0, tok, out=self.bx)
+        delta = None
+        for li, lw in enumerate(self.layers):
+            ok(lib.msq_add_rmsnorm(None, st, self.bx.data_ptr(), delta, lw["norm_attn"].data_ptr(), self.bh.data_ptr(),
+                                   1, cfg.hidden, cfg.eps), "msq_add_rmsnorm")
+            lw["qkv"].matmul(self.bh, out=self.bqkv, path=N.PATH_GEMV)
+            ok(lib.msq_rope_append(None, st, self.bqkv.data_ptr(), cfg.heads, cfg.kv_heads, cfg.head_dim,
+                                   self.cos.data_ptr(), self.sin.data_ptr(), pos.data_ptr(), self.kc[li].data_ptr(),
+                                   self.vc[li].data_ptr(), cfg.max_seq), "msq_rope_append")
+            ok(lib.msq_gqa_decode(None, st, self.bqkv.data_ptr(), self.kc[li].data_ptr(), self.vc[li].data_ptr(),
+                                  pos.data_ptr(), self.battn.data_ptr(), cfg.heads, cfg.kv_heads, cfg.head_dim,
+                                  cfg.max_seq), "msq_gqa_decode")
+            lw["o"].matmul(self.battn, out=self.bo, path=N.PATH_GEMV)
+            ok(lib.msq_add_rmsnorm(None, st, self.bx.data_ptr(), self.bo.data_ptr(), lw["norm_mlp"].data_ptr(),
+                                   self.bh.data_ptr(), 1, cfg.hidden, cfg.eps), "msq_add_rmsnorm")
+            lw["gate_up"].matmul(self.bh, out=self.bgu, path=N.PATH_GEMV)
+            ok(lib.msq_swiglu(None, st, self.bgu.data_ptr(), self.bact.data_ptr(), cfg.inter), "msq_swiglu")
+            lw["down"].matmul(self.bact, out=self.bdown, path=N.PATH_GEMV)
+            delta = self.bdown.data_ptr()
+        ok(lib.msq_add_rmsnorm(None, st, self.bx.data_ptr(), delta, self.norm_final.data_ptr(), self.bh.data_ptr(),
+                               1, cfg.hidden, cfg.eps), "msq_add_rmsnorm")
+        self.lm_head.matmul(self.bh, out=self.blogits, path=N.PATH_GEMV)
+        ok(lib.msq_argmax(None, st, self.blogits.data_ptr(), cfg.vocab, tok.data_ptr(), pos.data_ptr()), "msq_argmax")
+        return self.blogits[0]
 
     def generate(self, prompt: torch.Tensor, n_new: int, path: int = N.PATH_AUTO) -> torch.Tensor:
         """Greedy: the prompt in one pass, then n_new - 1 decode steps; the new tokens [n_new]."""
@@ -200,6 +235,6 @@ class CudaDecoder:
 
     def free(self) -> None:
         for lw in self.layers:
-            for name in PROJ:
+            for name in ("qkv", "o", "gate_up", "down"):
                 lw[name].free()
         self.lm_head.free()
