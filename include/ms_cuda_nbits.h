@@ -218,6 +218,29 @@ int msq_wait_gathered(void* cu_ctx, void* stream, const msq_wait_t* wait);
  * device memory). Not part of the reference's C ABI: each restates one of the reference's CPU
  * graph kernels (cited per entry).                                                      */
 
+/* The decode GEMV (M <= 16) with the glue on either side folded in: no counterpart in the
+ * reference (whose graph runs these as separate nodes: SimplifiedLayerNormalization before
+ * MatMulNBits, Sigmoid/Mul before the down projection, Add after). With
+ *   rms_gamma != NULL  A rows are RMSNorm inputs x; the GEMV computes
+ *                      (x / sqrt(mean(x^2) + rms_eps) * gamma) . W^T
+ *                      (SimplifiedLayerNormalizationKernel.cs:48-54 then MatMulNBits);
+ *   swiglu != 0        A rows are [gate | up] of 2K floats; the GEMV computes
+ *                      (gate / (1 + exp(-gate)) * up) . W^T;
+ *   accumulate != 0    Y += result (a residual add) instead of Y = result.
+ * rms_gamma and swiglu are exclusive. fp32 A only; MSQ_E_UNSUPPORTED unless the weights take
+ * the decode GEMV (bits 4, block_size 32 / 64 / 128), K % 4 == 0 and A and gamma are 16-byte
+ * aligned. Agreement with the unfused chain is to fp32 rounding (the norm's scale is applied
+ * to the dot product rather than to each element).                                       */
+typedef struct msq_fusion {
+  const float* rms_gamma;
+  float rms_eps;
+  int32_t swiglu;
+  int32_t accumulate;
+} msq_fusion_t;
+
+int msq_matmul_fused(void* cu_ctx, void* stream, msq_weights_t w, const float* d_a, int64_t M,
+                     float* d_y, int64_t ldy, const msq_fusion_t* fusion);
+
 /* x[r] <- x[r] + delta[r] (delta may be NULL); y[r] <- x[r] / sqrt(mean(x[r]^2) + eps) * gamma,
  * for rows r < rows of n floats (SkipSimplifiedLayerNormalizationKernel.cs:64-67,
  * SimplifiedLayerNormalizationKernel.cs:48-54).                                         */

@@ -40,6 +40,13 @@ class GatherT(C.Structure):
 class WaitT(C.Structure):
     """msq_wait_t: a gathered input to wait for."""
     _fields_ = [("arrivals", C.c_void_p), ("produced", C.c_void_p), ("nranks", C.c_int)]
+
+
+class FusionT(C.Structure):
+    """msq_fusion_t: glue folded into a decode GEMV."""
+    _fields_ = [("rms_gamma", C.c_void_p), ("rms_eps", C.c_float), ("swiglu", C.c_int32), ("accumulate", C.c_int32)]
+
+
 PACK_DEFAULT, PACK_GENERIC_ONLY = 0, 1
 
 LIB_NAME = "libms_cuda_nbits.so"
@@ -80,6 +87,7 @@ SIGNATURES: dict[str, tuple] = {
     "msq_gqa_decode": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i64]),
     "msq_swiglu": (_i32, [_vp, _vp, _vp, _vp, _i64]),
     "msq_argmax": (_i32, [_vp, _vp, _vp, _i64, _vp, _vp]),
+    "msq_matmul_fused": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, C.POINTER(FusionT)]),
     "msq_qgemm_nbits": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32]),
 }
 

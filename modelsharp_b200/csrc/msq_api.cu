@@ -636,6 +636,41 @@ int msq_matmul_gather(void* cu_ctx, void* stream, msq_weights_t h, const void* d
   return run_gemv_gather(static_cast<cudaStream_t>(stream), *w, d_a, a_dtype, M, wait, gather);
 }
 
+int msq_matmul_fused(void* cu_ctx, void* stream, msq_weights_t h, const float* d_a, int64_t M, float* d_y,
+                     int64_t ldy, const msq_fusion_t* fusion) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  Weights* w = reinterpret_cast<Weights*>(h);
+  if (!w) return fail(MSQ_E_INVALID, "msq_matmul_fused: NULL weights handle");
+  if (!fusion) return fail(MSQ_E_INVALID, "msq_matmul_fused: NULL fusion");
+  if (fusion->rms_gamma && fusion->swiglu)
+    return fail(MSQ_E_INVALID, "msq_matmul_fused: RMSNorm and SwiGLU inputs are exclusive");
+  if (M < 0) return fail(MSQ_E_INVALID, "msq_matmul_fused: negative M (%lld)", (long long)M);
+  if (ldy < w->n_rows) return fail(MSQ_E_INVALID, "msq_matmul_fused: ldy %lld < rows %d", (long long)ldy, w->n_rows);
+  if (M == 0) return MSQ_OK;
+  if (!d_a || !d_y) return fail(MSQ_E_INVALID, "msq_matmul_fused: NULL device pointer");
+  if (!w->fast4 || !w->strm || M > 16 || w->K % 4 ||
+      ((uintptr_t)d_a | (uintptr_t)fusion->rms_gamma) & 15)
+    return fail(MSQ_E_UNSUPPORTED,
+                "msq_matmul_fused needs the decode GEMV (bits 4, block_size 32/64/128, M <= 16), K %% 4 == 0 and "
+                "16-byte aligned A and gamma");
+  int dev;
+  int rc = current_device(&dev);
+  if (rc != MSQ_OK) return rc;
+  if (dev != w->device)
+    return fail(MSQ_E_INVALID, "weights handle lives on device %d but the current device is %d", w->device, dev);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  refresh_settled(*w, st);
+  Fusion f;
+  f.gamma = fusion->rms_gamma;
+  f.eps = fusion->rms_eps;
+  f.swiglu = fusion->swiglu ? 1 : 0;
+  f.accumulate = fusion->accumulate ? 1 : 0;
+  rc = run_gemv_fused(st, *w, d_a, M, d_y, ldy, f);
+  if (rc == MSQ_E_UNSUPPORTED) return fail(rc, "msq_matmul_fused: these weights do not fit the decode GEMV");
+  return rc;
+}
+
 int msq_wait_gathered(void* cu_ctx, void* stream, const msq_wait_t* wait) {
   CtxGuard g(cu_ctx);
   if (g.rc != MSQ_OK) return g.rc;

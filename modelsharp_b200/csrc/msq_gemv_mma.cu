@@ -53,6 +53,14 @@ struct Args {
   int kpp;    // row pitch of the digit array: kp + 16 bytes (column c starts 4c banks later)
   int a_vec;  // rows of A may be read 4 elements at a time
   int prefetch;  // weights settled: stream them before the programmatic-dependency wait
+  int64_t lda;   // row stride of A in elements (K, or 2K for the SwiGLU form)
+  // decode-step fusions (fp32 A, a_vec only): A row = RMSNorm input x, a = x * gamma and the
+  // output scaled by 1 / sqrt(mean(x^2) + eps); or A row = [gate | up], a = silu(gate) * up;
+  // and Y += result instead of Y = result
+  const float* gamma;
+  float eps;
+  int swiglu;
+  int accumulate;
   int off_dig, off_s, off_ysum, off_bar, off_ring;  // shared-memory offsets (bytes)
   // column-split exchange (the XG kernels): outputs to every rank's full-Y buffer
   int nranks;
@@ -123,10 +131,19 @@ __device__ __forceinline__ void imma(int (&c)[4], uint32_t a0, uint32_t a1, uint
 }
 
 // A[m0 + m][k .. k+3] as fp32, zeros past K.
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + expf(-g)) * u; }
+
+template <bool FU>
 __device__ __forceinline__ float4 load4(const Args& p, int m, int k) {
-  const int64_t base = (p.m0 + m) * (int64_t)p.K + k;
+  const int64_t base = (p.m0 + m) * (FU ? p.lda : (int64_t)p.K) + k;
   if (p.a_vec && k + 4 <= p.K) {
-    if (p.a_dtype == MSQ_DT_F32) return *reinterpret_cast<const float4*>(static_cast<const float*>(p.a) + base);
+    if (p.a_dtype == MSQ_DT_F32) {
+      const float* ap = static_cast<const float*>(p.a) + base;
+      const float4 v = *reinterpret_cast<const float4*>(ap);
+      if (!FU || !p.swiglu) return v;
+      const float4 u = *reinterpret_cast<const float4*>(ap + p.K);  // the up half of the row
+      return make_float4(silu_mul(v.x, u.x), silu_mul(v.y, u.y), silu_mul(v.z, u.z), silu_mul(v.w, u.w));
+    }
     const uint2 r = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.a) + base);
     float2 lo, hi;
     if (p.a_dtype == MSQ_DT_F16) {
@@ -184,10 +201,11 @@ __device__ __forceinline__ float exp2i(int s) { return __int_as_float((s + 127) 
 
 // BS = quantisation block size (32 / 64 / 128); NT = n8 tiles of B (1: M <= 2, 2: M <= 4);
 // XG = the column-split form (outputs to every rank's full-Y buffer, optional wait for a
-// gathered input). A "unit" is max(BS, 64) k: one or two 64-k chunks (a uint4 of code words
+// gathered input); FU = the decode-step fusion forms (RMSNorm / SwiGLU input, accumulate). A "unit" is max(BS, 64) k: one or two 64-k chunks (a uint4 of code words
 // per lane each).
-template <int BS, int NT, bool XG>
+template <int BS, int NT, bool XG, bool FU>
 __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
+  static_assert(!(XG && FU), "the column-split form takes no fusion");
   constexpr int UNIT = BS > 64 ? BS : 64;
   constexpr int CH = UNIT / 64;     // 64-k chunks per unit
   constexpr int UB = UNIT / BS;     // blocks per unit
@@ -199,6 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
   int* sblk = reinterpret_cast<int*>(smem + p.off_s);         // [mc][kp/BS] exact block sums of a_int
   float* sinv = reinterpret_cast<float*>(sblk + p.mc * (p.kp / BS));  // [mc][kp/BS] 2^-sigma_b
   float* ysum = reinterpret_cast<float*>(smem + p.off_ysum);  // [rows_cta][mc][33]: per warp
+  float* rowsq = reinterpret_cast<float*>(smem + 64);         // [kConsumers][kMaxM] sums of x^2
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bar);
   uint64_t* empty = full + kMaxSlots;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kMaxSlots);
@@ -278,6 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
   constexpr int GL = BS / 4;  // float4 per quantisation block (8 / 16 / 32 lanes)
   const int n4row = p.kp / 4;
   const int n4 = mc * n4row;
+  float ssq[kMaxM] = {};  // RMSNorm form: this thread's share of sum x^2 per A row
   for (int base = 0; base < n4; base += kC * U) {
     const int nu = min(U, (n4 - base + kC - 1) / kC);  // warp-uniform
     float4 v[U];
@@ -285,7 +305,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
     for (int u = 0; u < U; ++u) {
       const int f = base + tid + u * kC;
       const int m = f / n4row;
-      v[u] = (u < nu && f < n4) ? load4(p, m, 4 * (f - m * n4row)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[u] = (u < nu && f < n4) ? load4<FU>(p, m, 4 * (f - m * n4row)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (FU && p.gamma) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int f = base + tid + u * kC;
+        const int m = f / n4row, k = 4 * (f - m * n4row);
+        if (u < nu && f < n4 && k < p.K) {  // K % 4 == 0 here: a float4 is all in or all out
+          const float sq = fmaf(v[u].x, v[u].x, fmaf(v[u].y, v[u].y, fmaf(v[u].z, v[u].z, v[u].w * v[u].w)));
+#pragma unroll
+          for (int j = 0; j < kMaxM; ++j) ssq[j] += m == j ? sq : 0.f;
+          const float4 g = *reinterpret_cast<const float4*>(p.gamma + k);
+          v[u] = make_float4(v[u].x * g.x, v[u].y * g.y, v[u].z * g.z, v[u].w * g.w);
+        }
+      }
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -315,6 +349,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
           sinv[f / GL] = exp2i(-sh);
         }
       }
+    }
+  }
+  if (FU && p.gamma) {  // per-warp sums of x^2 per row, in a fixed order
+#pragma unroll
+    for (int j = 0; j < kMaxM; ++j) {
+      float v = ssq[j];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      if (lane == 0) rowsq[warp * kMaxM + j] = v;
     }
   }
   ptx::named_bar_sync(1, kConsumers * 32);
@@ -495,7 +538,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
         if constexpr (XG) {
           for (int r = 0; r < p.nranks; ++r) p.gy[r][(p.m0 + m) * p.gldy + p.gcol0 + row] = acc;
         } else {
-          p.y[(p.m0 + m) * p.ldy + row] = acc;
+          float* yp = p.y + (p.m0 + m) * p.ldy + row;
+          if constexpr (FU) {
+            if (p.gamma) {
+              float t = 0.f;
+#pragma unroll
+              for (int q = 0; q < kConsumers; ++q) t += rowsq[q * kMaxM + m];
+              acc *= 1.0f / sqrtf(t / (float)p.K + p.eps);
+            }
+            if (p.accumulate) acc += *yp;
+          }
+          *yp = acc;
         }
       }
     }
@@ -525,9 +578,9 @@ __global__ void wait_gathered_kernel(const unsigned long long* arr, const unsign
   if (threadIdx.x == 0) wait_arrivals(arr, prod, nranks);
 }
 
-template <int BS, int NT, bool XG>
+template <int BS, int NT, bool XG, bool FU>
 int launch(cudaStream_t st, const Args& a, int grid, size_t smem) {
-  auto kern = gemv_mma_kernel<BS, NT, XG>;
+  auto kern = gemv_mma_kernel<BS, NT, XG, FU>;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -575,9 +628,9 @@ size_t plan_smem(const Weights& w, int mc, int grid, Args& a) {
   return (size_t)a.off_ring + (size_t)slots * w.stage_bytes;
 }
 
-template <int BS, bool XG>
+template <int BS, bool XG, bool FU = false>
 int launch_nt(cudaStream_t st, const Args& a, int grid, size_t smem) {
-  return a.mc <= 2 ? launch<BS, 1, XG>(st, a, grid, smem) : launch<BS, 2, XG>(st, a, grid, smem);
+  return a.mc <= 2 ? launch<BS, 1, XG, FU>(st, a, grid, smem) : launch<BS, 2, XG, FU>(st, a, grid, smem);
 }
 
 }  // namespace
@@ -587,7 +640,7 @@ namespace {
 // One decode GEMV call: passes of up to 4 A rows; with `g` (column split) a single pass
 // whose outputs go to every rank's full-Y buffer, after waiting for `wt` (or nothing).
 int gemv_impl(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M, float* d_y,
-              int64_t ldy, const msq_wait_t* wt, const msq_gather_t* g) {
+              int64_t ldy, const msq_wait_t* wt, const msq_gather_t* g, const Fusion* fu = nullptr) {
   if (!w.strm || (w.block_size != 32 && w.block_size != 64 && w.block_size != 128)) return MSQ_E_UNSUPPORTED;
   const int unit = w.block_size > 64 ? w.block_size : 64;
   if (w.kt / unit > kUpw * kConsumers) return MSQ_E_UNSUPPORTED;
@@ -617,6 +670,15 @@ int gemv_impl(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, i
       const uintptr_t ap = reinterpret_cast<uintptr_t>(d_a);
       const int align = a_dtype == MSQ_DT_F32 ? 16 : 8;
       a.a_vec = (w.K % 4 == 0) && (ap % align == 0);
+    }
+    a.lda = w.K;
+    if (fu) {
+      if (!a.a_vec || a_dtype != MSQ_DT_F32 || g) return MSQ_E_UNSUPPORTED;
+      a.gamma = fu->gamma;
+      a.eps = fu->eps;
+      a.swiglu = fu->swiglu;
+      a.accumulate = fu->accumulate;
+      if (fu->swiglu) a.lda = 2 * (int64_t)w.K;
     }
     if (g) {
       a.nranks = g->nranks;
@@ -659,6 +721,12 @@ int gemv_impl(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, i
         case 64: rc = launch_nt<64, true>(st, a, grid, smem); break;
         default: rc = launch_nt<128, true>(st, a, grid, smem); break;
       }
+    } else if (fu) {
+      switch (w.block_size) {
+        case 32: rc = launch_nt<32, false, true>(st, a, grid, smem); break;
+        case 64: rc = launch_nt<64, false, true>(st, a, grid, smem); break;
+        default: rc = launch_nt<128, false, true>(st, a, grid, smem); break;
+      }
     } else {
       switch (w.block_size) {
         case 32: rc = launch_nt<32, false>(st, a, grid, smem); break;
@@ -669,7 +737,7 @@ int gemv_impl(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, i
     if (rc != MSQ_OK) return rc;
     m0 += mc;
   }
-  note_path(g ? "gemv_imma_gather" : M <= 4 ? "gemv_imma" : "gemv_imma_multipass");
+  note_path(g ? "gemv_imma_gather" : fu ? "gemv_imma_fused" : M <= 4 ? "gemv_imma" : "gemv_imma_multipass");
   return MSQ_OK;
 }
 
@@ -683,6 +751,11 @@ int run_gemv_mma(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype
 int run_gemv_gather(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M,
                     const msq_wait_t* wt, const msq_gather_t* g) {
   return gemv_impl(st, w, d_a, a_dtype, M, nullptr, 0, wt, g);
+}
+
+int run_gemv_fused(cudaStream_t st, const Weights& w, const float* d_a, int64_t M, float* d_y, int64_t ldy,
+                   const Fusion& f) {
+  return gemv_impl(st, w, d_a, MSQ_DT_F32, M, d_y, ldy, nullptr, nullptr, &f);
 }
 
 int run_wait_gathered(cudaStream_t st, const msq_wait_t* wt) {

@@ -104,6 +104,15 @@ int run_gemv_mma(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype
 int run_gemv_gather(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M,
                     const msq_wait_t* wt, const msq_gather_t* g);
 int run_wait_gathered(cudaStream_t st, const msq_wait_t* wt);
+// The decode GEMV with decode-step fusions (fp32 A, K % 4 == 0, 16-byte aligned A and gamma).
+struct Fusion {
+  const float* gamma = nullptr;  // RMSNorm of each A row folded in (scale per row, gamma per k)
+  float eps = 0.f;
+  int swiglu = 0;                // A rows are [gate | up] of 2K: a = silu(gate) * up
+  int accumulate = 0;            // Y += result
+};
+int run_gemv_fused(cudaStream_t st, const Weights& w, const float* d_a, int64_t M, float* d_y, int64_t ldy,
+                   const Fusion& f);
 int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t M,
              float* d_y, int64_t ldy);
 void release_gemm_state(Weights& w);

@@ -101,8 +101,9 @@ class CudaDecoder:
 
     q/k/v are packed into one weight (N = (H + 2 Hkv) d) and gate/up into another (N = 2 I), as
     packed-QKV exports do, so a layer runs four MatMulNBits. The prompt pass uses torch glue;
-    a decode step uses the library's fused glue (add + RMSNorm, rotary + KV append, GQA decode,
-    SwiGLU, argmax), every launch chained with programmatic dependent launch."""
+    a decode step folds RMSNorm, SwiGLU and the residual adds into its GEMVs and uses the
+    library's rotary + KV append, GQA decode and argmax kernels, every launch chained with
+    programmatic dependent launch."""
 
     def __init__(self, cfg: DecoderConfig, weights: dict, device: torch.device | str):
         self.cfg = cfg
@@ -135,11 +136,10 @@ class CudaDecoder:
         self.keys = torch.arange(cfg.max_seq, device=dev)
         # decode-step buffers (fixed addresses, so a captured step can be replayed)
         f = dict(device=dev, dtype=torch.float32)
-        self.bx, self.bh = torch.empty(1, cfg.hidden, **f), torch.empty(1, cfg.hidden, **f)
+        self.bx = torch.empty(1, cfg.hidden, **f)
         self.bqkv = torch.empty(1, self.n_q + 2 * self.n_kv, **f)
-        self.battn, self.bo = torch.empty(1, self.n_q, **f), torch.empty(1, cfg.hidden, **f)
-        self.bgu, self.bact = torch.empty(1, 2 * cfg.inter, **f), torch.empty(1, cfg.inter, **f)
-        self.bdown, self.blogits = torch.empty(1, cfg.hidden, **f), torch.empty(1, cfg.vocab, **f)
+        self.battn = torch.empty(1, self.n_q, **f)
+        self.bgu, self.blogits = torch.empty(1, 2 * cfg.inter, **f), torch.empty(1, cfg.vocab, **f)
 
     # ---- torch glue (prompt pass)
     def _norm(self, x, gamma):
@@ -189,7 +189,11 @@ class CudaDecoder:
     def decode_step(self, tok: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
         """One token: tok [1] (int64) at position pos [1] (int64), both on the device; writes
         the argmax into tok, advances pos and returns the logits [vocab]. Only device memory
-        changes, so the step can be captured in a CUDA graph and replayed."""
+        changes, so the step can be captured in a CUDA graph and replayed.
+
+        Per layer six launches: q/k/v GEMV with the attention RMSNorm folded in, rotary + KV
+        append, GQA, o GEMV adding into the residual, gate/up GEMV with the MLP RMSNorm folded
+        in, down GEMV taking SwiGLU of its input and adding into the residual."""
         cfg, lib = self.cfg, N.lib()
         st = torch.cuda.current_stream(self.device).cuda_stream
 
@@ -198,27 +202,18 @@ class CudaDecoder:
                 N.check(rc, what)
 
         torch.index_select(self.embed, 0, tok, out=self.bx)
-        delta = None
         for li, lw in enumerate(self.layers):
-            ok(lib.msq_add_rmsnorm(None, st, self.bx.data_ptr(), delta, lw["norm_attn"].data_ptr(), self.bh.data_ptr(),
-                                   1, cfg.hidden, cfg.eps), "msq_add_rmsnorm")
-            lw["qkv"].matmul(self.bh, out=self.bqkv, path=N.PATH_GEMV)
+            lw["qkv"].matmul_fused(self.bx, self.bqkv, rms_gamma=lw["norm_attn"], rms_eps=cfg.eps, stream=st)
             ok(lib.msq_rope_append(None, st, self.bqkv.data_ptr(), cfg.heads, cfg.kv_heads, cfg.head_dim,
                                    self.cos.data_ptr(), self.sin.data_ptr(), pos.data_ptr(), self.kc[li].data_ptr(),
                                    self.vc[li].data_ptr(), cfg.max_seq), "msq_rope_append")
             ok(lib.msq_gqa_decode(None, st, self.bqkv.data_ptr(), self.kc[li].data_ptr(), self.vc[li].data_ptr(),
                                   pos.data_ptr(), self.battn.data_ptr(), cfg.heads, cfg.kv_heads, cfg.head_dim,
                                   cfg.max_seq), "msq_gqa_decode")
-            lw["o"].matmul(self.battn, out=self.bo, path=N.PATH_GEMV)
-            ok(lib.msq_add_rmsnorm(None, st, self.bx.data_ptr(), self.bo.data_ptr(), lw["norm_mlp"].data_ptr(),
-                                   self.bh.data_ptr(), 1, cfg.hidden, cfg.eps), "msq_add_rmsnorm")
-            lw["gate_up"].matmul(self.bh, out=self.bgu, path=N.PATH_GEMV)
-            ok(lib.msq_swiglu(None, st, self.bgu.data_ptr(), self.bact.data_ptr(), cfg.inter), "msq_swiglu")
-            lw["down"].matmul(self.bact, out=self.bdown, path=N.PATH_GEMV)
-            delta = self.bdown.data_ptr()
-        ok(lib.msq_add_rmsnorm(None, st, self.bx.data_ptr(), delta, self.norm_final.data_ptr(), self.bh.data_ptr(),
-                               1, cfg.hidden, cfg.eps), "msq_add_rmsnorm")
-        self.lm_head.matmul(self.bh, out=self.blogits, path=N.PATH_GEMV)
+            lw["o"].matmul_fused(self.battn, self.bx, accumulate=True, stream=st)
+            lw["gate_up"].matmul_fused(self.bx, self.bgu, rms_gamma=lw["norm_mlp"], rms_eps=cfg.eps, stream=st)
+            lw["down"].matmul_fused(self.bgu, self.bx, swiglu=True, accumulate=True, stream=st)
+        self.lm_head.matmul_fused(self.bx, self.blogits, rms_gamma=self.norm_final, rms_eps=cfg.eps, stream=st)
         ok(lib.msq_argmax(None, st, self.blogits.data_ptr(), cfg.vocab, tok.data_ptr(), pos.data_ptr()), "msq_argmax")
         return self.blogits[0]
 

@@ -112,6 +112,24 @@ class QuantizedWeights:
         N.check(rc, "msq_matmul")
         return out
 
+    def matmul_fused(self, a: torch.Tensor, out: torch.Tensor, rms_gamma: torch.Tensor | None = None,
+                     rms_eps: float = 1e-5, swiglu: bool = False, accumulate: bool = False,
+                     stream: int | None = None) -> torch.Tensor:
+        """The decode GEMV with glue folded in (msq_matmul_fused): A rows normalised by RMSNorm
+        with `rms_gamma`, or A rows [gate | up] of 2K through SwiGLU; `accumulate` adds the
+        product into `out`. fp32, M <= 16; enqueued, not synchronized."""
+        kin = 2 * self.K if swiglu else self.K
+        if a.dtype != torch.float32 or not a.is_cuda or a.shape[-1] != kin:
+            raise ModelSharpException(f"matmul_fused expects a CUDA float32 A with rows of {kin}")
+        a = a.contiguous()
+        f = N.FusionT(rms_gamma.data_ptr() if rms_gamma is not None else None, rms_eps, int(swiglu), int(accumulate))
+        with torch.cuda.device(a.device):
+            st = current_stream_ptr(a.device) if stream is None else stream
+            rc = N.lib().msq_matmul_fused(None, st, self.handle, a.data_ptr(), a.numel() // kin, out.data_ptr(),
+                                          out.stride(-2) if out.dim() >= 2 else self.n_rows, C.byref(f))
+        N.check(rc, "msq_matmul_fused")
+        return out
+
     def matmul_host(self, a: np.ndarray | torch.Tensor) -> np.ndarray:
         """Host buffers in and out (copies inside the call), synchronous."""
         at = as_torch(a).contiguous()
