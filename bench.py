@@ -755,11 +755,15 @@ def run_decode(args, rank: int, world: int, local_rank: int):
                 pos.fill_(n_prompt)
                 out[r, 0] = tok[0]
                 e1.record(stream)
+                if r == 0:  # the first generation's decode steps are what `ncu --profile-from-start off` sees
+                    torch.cuda.profiler.start()
                 for i in range(1, n_new):
                     g.replay()
                     out[r, i] = tok[0]
                 e2.record(stream)
             stream.synchronize()
+            if r == 0:
+                torch.cuda.profiler.stop()
             pre_ms += e0.elapsed_time(e1)
             dec_ms += e1.elapsed_time(e2)
     launches = N.launch_count() - launches0 + reps * (n_new - 1) * per_replay  # prompt passes + replays

@@ -257,11 +257,19 @@ int msq_rope_append(void* cu_ctx, void* stream, float* qkv, int heads, int kv_he
 /* out[h] = softmax(q[h] . K[g]^T / sqrt(d)) . V[g] over cache rows 0..*d_pos, g = h / (heads /
  * kv_heads) (GroupQueryAttentionKernel.cs:194-195, 275-312). A position past the cache reads
  * all max_seq rows. MSQ_E_UNSUPPORTED unless heads / kv_heads <= 8, d <= 256 with d % 4 == 0,
- * q and the caches 16-byte aligned, and max_seq fits the shared-memory plan (max_seq 2^15
- * at 4 query heads per kv head).                                                           */
+ * and q and the caches are 16-byte aligned.                                               */
 int msq_gqa_decode(void* cu_ctx, void* stream, const float* q, const float* kcache,
                    const float* vcache, const int64_t* d_pos, float* out, int heads, int kv_heads,
                    int d, int64_t max_seq);
+
+/* msq_rope_append followed by msq_gqa_decode in one launch: qkv = [q | k | v] of the token
+ * at position *d_pos, unrotated (and left unchanged); q and k are rotated, k and v written to
+ * cache row *d_pos, out = attention of the rotated q over rows 0..*d_pos. A position outside
+ * the cache writes nothing and attends with q unrotated over the rows 0..max_seq-1 (as the two
+ * separate entries do). Also needs d a power of two >= 8 and 16-byte aligned tables.        */
+int msq_rope_gqa_decode(void* cu_ctx, void* stream, const float* qkv, int heads, int kv_heads,
+                        int d, const float* cos_t, const float* sin_t, const int64_t* d_pos,
+                        float* kcache, float* vcache, float* out, int64_t max_seq);
 
 /* gate_up = [gate (n) | up (n)]: out = gate / (1 + exp(-gate)) * up.                     */
 int msq_swiglu(void* cu_ctx, void* stream, const float* gate_up, float* out, int64_t n);

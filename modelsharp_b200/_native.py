@@ -85,6 +85,7 @@ SIGNATURES: dict[str, tuple] = {
     "msq_add_rmsnorm": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, C.c_float]),
     "msq_rope_append": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _i64]),
     "msq_gqa_decode": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i64]),
+    "msq_rope_gqa_decode": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64]),
     "msq_swiglu": (_i32, [_vp, _vp, _vp, _vp, _i64]),
     "msq_argmax": (_i32, [_vp, _vp, _vp, _i64, _vp, _vp]),
     "msq_matmul_fused": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, C.POINTER(FusionT)]),

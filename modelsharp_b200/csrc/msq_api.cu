@@ -703,21 +703,47 @@ int msq_rope_append(void* cu_ctx, void* stream, float* qkv, int heads, int kv_he
                          vcache, max_seq);
 }
 
+namespace {
+int check_gqa(const char* fn, int heads, int kv_heads, int d, int64_t max_seq, const void* q, const void* kc,
+              const void* vc) {
+  if (heads < 1 || kv_heads < 1 || heads % kv_heads || d < 1 || max_seq < 1 || max_seq > 0x7fffffff)
+    return fail(MSQ_E_INVALID, "%s: heads %d, kv_heads %d, d %d, max_seq %lld", fn, heads, kv_heads, d,
+                (long long)max_seq);
+  if (heads / kv_heads > 8 || d > 256 || (d & 3) || ((uintptr_t)q | (uintptr_t)kc | (uintptr_t)vc) & 15)
+    return fail(MSQ_E_UNSUPPORTED,
+                "%s: needs heads / kv_heads <= 8, d <= 256 and a multiple of 4, 16-byte aligned q and caches "
+                "(heads %d, kv_heads %d, d %d)", fn, heads, kv_heads, d);
+  if (gqa_decode_smem(heads, kv_heads, d) > 200 * 1024)
+    return fail(MSQ_E_UNSUPPORTED, "%s: d %d with %d query heads per kv head exceeds the shared-memory plan", fn, d,
+                heads / kv_heads);
+  return MSQ_OK;
+}
+}  // namespace
+
 int msq_gqa_decode(void* cu_ctx, void* stream, const float* q, const float* kcache, const float* vcache,
                    const int64_t* d_pos, float* out, int heads, int kv_heads, int d, int64_t max_seq) {
   CtxGuard g(cu_ctx);
   if (g.rc != MSQ_OK) return g.rc;
   if (!q || !kcache || !vcache || !d_pos || !out) return fail(MSQ_E_INVALID, "msq_gqa_decode: NULL pointer");
-  if (heads < 1 || kv_heads < 1 || heads % kv_heads || d < 1 || max_seq < 1)
-    return fail(MSQ_E_INVALID, "msq_gqa_decode: heads %d, kv_heads %d, d %d", heads, kv_heads, d);
-  if (heads / kv_heads > 8 || d > 256 || (d & 3) || ((uintptr_t)q | (uintptr_t)kcache | (uintptr_t)vcache) & 15)
-    return fail(MSQ_E_UNSUPPORTED,
-                "msq_gqa_decode: needs heads / kv_heads <= 8, d <= 256 and a multiple of 4, 16-byte aligned q and "
-                "caches (heads %d, kv_heads %d, d %d)", heads, kv_heads, d);
-  if (gqa_decode_smem(heads, kv_heads, d, max_seq) > 200 * 1024)
-    return fail(MSQ_E_UNSUPPORTED, "msq_gqa_decode: max_seq %lld with d %d exceeds the shared-memory plan",
-                (long long)max_seq, d);
+  const int rc = check_gqa("msq_gqa_decode", heads, kv_heads, d, max_seq, q, kcache, vcache);
+  if (rc != MSQ_OK) return rc;
   return run_gqa_decode(static_cast<cudaStream_t>(stream), q, kcache, vcache, d_pos, out, heads, kv_heads, d, max_seq);
+}
+
+int msq_rope_gqa_decode(void* cu_ctx, void* stream, const float* qkv, int heads, int kv_heads, int d,
+                        const float* cos_t, const float* sin_t, const int64_t* d_pos, float* kcache, float* vcache,
+                        float* out, int64_t max_seq) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  if (!qkv || !cos_t || !sin_t || !d_pos || !kcache || !vcache || !out)
+    return fail(MSQ_E_INVALID, "msq_rope_gqa_decode: NULL pointer");
+  int rc = check_gqa("msq_rope_gqa_decode", heads, kv_heads, d, max_seq, qkv, kcache, vcache);
+  if (rc != MSQ_OK) return rc;
+  if (d < 8 || (d & (d - 1)) || ((uintptr_t)cos_t | (uintptr_t)sin_t) & 15)
+    return fail(MSQ_E_UNSUPPORTED, "msq_rope_gqa_decode: needs d a power of two >= 8 and 16-byte aligned tables (d %d)",
+                d);
+  return run_rope_gqa_decode(static_cast<cudaStream_t>(stream), qkv, kcache, vcache, cos_t, sin_t, d_pos, out, heads,
+                             kv_heads, d, max_seq);
 }
 
 int msq_swiglu(void* cu_ctx, void* stream, const float* gate_up, float* out, int64_t n) {

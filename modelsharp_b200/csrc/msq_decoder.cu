@@ -6,7 +6,8 @@
 //   rope_append   half-split rotary of q and k at the token's position, k and v appended to
 //                 the KV cache (RotaryEmbeddingKernel.cs:96-114; GroupQueryAttentionKernel.cs present K/V)
 //   gqa_decode    causal grouped-query attention of one query over the cache
-//                 (GroupQueryAttentionKernel.cs:194-195, 275-312)
+//                 (GroupQueryAttentionKernel.cs:194-195, 275-312); rope_gqa_decode also does
+//                 rope_append's work for the current token
 //   swiglu        silu(gate) * up
 //   argmax        first index of the maximum; also advances the device-side position
 // Positions are read from device memory so a decode step can be replayed from a CUDA graph.
@@ -111,45 +112,139 @@ __global__ void rope_append_kernel(float* __restrict__ qkv, int heads, int kv, i
   }
 }
 
-// Split-K decode attention. A cluster of kGqaSplit blocks per kv head g; block r of the cluster
-// takes keys [r C, (r + 1) C), C = ceil(T / kGqaSplit), for all G query heads of the group (the
-// K and V rows are read once for the group). Per block and head: scores, local max m, local
-// sum l of exp(score - m) and o = sum exp(score - m) v, kept in shared memory. After a cluster
-// barrier every block combines a slice of the group's outputs from all blocks' (m, l, o) through
-// distributed shared memory: out = sum_r o_r e^(m_r - M) / sum_r l_r e^(m_r - M), M = max m_r.
-// A warp reads a key row as one float4 per lane (d <= 128 DV) and reduces the G dot products
-// with shuffles. GM >= G is the compiled head-group size, DV = ceil(d / 128).
-constexpr int kGqaSplit = 8;
+// Split-K decode attention. A cluster of kGqaSplit blocks per kv head g; block r takes cache
+// keys [r C, (r + 1) C), C = ceil(Tc / kGqaSplit), for all G query heads of the group (each K
+// and V row is read once for the group). Inside a block every warp keeps its own online
+// softmax over the keys it takes (running max m, running sum l of exp(s - m), o = sum of
+// exp(s - m) v), loading the K and V rows of KB keys at once so their latencies overlap; the
+// warps are combined in shared memory, then, after a cluster barrier, every block combines a
+// slice of the group's outputs from all blocks through distributed shared memory:
+// out = sum_r o_r e^(m_r - M) / sum_r l_r e^(m_r - M), M = max m_r over non-empty parts.
+// A lane holds one float4 of a d-row per 128 elements (DV = ceil(d / 128)).
+//
+// ROPE: q, k and v of the current token come unrotated from qkv = [q | k | v]; each block
+// rotates its G query heads at position pos, and the cluster's last block rotates k, appends
+// k and v to cache row pos and attends to them from registers (so no block reads a cache row
+// this launch writes). Without ROPE, q is already rotated and keys 0..pos are all in the cache.
+constexpr int kGqaSplit = 8;   // blocks per cluster: one cluster per kv head
+constexpr int kGqaWarps = 16;  // warps per block
 
-// Score slots per head: the largest key slice rounded up to 4 floats, so that the float4
-// regions after the scores start on 16-byte boundaries.
-__host__ __device__ __forceinline__ int gqa_cmax(int64_t max_seq) {
-  return (int)(((max_seq + kGqaSplit - 1) / kGqaSplit + 3) & ~int64_t(3));
+// Half-split rotary of the float4s x (elements 128 j + 4 l .. + 3 of a d-row) at the table rows
+// cs / sn (d / 2 entries each). Element e pairs with e + d/2 (first half) or e - d/2: for
+// d <= 128 in lane l ^ (d / 8), for d = 256 in the other float4 of the same lane.
+template <int DV>
+__device__ __forceinline__ void rope4(float4 (&x)[DV], int l, int d, const float* __restrict__ cs,
+                                      const float* __restrict__ sn) {
+  const int half = d >> 1;
+  float4 pr[DV];
+  if constexpr (DV == 1) {
+    const int o = d >> 3;
+    pr[0].x = __shfl_xor_sync(0xffffffffu, x[0].x, o);
+    pr[0].y = __shfl_xor_sync(0xffffffffu, x[0].y, o);
+    pr[0].z = __shfl_xor_sync(0xffffffffu, x[0].z, o);
+    pr[0].w = __shfl_xor_sync(0xffffffffu, x[0].w, o);
+  } else {
+    pr[0] = x[1];
+    pr[1] = x[0];
+  }
+#pragma unroll
+  for (int j = 0; j < DV; ++j) {
+    const int c = 128 * j + 4 * l;
+    if (c < d) {
+      const bool first = c < half;
+      const int e = first ? c : c - half;
+      const float4 cv = *reinterpret_cast<const float4*>(cs + e), sv = *reinterpret_cast<const float4*>(sn + e);
+      const float sg = first ? -1.f : 1.f;
+      x[j] = make_float4(x[j].x * cv.x + sg * (pr[j].x * sv.x), x[j].y * cv.y + sg * (pr[j].y * sv.y),
+                         x[j].z * cv.z + sg * (pr[j].z * sv.z), x[j].w * cv.w + sg * (pr[j].w * sv.w));
+    }
+  }
 }
 
-template <int GM, int DV>
-__global__ void gqa_decode_kernel(const float* __restrict__ q, const float* __restrict__ kc,
-                                  const float* __restrict__ vc, const int64_t* __restrict__ pos_p,
-                                  float* __restrict__ out, int G, int d, int64_t max_seq, float scale) {
+// One warp's online-softmax update with nv (>= 1) keys of a batch.
+template <int GM, int DV, int KB>
+__device__ __forceinline__ void attend_batch(const float4 (&qr)[GM][DV], const float4 (&kr)[KB][DV],
+                                             const float4 (&vr)[KB][DV], int nv, float scale, float (&mw)[GM],
+                                             float (&lw)[GM], float4 (&acc)[GM][DV]) {
+  float sc[KB][GM];
+#pragma unroll
+  for (int i = 0; i < KB; ++i)
+#pragma unroll
+    for (int h = 0; h < GM; ++h) {
+      float v = 0.f;
+#pragma unroll
+      for (int j = 0; j < DV; ++j) {
+        v = fmaf(qr[h][j].x, kr[i][j].x, v);
+        v = fmaf(qr[h][j].y, kr[i][j].y, v);
+        v = fmaf(qr[h][j].z, kr[i][j].z, v);
+        v = fmaf(qr[h][j].w, kr[i][j].w, v);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      sc[i][h] = v * scale;
+    }
+#pragma unroll
+  for (int h = 0; h < GM; ++h) {
+    float bm = -FLT_MAX;
+#pragma unroll
+    for (int i = 0; i < KB; ++i)
+      if (i < nv) bm = fmaxf(bm, sc[i][h]);
+    const float mn = fmaxf(mw[h], bm);
+    const float alpha = expf(mw[h] - mn);  // 0 while the warp has seen no key (mw = -FLT_MAX)
+    lw[h] *= alpha;
+#pragma unroll
+    for (int j = 0; j < DV; ++j) {
+      acc[h][j].x *= alpha;
+      acc[h][j].y *= alpha;
+      acc[h][j].z *= alpha;
+      acc[h][j].w *= alpha;
+    }
+#pragma unroll
+    for (int i = 0; i < KB; ++i) {
+      const float pt = i < nv ? expf(sc[i][h] - mn) : 0.f;
+      lw[h] += pt;
+#pragma unroll
+      for (int j = 0; j < DV; ++j) {
+        acc[h][j].x = fmaf(pt, vr[i][j].x, acc[h][j].x);
+        acc[h][j].y = fmaf(pt, vr[i][j].y, acc[h][j].y);
+        acc[h][j].z = fmaf(pt, vr[i][j].z, acc[h][j].z);
+        acc[h][j].w = fmaf(pt, vr[i][j].w, acc[h][j].w);
+      }
+    }
+    mw[h] = mn;
+  }
+}
+
+template <int GM, int DV, bool ROPE>
+__global__ void __launch_bounds__(kGqaWarps * 32) gqa_decode_kernel(
+    const float* __restrict__ q, float* kc, float* vc, const float* __restrict__ cos_t,
+    const float* __restrict__ sin_t, const int64_t* __restrict__ pos_p, float* __restrict__ out, int heads, int kv,
+    int d, int64_t max_seq, float scale) {
+  constexpr int KB = GM * DV <= 4 ? 4 : GM * DV <= 8 ? 2 : 1;  // keys per warp batch (registers)
   namespace cg = cooperative_groups;
   cg::cluster_group cl = cg::this_cluster();
+  const int G = heads / kv;
   extern __shared__ __align__(16) float sm[];
-  const int cmax = gqa_cmax(max_seq);
-  float* sc = sm;                      // [GM][cmax] scores, then probabilities
-  float* part = sc + GM * cmax;        // [8 warps][G][d] partial sums of p v
-  float* ob = part + 8 * G * d;        // [G][d] this block's o
-  float* ml = ob + G * d;              // [G] m, then [G] l
+  float* part = sm;                      // [warps][G][d] per-warp o
+  float* wm = part + kGqaWarps * G * d;  // [warps][G] per-warp m
+  float* wl = wm + kGqaWarps * G;        // [warps][G] per-warp l
+  float* ob = wl + kGqaWarps * G;        // [G][d] this block's o
+  float* ml = ob + G * d;                // [G] m, then [G] l of this block
   pdl_wait();
   pdl_trigger();
   const int r = (int)cl.block_rank();
   const int g = blockIdx.x / kGqaSplit;
-  const int64_t pos = *pos_p;
-  const int T = (int)(pos < 0 ? 0 : pos >= max_seq ? max_seq : pos + 1);  // keys 0..pos within the cache
-  const int C = (T + kGqaSplit - 1) / kGqaSplit;
-  const int lo = min(T, r * C), hi = min(T, lo + C), n = hi - lo;
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  const int64_t pos = *pos_p;
+  const bool cur = ROPE && pos >= 0 && pos < max_seq;  // the current token's k / v come from qkv
+  const int T = (int)(pos < 0 ? 0 : pos >= max_seq ? max_seq : pos + 1);  // keys 0..pos within the cache
+  const int Tc = cur ? T - 1 : T;                                        // of which read from the cache
+  const int C = (Tc + kGqaSplit - 1) / kGqaSplit;
+  const int lo = min(Tc, r * C), hi = min(Tc, lo + C);
   const float* kb = kc + (int64_t)g * max_seq * d;
   const float* vb = vc + (int64_t)g * max_seq * d;
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int half = d >> 1;
 
   float4 qr[GM][DV];
 #pragma unroll
@@ -157,93 +252,100 @@ __global__ void gqa_decode_kernel(const float* __restrict__ q, const float* __re
 #pragma unroll
     for (int j = 0; j < DV; ++j) {
       const int c = 128 * j + 4 * l;
-      qr[h][j] = (h < G && c < d) ? *reinterpret_cast<const float4*>(q + ((int64_t)g * G + h) * d + c)
-                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+      qr[h][j] = (h < G && c < d) ? *reinterpret_cast<const float4*>(q + ((int64_t)g * G + h) * d + c) : z4;
     }
-  // scores: a warp per key
-#pragma unroll 2
-  for (int t = w; t < n; t += 8) {
-    float4 kr[DV];
+  if (cur) {
 #pragma unroll
-    for (int j = 0; j < DV; ++j) {
-      const int c = 128 * j + 4 * l;
-      kr[j] = c < d ? *reinterpret_cast<const float4*>(kb + (int64_t)(lo + t) * d + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-#pragma unroll
-    for (int h = 0; h < GM; ++h) {
-      float acc = 0.f;
-#pragma unroll
-      for (int j = 0; j < DV; ++j) {
-        acc = fmaf(qr[h][j].x, kr[j].x, acc);
-        acc = fmaf(qr[h][j].y, kr[j].y, acc);
-        acc = fmaf(qr[h][j].z, kr[j].z, acc);
-        acc = fmaf(qr[h][j].w, kr[j].w, acc);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-      if (l == 0 && h < G) sc[h * cmax + t] = acc * scale;
-    }
+    for (int h = 0; h < GM; ++h) rope4<DV>(qr[h], l, d, cos_t + pos * half, sin_t + pos * half);
   }
-  __syncthreads();
-  // local max and exponentials: warp h for head h
-  for (int h = w; h < G; h += 8) {
-    float mx = -FLT_MAX;
-    for (int t = l; t < n; t += 32) mx = fmaxf(mx, sc[h * cmax + t]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float sum = 0.f;
-    for (int t = l; t < n; t += 32) {
-      const float e = expf(sc[h * cmax + t] - mx);
-      sc[h * cmax + t] = e;
-      sum += e;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (l == 0) {
-      ml[h] = mx;
-      ml[G + h] = sum;  // 0 for an empty slice
-    }
-  }
-  __syncthreads();
-  // o = sum_t p_t v_t: warp w takes keys w, w + 8, ...
+  float mw[GM], lw[GM];
   float4 acc[GM][DV];
 #pragma unroll
-  for (int h = 0; h < GM; ++h)
+  for (int h = 0; h < GM; ++h) {
+    mw[h] = -FLT_MAX;
+    lw[h] = 0.f;
 #pragma unroll
-    for (int j = 0; j < DV; ++j) acc[h][j] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 2
-  for (int t = w; t < n; t += 8) {
-    float4 vr[DV];
+    for (int j = 0; j < DV; ++j) acc[h][j] = z4;
+  }
+  for (int t0 = lo + w * KB; t0 < hi; t0 += kGqaWarps * KB) {
+    float4 kr[KB][DV], vr[KB][DV];
+#pragma unroll
+    for (int i = 0; i < KB; ++i)
+#pragma unroll
+      for (int j = 0; j < DV; ++j) {
+        const int c = 128 * j + 4 * l;
+        const bool ok = t0 + i < hi && c < d;
+        kr[i][j] = ok ? *reinterpret_cast<const float4*>(kb + (int64_t)(t0 + i) * d + c) : z4;
+        vr[i][j] = ok ? *reinterpret_cast<const float4*>(vb + (int64_t)(t0 + i) * d + c) : z4;
+      }
+    attend_batch<GM, DV, KB>(qr, kr, vr, min(KB, hi - t0), scale, mw, lw, acc);
+  }
+  if (cur && r == kGqaSplit - 1 && w == 0) {  // the current key: rotate, append, attend
+    float4 kr[KB][DV], vr[KB][DV];
+#pragma unroll
+    for (int i = 0; i < KB; ++i)
+#pragma unroll
+      for (int j = 0; j < DV; ++j) kr[i][j] = vr[i][j] = z4;
 #pragma unroll
     for (int j = 0; j < DV; ++j) {
       const int c = 128 * j + 4 * l;
-      vr[j] = c < d ? *reinterpret_cast<const float4*>(vb + (int64_t)(lo + t) * d + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (c < d) {
+        kr[0][j] = *reinterpret_cast<const float4*>(q + ((int64_t)heads + g) * d + c);
+        vr[0][j] = *reinterpret_cast<const float4*>(q + ((int64_t)heads + kv + g) * d + c);
+      }
     }
+    float4 k1[DV];
 #pragma unroll
-    for (int h = 0; h < GM; ++h) {
-      const float pt = h < G ? sc[h * cmax + t] : 0.f;
+    for (int j = 0; j < DV; ++j) k1[j] = kr[0][j];
+    rope4<DV>(k1, l, d, cos_t + pos * half, sin_t + pos * half);
+#pragma unroll
+    for (int j = 0; j < DV; ++j) {
+      kr[0][j] = k1[j];
+      const int c = 128 * j + 4 * l;
+      if (c < d) {
+        *reinterpret_cast<float4*>(kc + ((int64_t)g * max_seq + pos) * d + c) = k1[j];
+        *reinterpret_cast<float4*>(vc + ((int64_t)g * max_seq + pos) * d + c) = vr[0][j];
+      }
+    }
+    attend_batch<GM, DV, KB>(qr, kr, vr, 1, scale, mw, lw, acc);
+  }
+  // the warps' parts, then this block's (m, l, o)
+#pragma unroll
+  for (int h = 0; h < GM; ++h) {
+    if (h < G) {
 #pragma unroll
       for (int j = 0; j < DV; ++j) {
-        acc[h][j].x = fmaf(pt, vr[j].x, acc[h][j].x);
-        acc[h][j].y = fmaf(pt, vr[j].y, acc[h][j].y);
-        acc[h][j].z = fmaf(pt, vr[j].z, acc[h][j].z);
-        acc[h][j].w = fmaf(pt, vr[j].w, acc[h][j].w);
+        const int c = 128 * j + 4 * l;
+        if (c < d) *reinterpret_cast<float4*>(part + ((int64_t)w * G + h) * d + c) = acc[h][j];
+      }
+      if (l == 0) {
+        wm[w * G + h] = mw[h];
+        wl[w * G + h] = lw[h];
       }
     }
   }
-#pragma unroll
-  for (int h = 0; h < GM; ++h)
-#pragma unroll
-    for (int j = 0; j < DV; ++j) {
-      const int c = 128 * j + 4 * l;
-      if (h < G && c < d) *reinterpret_cast<float4*>(part + ((int64_t)w * G + h) * d + c) = acc[h][j];
-    }
   __syncthreads();
   for (int i = threadIdx.x; i < G * d; i += blockDim.x) {
-    float v = 0.f;
+    const int h = i / d;
+    float M = -FLT_MAX;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) v += part[k * G * d + i];
-    ob[i] = v;
+    for (int k = 0; k < kGqaWarps; ++k)
+      if (wl[k * G + h] > 0.f) M = fmaxf(M, wm[k * G + h]);
+    float O = 0.f, L = 0.f;
+#pragma unroll
+    for (int k = 0; k < kGqaWarps; ++k) {
+      const float lk = wl[k * G + h];
+      if (lk > 0.f) {
+        const float f = expf(wm[k * G + h] - M);
+        O = fmaf(part[(k * G + h) * d + (i - h * d)], f, O);
+        L = fmaf(lk, f, L);
+      }
+    }
+    ob[i] = O;
+    if (i - h * d == 0) {
+      ml[h] = M;
+      ml[G + h] = L;
+    }
   }
   cl.sync();  // every block's (m, l, o) is complete and visible to the cluster
   for (int i = r * blockDim.x + threadIdx.x; i < G * d; i += kGqaSplit * blockDim.x) {
@@ -352,22 +454,22 @@ int run_rope_append(cudaStream_t st, float* qkv, int heads, int kv, int d, const
                     heads, kv, d, cos_t, sin_t, pos, kc, vc, max_seq);
 }
 
-size_t gqa_decode_smem(int heads, int kv, int d, int64_t max_seq) {
-  const int G = heads / kv;
-  const int gm = G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8;
-  return sizeof(float) * (size_t)(gm * (int64_t)gqa_cmax(max_seq) + 9 * (int64_t)G * d + 2 * G);
+size_t gqa_decode_smem(int heads, int kv, int d) {
+  const int64_t G = heads / kv;
+  return sizeof(float) * (size_t)(kGqaWarps * G * d + 2 * kGqaWarps * G + G * d + 2 * G);
 }
 
-template <int GM, int DV>
-int launch_gqa(cudaStream_t st, const float* q, const float* kc, const float* vc, const int64_t* pos, float* out,
-               int kv, int G, int d, int64_t max_seq) {
-  const size_t smem = gqa_decode_smem(G * kv, kv, d, max_seq);
-  auto kern = gqa_decode_kernel<GM, DV>;
-  MSQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-               "gqa smem attribute");
+template <int GM, int DV, bool ROPE>
+int launch_gqa(cudaStream_t st, const float* q, float* kc, float* vc, const float* cos_t, const float* sin_t,
+               const int64_t* pos, float* out, int heads, int kv, int d, int64_t max_seq) {
+  const size_t smem = gqa_decode_smem(heads, kv, d);
+  auto kern = gqa_decode_kernel<GM, DV, ROPE>;
+  if (smem > 48 * 1024)
+    MSQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                 "gqa smem attribute");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(kv * kGqaSplit));
-  cfg.blockDim = dim3(256);
+  cfg.blockDim = dim3(kGqaWarps * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
@@ -379,25 +481,42 @@ int launch_gqa(cudaStream_t st, const float* q, const float* kc, const float* vc
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  MSQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, q, kc, vc, pos, out, G, d, max_seq, 1.0f / sqrtf((float)d)),
+  MSQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, q, kc, vc, cos_t, sin_t, pos, out, heads, kv, d, max_seq,
+                                  1.0f / sqrtf((float)d)),
                "gqa_decode launch");
   note_launch();
   return MSQ_OK;
 }
 
+template <bool ROPE>
+int dispatch_gqa(cudaStream_t st, const float* q, float* kc, float* vc, const float* cos_t, const float* sin_t,
+                 const int64_t* pos, float* out, int heads, int kv, int d, int64_t max_seq) {
+  const int G = heads / kv;
+#define MSQ_GQA(GM, DV) launch_gqa<GM, DV, ROPE>(st, q, kc, vc, cos_t, sin_t, pos, out, heads, kv, d, max_seq)
+  if (d <= 128) {
+    if (G <= 1) return MSQ_GQA(1, 1);
+    if (G <= 2) return MSQ_GQA(2, 1);
+    if (G <= 4) return MSQ_GQA(4, 1);
+    return MSQ_GQA(8, 1);
+  }
+  if (G <= 1) return MSQ_GQA(1, 2);
+  if (G <= 2) return MSQ_GQA(2, 2);
+  if (G <= 4) return MSQ_GQA(4, 2);
+  return MSQ_GQA(8, 2);
+#undef MSQ_GQA
+}
+
 int run_gqa_decode(cudaStream_t st, const float* q, const float* kc, const float* vc, const int64_t* pos, float* out,
                    int heads, int kv, int d, int64_t max_seq) {
-  const int G = heads / kv;
-  if (d <= 128) {
-    if (G <= 1) return launch_gqa<1, 1>(st, q, kc, vc, pos, out, kv, G, d, max_seq);
-    if (G <= 2) return launch_gqa<2, 1>(st, q, kc, vc, pos, out, kv, G, d, max_seq);
-    if (G <= 4) return launch_gqa<4, 1>(st, q, kc, vc, pos, out, kv, G, d, max_seq);
-    return launch_gqa<8, 1>(st, q, kc, vc, pos, out, kv, G, d, max_seq);
-  }
-  if (G <= 1) return launch_gqa<1, 2>(st, q, kc, vc, pos, out, kv, G, d, max_seq);
-  if (G <= 2) return launch_gqa<2, 2>(st, q, kc, vc, pos, out, kv, G, d, max_seq);
-  if (G <= 4) return launch_gqa<4, 2>(st, q, kc, vc, pos, out, kv, G, d, max_seq);
-  return launch_gqa<8, 2>(st, q, kc, vc, pos, out, kv, G, d, max_seq);
+  // without ROPE the kernel never writes the caches
+  return dispatch_gqa<false>(st, q, const_cast<float*>(kc), const_cast<float*>(vc), nullptr, nullptr, pos, out,
+                             heads, kv, d, max_seq);
+}
+
+int run_rope_gqa_decode(cudaStream_t st, const float* qkv, float* kc, float* vc, const float* cos_t,
+                        const float* sin_t, const int64_t* pos, float* out, int heads, int kv, int d,
+                        int64_t max_seq) {
+  return dispatch_gqa<true>(st, qkv, kc, vc, cos_t, sin_t, pos, out, heads, kv, d, max_seq);
 }
 
 int run_swiglu(cudaStream_t st, const float* gu, float* out, int64_t n) {

@@ -133,8 +133,11 @@ int run_rope_append(cudaStream_t st, float* qkv, int heads, int kv, int d, const
                     const int64_t* pos, float* kc, float* vc, int64_t max_seq);
 int run_gqa_decode(cudaStream_t st, const float* q, const float* kc, const float* vc, const int64_t* pos, float* out,
                    int heads, int kv, int d, int64_t max_seq);
+int run_rope_gqa_decode(cudaStream_t st, const float* qkv, float* kc, float* vc, const float* cos_t,
+                        const float* sin_t, const int64_t* pos, float* out, int heads, int kv, int d,
+                        int64_t max_seq);
 // Dynamic shared memory of one gqa_decode block (heads / kv <= 8, d <= 256).
-size_t gqa_decode_smem(int heads, int kv, int d, int64_t max_seq);
+size_t gqa_decode_smem(int heads, int kv, int d);
 int run_swiglu(cudaStream_t st, const float* gu, float* out, int64_t n);
 int run_argmax(cudaStream_t st, const float* x, int64_t n, int64_t* idx, int64_t* pos);
 

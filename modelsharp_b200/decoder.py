@@ -102,8 +102,8 @@ class CudaDecoder:
     q/k/v are packed into one weight (N = (H + 2 Hkv) d) and gate/up into another (N = 2 I), as
     packed-QKV exports do, so a layer runs four MatMulNBits. The prompt pass uses torch glue;
     a decode step folds RMSNorm, SwiGLU and the residual adds into its GEMVs and uses the
-    library's rotary + KV append, GQA decode and argmax kernels, every launch chained with
-    programmatic dependent launch."""
+    library's fused rotary + KV append + GQA decode and argmax kernels, every launch chained
+    with programmatic dependent launch."""
 
     def __init__(self, cfg: DecoderConfig, weights: dict, device: torch.device | str):
         self.cfg = cfg
@@ -191,9 +191,9 @@ class CudaDecoder:
         the argmax into tok, advances pos and returns the logits [vocab]. Only device memory
         changes, so the step can be captured in a CUDA graph and replayed.
 
-        Per layer six launches: q/k/v GEMV with the attention RMSNorm folded in, rotary + KV
-        append, GQA, o GEMV adding into the residual, gate/up GEMV with the MLP RMSNorm folded
-        in, down GEMV taking SwiGLU of its input and adding into the residual."""
+        Per layer five launches: q/k/v GEMV with the attention RMSNorm folded in; rotary, KV
+        append and GQA in one; o GEMV adding into the residual; gate/up GEMV with the MLP
+        RMSNorm folded in; down GEMV taking SwiGLU of its input and adding into the residual."""
         cfg, lib = self.cfg, N.lib()
         st = torch.cuda.current_stream(self.device).cuda_stream
 
@@ -204,12 +204,10 @@ class CudaDecoder:
         torch.index_select(self.embed, 0, tok, out=self.bx)
         for li, lw in enumerate(self.layers):
             lw["qkv"].matmul_fused(self.bx, self.bqkv, rms_gamma=lw["norm_attn"], rms_eps=cfg.eps, stream=st)
-            ok(lib.msq_rope_append(None, st, self.bqkv.data_ptr(), cfg.heads, cfg.kv_heads, cfg.head_dim,
-                                   self.cos.data_ptr(), self.sin.data_ptr(), pos.data_ptr(), self.kc[li].data_ptr(),
-                                   self.vc[li].data_ptr(), cfg.max_seq), "msq_rope_append")
-            ok(lib.msq_gqa_decode(None, st, self.bqkv.data_ptr(), self.kc[li].data_ptr(), self.vc[li].data_ptr(),
-                                  pos.data_ptr(), self.battn.data_ptr(), cfg.heads, cfg.kv_heads, cfg.head_dim,
-                                  cfg.max_seq), "msq_gqa_decode")
+            ok(lib.msq_rope_gqa_decode(None, st, self.bqkv.data_ptr(), cfg.heads, cfg.kv_heads, cfg.head_dim,
+                                       self.cos.data_ptr(), self.sin.data_ptr(), pos.data_ptr(), self.kc[li].data_ptr(),
+                                       self.vc[li].data_ptr(), self.battn.data_ptr(), cfg.max_seq),
+               "msq_rope_gqa_decode")
             lw["o"].matmul_fused(self.battn, self.bx, accumulate=True, stream=st)
             lw["gate_up"].matmul_fused(self.bx, self.bgu, rms_gamma=lw["norm_mlp"], rms_eps=cfg.eps, stream=st)
             lw["down"].matmul_fused(self.bgu, self.bx, swiglu=True, accumulate=True, stream=st)

@@ -4,9 +4,10 @@ Each kernel runs on seeded inputs and is compared with oracle/decoder.py (float3
 of the reference's CPU kernels): add + RMSNorm, rotary + KV-cache append at a device-side
 position, grouped-query decode attention, SwiGLU and argmax. Float results agree to 1e-5
 relative L2 (a different summation order than the checker's); index results are exact.
-Edge cases: the first position (one key, most of the split-K slices empty), the last cache
-row, 1 to 8 query heads per kv head, head sizes 32 to 256, ties in argmax (the first index
-wins), a position past the cache (no write, all keys read).
+The fused rotary + append + attention entry is compared with the checker's rope followed by
+attention. Edge cases: the first position (one key, most of the split-K slices empty), the
+last cache row, 1 to 8 query heads per kv head, head sizes 16 to 256, a 40 000-row cache,
+ties in argmax (the first index wins), a position past the cache (no write, all keys read).
 """
 import numpy as np
 import pytest
@@ -128,12 +129,81 @@ def test_gqa_decode_position_past_cache_reads_all_keys(cuda_device):
     assert oracle.rel_l2(out.cpu().numpy(), od.attention(q, kc, vc, max_seq - 1, cfg)) <= TOL
 
 
-def test_gqa_decode_rejects_oversized_cache(cuda_device):
+def test_gqa_decode_limits(cuda_device):
     t = torch.zeros(8, device=cuda_device)
     dpos = torch.zeros(1, dtype=torch.int64, device=cuda_device)
-    rc = N.lib().msq_gqa_decode(None, _stream(cuda_device), t.data_ptr(), t.data_ptr(), t.data_ptr(), dpos.data_ptr(),
-                                t.data_ptr(), 8, 8, 128, 1 << 20)
-    assert rc == N.MSQ_E_UNSUPPORTED
+    L, st = N.lib(), _stream(cuda_device)
+    # 16 query heads per kv head, and d = 512: outside the compiled plans
+    assert L.msq_gqa_decode(None, st, t.data_ptr(), t.data_ptr(), t.data_ptr(), dpos.data_ptr(), t.data_ptr(),
+                            16, 1, 128, 64) == N.MSQ_E_UNSUPPORTED
+    assert L.msq_gqa_decode(None, st, t.data_ptr(), t.data_ptr(), t.data_ptr(), dpos.data_ptr(), t.data_ptr(),
+                            2, 1, 512, 64) == N.MSQ_E_UNSUPPORTED
+    # a long cache is fine: shared memory does not grow with max_seq
+    heads, kv, d, max_seq, pos = 8, 2, 128, 40000, 39000
+    cfg = _Cfg(heads, kv, d, max_seq)
+    rng = np.random.default_rng(40000)
+    q = rng.standard_normal((1, heads * d)).astype(np.float32)
+    kc = rng.standard_normal((kv, max_seq, d)).astype(np.float32)
+    vc = rng.standard_normal((kv, max_seq, d)).astype(np.float32)
+    dq, dkc, dvc = (torch.from_numpy(v).to(cuda_device) for v in (q, kc, vc))
+    out = torch.empty(1, heads * d, device=cuda_device)
+    dpos.fill_(pos)
+    _ok(L.msq_gqa_decode(None, st, dq.data_ptr(), dkc.data_ptr(), dvc.data_ptr(), dpos.data_ptr(), out.data_ptr(),
+                         heads, kv, d, max_seq))
+    assert oracle.rel_l2(out.cpu().numpy(), od.attention(q, kc, vc, pos, cfg)) <= TOL
+
+
+@pytest.mark.parametrize("heads,kv,d,max_seq,pos", [(32, 8, 128, 640, 0), (32, 8, 128, 640, 600), (4, 2, 64, 64, 63),
+                                                    (6, 3, 32, 100, 41), (16, 2, 256, 300, 77), (8, 8, 128, 2048, 9),
+                                                    (8, 1, 16, 24, 23)])
+def test_rope_gqa_decode_matches_rope_then_attention(cuda_device, heads, kv, d, max_seq, pos):
+    """The fused entry against the checker's rope then attention, and the cache rows it writes."""
+    cfg = _Cfg(heads, kv, d, max_seq)
+    cos, sin = od.rope_tables(cfg)
+    rng = np.random.default_rng(pos * 7 + d)
+    qkv = rng.standard_normal((1, (heads + 2 * kv) * d)).astype(np.float32)
+    kc = rng.standard_normal((kv, max_seq, d)).astype(np.float32)
+    vc = rng.standard_normal((kv, max_seq, d)).astype(np.float32)
+    dqkv, dkc, dvc = (torch.from_numpy(v.copy()).to(cuda_device) for v in (qkv, kc, vc))
+    dcos, dsin = torch.from_numpy(cos).to(cuda_device), torch.from_numpy(sin).to(cuda_device)
+    dpos = torch.tensor([pos], dtype=torch.int64, device=cuda_device)
+    out = torch.empty(1, heads * d, device=cuda_device)
+    _ok(N.lib().msq_rope_gqa_decode(None, _stream(cuda_device), dqkv.data_ptr(), heads, kv, d, dcos.data_ptr(),
+                                    dsin.data_ptr(), dpos.data_ptr(), dkc.data_ptr(), dvc.data_ptr(), out.data_ptr(),
+                                    max_seq))
+    p = np.asarray([pos])
+    nq, nk = heads * d, kv * d
+    q = od.rope(qkv[:, :nq], heads, d, p, cos, sin)
+    k = od.rope(qkv[:, nq:nq + nk], kv, d, p, cos, sin)
+    kc[:, pos] = k.reshape(kv, d)
+    vc[:, pos] = qkv[0, nq + nk:].reshape(kv, d)
+    assert oracle.rel_l2(out.cpu().numpy(), od.attention(q, kc, vc, pos, cfg)) <= TOL
+    got_k = dkc.cpu().numpy()
+    assert oracle.rel_l2(got_k[:, pos], kc[:, pos]) <= TOL
+    np.testing.assert_array_equal(np.delete(got_k, pos, axis=1), np.delete(kc, pos, axis=1))  # other rows untouched
+    np.testing.assert_array_equal(dvc.cpu().numpy(), vc)
+    np.testing.assert_array_equal(dqkv.cpu().numpy(), qkv)  # the input stays unrotated
+
+
+def test_rope_gqa_decode_position_past_cache(cuda_device):
+    heads, kv, d, max_seq = 4, 2, 64, 32
+    cfg = _Cfg(heads, kv, d, max_seq)
+    cos, sin = od.rope_tables(cfg)
+    rng = np.random.default_rng(6)
+    qkv = rng.standard_normal((1, (heads + 2 * kv) * d)).astype(np.float32)
+    kc = rng.standard_normal((kv, max_seq, d)).astype(np.float32)
+    vc = rng.standard_normal((kv, max_seq, d)).astype(np.float32)
+    dqkv, dkc, dvc = (torch.from_numpy(v.copy()).to(cuda_device) for v in (qkv, kc, vc))
+    dpos = torch.tensor([max_seq + 3], dtype=torch.int64, device=cuda_device)
+    out = torch.empty(1, heads * d, device=cuda_device)
+    _ok(N.lib().msq_rope_gqa_decode(None, _stream(cuda_device), dqkv.data_ptr(), heads, kv, d,
+                                    torch.from_numpy(cos).to(cuda_device).data_ptr(),
+                                    torch.from_numpy(sin).to(cuda_device).data_ptr(), dpos.data_ptr(),
+                                    dkc.data_ptr(), dvc.data_ptr(), out.data_ptr(), max_seq))
+    ref = od.attention(qkv[:, :heads * d], kc, vc, max_seq - 1, cfg)
+    assert oracle.rel_l2(out.cpu().numpy(), ref) <= TOL
+    np.testing.assert_array_equal(dkc.cpu().numpy(), kc)
+    np.testing.assert_array_equal(dvc.cpu().numpy(), vc)
 
 
 @pytest.mark.parametrize("n", [14336, 1, 1000])
