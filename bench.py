@@ -714,7 +714,7 @@ def run_decode(args, rank: int, world: int, local_rank: int):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    cfg = DecoderConfig()
+    cfg = DecoderConfig(layers=args.layers)
     w = make_weights(cfg, 0, dev)
     dec = CudaDecoder(cfg, w, dev)
     host_w = None
@@ -825,7 +825,9 @@ def run_decode(args, rank: int, world: int, local_rank: int):
             "metric": "7B INT4 decode tok/s", "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps,
             "warmup": 2, "ms_per_step": ms_tok, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32 activations, int4 weights", "data": "synthetic",
-            "config": {"workload": DECODE_WORKLOAD, "prompt_tokens": n_prompt, "new_tokens": n_new,
+            "config": {"workload": DECODE_WORKLOAD if cfg.layers == 32 else
+                       f"{cfg.layers}-layer cut of: {DECODE_WORKLOAD} (a profiling case, not the 7B shape)",
+                       "prompt_tokens": n_prompt, "new_tokens": n_new,
                        "generations": reps, "prompt_ms": pre_ms / reps, "prompt_tok_s": n_prompt / (pre_ms / reps) * 1e3,
                        "weight_bytes_per_token": wb, "parallelism": f"replicas{world}",
                        "l2": "4.5 GB of weights per token, far above L2",
@@ -856,6 +858,8 @@ def main():
     ap.add_argument("--m", type=int, default=1, help="A rows for the nsplit70b workload")
     ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
                     help="nsplit70b: fused peer-store gather (M <= 4) or NCCL all-gather")
+    ap.add_argument("--layers", type=int, default=32,
+                    help="decode7b: decoder layers (32 = the 7B shape; fewer only for small profiling cases)")
     ap.add_argument("--shapes", default="",
                     help="restrict the step to these KxN shapes (comma separated), for profiling one shape")
     args = ap.parse_args()
