@@ -855,7 +855,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--workload", default="sweep7b", choices=["sweep7b", "nsplit70b", "prefill", "decode7b"])
-    ap.add_argument("--m", type=int, default=1, help="A rows for the nsplit70b workload")
+    ap.add_argument("--rows", "--m", dest="m", type=int, default=1,
+                    help="A rows for the nsplit70b workload (--rows under torchrun, whose parser takes --m as a "
+                         "prefix of its own options)")
     ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
                     help="nsplit70b: fused peer-store gather (M <= 4) or NCCL all-gather")
     ap.add_argument("--layers", type=int, default=32,

@@ -68,6 +68,8 @@ struct GemmArgs {
   int M, n_rows, K, ksteps;
   int bs_shift;
   int vec_store;
+  int kper;              // k-stages per CTA: blockIdx.z takes stages [z kper, (z + 1) kper)
+  int64_t split_stride;  // with several k-splits: elements between their partial outputs
 };
 
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -128,6 +130,9 @@ __global__ void __launch_bounds__(Plan<TM, BN>::kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BN, m0 = blockIdx.y * PL::kRows;
+  // this CTA's k-stages (never empty: the host sizes the splits)
+  const int kb = (int)blockIdx.z * p.kper;
+  const int nk = min(p.ksteps, kb + p.kper) - kb;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -157,10 +162,10 @@ __global__ void __launch_bounds__(Plan<TM, BN>::kThreads, 1)
   if (warp == kTmaWarp) {
     if (lane == 0) {
       int issued = 0;
-      for (int kt = 0; kt < p.ksteps; ++kt) {
-        const int s = kt % S;
-        const uint32_t u = kt / S;
-        if (kt >= S && !wait_abort(&empty[s], (u - 1) & 1, abort_flag, ptx::kErrTimeoutEmpty)) break;
+      for (int i = 0; i < nk; ++i) {
+        const int kt = kb + i, s = i % S;
+        const uint32_t u = i / S;
+        if (i >= S && !wait_abort(&empty[s], (u - 1) & 1, abort_flag, ptx::kErrTimeoutEmpty)) break;
         // scales / zero points: the 16-byte-aligned column holding the stage's block(s)
         const int blk0 = (kt * BK) >> p.bs_shift;
         ptx::mbar_arrive_expect_tx(&full[s],
@@ -192,9 +197,9 @@ __global__ void __launch_bounds__(Plan<TM, BN>::kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
       bool ok = true;
-      for (int kt = 0; kt < p.ksteps && ok; ++kt) {
-        const int s = kt % S;
-        const uint32_t u = kt / S;
+      for (int i = 0; i < nk && ok; ++i) {
+        const int s = i % S;
+        const uint32_t u = i / S;
         ok = wait_abort(&full[s], u & 1, abort_flag, ptx::kErrTimeoutFull) &&
              wait_abort(&wready[s], u & 1, abort_flag, ptx::kErrTimeoutFull);
         if (!ok) break;
@@ -205,7 +210,7 @@ __global__ void __launch_bounds__(Plan<TM, BN>::kThreads, 1)
           const uint64_t ad = sw128_desc(ptx::smem_u32(smem + PL::kOffA + s * PL::kABytes + t * BM * 128));
 #pragma unroll
           for (int j = 0; j < BK / 16; ++j)
-            ptx::mma_f16(tmem + (uint32_t)(t * BN), ad + 2 * j, bd + 2 * j, idesc, (kt | j) != 0);
+            ptx::mma_f16(tmem + (uint32_t)(t * BN), ad + 2 * j, bd + 2 * j, idesc, (i | j) != 0);
         }
         ptx::mma_commit(&empty[s]);
       }
@@ -226,9 +231,9 @@ __global__ void __launch_bounds__(Plan<TM, BN>::kThreads, 1)
     const int tid = threadIdx.x;  // 0 .. 2*BN-1
     const int r = tid >> 1, c = tid & 1;
     uint8_t* brow_base = smem + PL::kOffB + (r >> 3) * 1024 + (r & 7) * 128;
-    for (int kt = 0; kt < p.ksteps; ++kt) {
-      const int s = kt % S;
-      const uint32_t u = kt / S;
+    for (int i = 0; i < nk; ++i) {
+      const int kt = kb + i, s = i % S;
+      const uint32_t u = i / S;
       const bool ok = wait_abort(&full[s], u & 1, abort_flag, ptx::kErrTimeoutFull);
       if (ok) {
         const uint4 w4 = *reinterpret_cast<const uint4*>(smem + PL::kOffP + s * PL::kPBytes + tid * 16);
@@ -288,7 +293,7 @@ __global__ void __launch_bounds__(Plan<TM, BN>::kThreads, 1)
         ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)tcol, v);
         ptx::tmem_ld_wait();
         if (m < p.M) {
-          float* yrow = p.y + (int64_t)m * p.ldy + n0 + col;
+          float* yrow = p.y + blockIdx.z * p.split_stride + (int64_t)m * p.ldy + n0 + col;
           if (p.vec_store && n0 + col + 32 <= p.n_rows) {
 #pragma unroll
             for (int j = 0; j < 32; j += 4)
@@ -319,6 +324,19 @@ __global__ void to_half_kernel(const void* __restrict__ a, int dt, int64_t M, in
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t m = i / K, k = i - m * K;
     out[m * lda + k] = __float2half_rn(load_act(a, dt, i));
+  }
+}
+
+// y[m][n] = sum over splits z (in order) of ws[z][m][n]; ws rows of pitch ldw.
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int64_t stride, int64_t M, int N,
+                                     int64_t ldw, float* __restrict__ y, int64_t ldy) {
+  const int64_t total = M * N;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / N, n = i - m * N;
+    const float* src = ws + m * ldw + n;
+    float acc = src[0];
+    for (int z = 1; z < splits; ++z) acc += src[z * stride];
+    y[m * ldy + n] = acc;
   }
 }
 
@@ -397,11 +415,36 @@ int launch_zp(cudaStream_t st, int zp_kind, const CUtensorMap& tmA, const Weight
 
 namespace {
 
+constexpr size_t kSplitWsMax = size_t(64) << 20;  // partial outputs of a k-split launch
+
+// K-splits for a launch of `ctas` tiles: 1 when the tiles fill the SMs; otherwise the count
+// (each split >= 8 k-stages, <= 32 splits, partial outputs <= kSplitWsMax) whose CTAs fill the
+// last wave best, preferring fewer splits unless more fill it by over 2 %.
+int choose_splits(int ctas, int sms, int ksteps, int64_t M, int64_t ldw) {
+  if (ctas >= sms) return 1;
+  auto fill = [&](int n) { return (double)n / (double)(((n + sms - 1) / sms) * sms); };
+  int best_s = 1;
+  double best = fill(ctas);
+  for (int s = 2; s <= 32 && 8 * s <= ksteps; ++s) {
+    if ((size_t)s * (size_t)M * (size_t)ldw * sizeof(float) > kSplitWsMax) break;
+    const int kper = (ksteps + s - 1) / s;
+    if ((ksteps + kper - 1) / kper != s) continue;  // every split must get a stage
+    const double f = fill(ctas * s);
+    if (f > best + 0.02) {
+      best = f;
+      best_s = s;
+    }
+  }
+  return best_s;
+}
+
 // Builds the activation map over fp16 rows of stride lda and launches the tile kernel:
 // 512 x 128 tiles (four accumulators sharing each dequantised weight tile) for M >= 512,
-// 256 x 128 for M > 128, else 128 x 128.
+// 256 x 128 for M > 128, else 128 x 128. When the tiles leave SMs idle and `allow_split`,
+// K is split across CTAs whose partial tiles go to stream-ordered scratch and are summed in a
+// fixed order into Y (deterministic).
 int launch_gemm(cudaStream_t st, const Weights& w, const WeightMaps& m128, const void* a16, int64_t lda,
-                int64_t M, float* d_y, int64_t ldy) {
+                int64_t M, float* d_y, int64_t ldy, bool allow_split) {
   const int tm = M >= 4 * BM ? 4 : M > BM ? 2 : 1;
   const int rows = tm * BM;
   CUtensorMap tmA;
@@ -418,12 +461,39 @@ int launch_gemm(cudaStream_t st, const Weights& w, const WeightMaps& m128, const
   int sh = 0;
   while ((1 << sh) < w.block_size) ++sh;
   g.bs_shift = sh;
-  g.vec_store = (ldy % 4 == 0) && ((reinterpret_cast<uintptr_t>(d_y) & 15) == 0);
-  const dim3 grid((w.n_rows + 127) / 128, (unsigned)((M + rows - 1) / rows));
+  const int gx = (w.n_rows + 127) / 128, gy = (int)((M + rows - 1) / rows);
+  const int64_t ldw = (w.n_rows + 3) / 4 * 4;
+  const int splits = allow_split ? choose_splits(gx * gy, num_sms(w.device), g.ksteps, M, ldw) : 1;
+  g.kper = (g.ksteps + splits - 1) / splits;
+  void* ws = nullptr;
+  if (splits > 1) {
+    rc = scratch_alloc(&ws, (size_t)splits * (size_t)M * (size_t)ldw * sizeof(float), st);
+    if (rc != MSQ_OK) return rc;
+    g.y = static_cast<float*>(ws);
+    g.ldy = ldw;
+    g.split_stride = M * ldw;
+  }
+  g.vec_store = (g.ldy % 4 == 0) && ((reinterpret_cast<uintptr_t>(g.y) & 15) == 0);
+  const dim3 grid(gx, gy, splits);
   rc = tm == 4   ? launch_zp<4, 128>(st, w.zp_kind, tmA, m128, g, grid)
        : tm == 2 ? launch_zp<2, 128>(st, w.zp_kind, tmA, m128, g, grid)
                  : launch_zp<1, 128>(st, w.zp_kind, tmA, m128, g, grid);
-  if (rc == MSQ_OK) note_path(tm == 4 ? "gemm_tc_m512_n128" : tm == 2 ? "gemm_tc_m256_n128" : "gemm_tc_m128_n128");
+  if (rc == MSQ_OK && splits > 1) {
+    const int64_t total = M * w.n_rows;
+    const int blocks = (int)std::min<int64_t>((total + 255) / 256, 8 * (int64_t)num_sms(w.device));
+    splitk_reduce_kernel<<<blocks, 256, 0, st>>>(static_cast<const float*>(ws), splits, g.split_stride, M, w.n_rows,
+                                                 ldw, d_y, ldy);
+    note_launch();
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) rc = cuda_fail(e, "split-K reduce launch");
+  }
+  scratch_free(ws, st);
+  if (rc == MSQ_OK) {
+    if (splits > 1)
+      note_path(tm == 4 ? "gemm_tc_m512_n128_splitk" : tm == 2 ? "gemm_tc_m256_n128_splitk" : "gemm_tc_m128_n128_splitk");
+    else
+      note_path(tm == 4 ? "gemm_tc_m512_n128" : tm == 2 ? "gemm_tc_m256_n128" : "gemm_tc_m128_n128");
+  }
   return rc;
 }
 
@@ -484,7 +554,7 @@ int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t 
     note_launch();
     a16 = scratch;
   }
-  const int rc = launch_gemm(st, w, gs->m128, a16, lda, M, d_y, ldy);
+  const int rc = launch_gemm(st, w, gs->m128, a16, lda, M, d_y, ldy, true);
   scratch_free(scratch, st);
   return rc;
 }
@@ -514,7 +584,7 @@ int run_gemm_staged(cudaStream_t st, const Weights& w, const void* d_a, int a_dt
     MSQ_CUDA_TRY(cudaGetLastError(), "staging launch");
     a16 = staging;
   }
-  return launch_gemm(st, w, m128, a16, lda, M, d_y, ldy);
+  return launch_gemm(st, w, m128, a16, lda, M, d_y, ldy, false);  // no scratch for k-splits here
 }
 
 void release_gemm_state(Weights& w) {

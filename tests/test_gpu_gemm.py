@@ -56,6 +56,32 @@ def test_gemm_prefill_config_fp16(cuda_device, M):
     assert oracle.rel_l2(got, ref) <= TOL_TC
 
 
+@pytest.mark.parametrize("M,N_,K,bs", [
+    (32, 2048, 28672, 128),   # a 4-GPU shard of the 70B down-projection: 16 tiles, K split 9 ways
+    (32, 256, 8192, 32),      # 2 tiles
+    (100, 640, 1000, 64),     # ragged K: the last split is short
+])
+def test_gemm_split_k(cuda_device, M, N_, K, bs):
+    """Tiles that leave SMs idle split K across CTAs; partial tiles are summed in a fixed order,
+    so two runs agree bit for bit."""
+    c = synth.make_case(35, M, N_, K, 4, bs, "packed", scale_lo=0.001, scale_hi=0.01)
+    w = QuantizedWeights(c["b"], c["scales"], c["zp"], N_, K, 4, bs, device=cuda_device)
+    a_t = torch.from_numpy(c["a"]).to(cuda_device).reshape(M, K)
+    y1 = w.matmul(a_t, path=N.PATH_GEMM)
+    assert N.last_path().endswith("_splitk")
+    y2 = w.matmul(a_t, path=N.PATH_GEMM)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
+    assert oracle.rel_l2(y1.cpu().numpy(), oracle.managed(c)) <= TOL_TC
+    w.free()
+
+
+def test_gemm_full_grid_does_not_split(cuda_device):
+    c = synth.make_case(36, 2048, 14336, 256, 4, 32, "packed", a_dtype="f16", scale_dtype="f16")
+    gemm(c, cuda_device)
+    assert N.last_path() == "gemm_tc_m512_n128"
+
+
 def test_gemm_auto_routes_prefill(cuda_device):
     c = synth.make_case(32, 40, 640, 1024, 4, 128, "packed")
     w = QuantizedWeights(c["b"], c["scales"], c["zp"], 640, 1024, 4, 128, device=cuda_device)
