@@ -75,6 +75,18 @@ def peaks() -> tuple[float, str]:
     return FALLBACK_HBM_GBS, "fallback"
 
 
+def tensor_peak() -> tuple[float, str]:
+    """Dense bf16 tensor peak for kernels timed inside a long step: the measured sustained cuBLAS
+    rate, else the fallback sustained figure."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops_sustained"]), "measured sustained cuBLAS bf16"
+        except Exception:
+            pass
+    return 1400.0, "fallback sustained bf16"
+
+
 # ---------------------------------------------------------------- clocks (NVML, in-process)
 class ClockSampler:
     """Samples SM clock and throttle reasons every ~2 ms on a background thread."""
@@ -380,6 +392,7 @@ def run_nsplit(args, rank: int, world: int, local_rank: int):
     import torch
     import torch.distributed as dist
 
+    from modelsharp_b200 import _native as N
     from modelsharp_b200 import synth
     from modelsharp_b200.nsplit import ShardedMatMulNBits
 
@@ -412,8 +425,10 @@ def run_nsplit(args, rank: int, world: int, local_rank: int):
     graphs, outs = [], []
     for r in range(reps_n):
         g = torch.cuda.CUDAGraph()
+        c0 = N.launch_count()
         with torch.cuda.graph(g, stream=stream):
             outs.append(step(r, a0))
+        per_step_launches = N.launch_count() - c0  # library kernels in one step (GEMV / GEMM, split-K reduce)
         graphs.append(g)
     with torch.cuda.stream(stream):
         for i in range(max(args.warmup, 3)):
@@ -470,6 +485,17 @@ def run_nsplit(args, rank: int, world: int, local_rank: int):
 
     peak, peak_kind = peaks()
     per_rank_achieved = shard_bytes / (ms / args.steps * 1e-3) / 1e9
+    flops = 2.0 * M * sum(n * k for k, n in NSPLIT_LAYERS)  # whole step, all ranks
+    if M >= 17:  # the tensor-core GEMM: a contraction, bounded by the tensor pipe
+        tc_peak = tensor_peak()
+        tflops_rank = flops / world / (ms / args.steps * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": tflops_rank, "peak": tc_peak[0], "unit": "TFLOP/s",
+                "frac": tflops_rank / tc_peak[0], "traffic": None, "peak_source": tc_peak[1],
+                "note": "per-rank FLOPs over the whole step time (all-gathers included)"}
+    else:
+        roof = {"bound": "hbm", "achieved": per_rank_achieved, "peak": peak, "unit": "GB/s",
+                "frac": per_rank_achieved / peak, "traffic": None, "peak_source": f"{peak_kind} HBM copy bandwidth",
+                "note": "per-rank shard bytes over the whole step time (all-gathers included)"}
     if rank == 0:
         from oracle import oracle
         # parity of the assembled output against the checker chain (up-proj output fed to the down-proj)
@@ -497,17 +523,16 @@ def run_nsplit(args, rank: int, world: int, local_rank: int):
                        "l2": f"{reps_n} replicas of each rank's shards rotate ({reps_n * shard_bytes / 1e6:.0f} MB per rank)",
                        "launch": ("one CUDA graph replay per step: 2 GEMV launches that store into every rank's "
                                   "Y over NVLink and signal completion" if gather == "p2p" else
-                                  "one CUDA graph replay per step (2 local GEMV launches + 2 NCCL all-gathers)"),
-                       "gather": gather,
+                                  f"one CUDA graph replay per step: {per_step_launches} library launches "
+                                  f"({'tensor-core GEMM' if M >= 17 else 'decode GEMV'}) + 2 NCCL all-gathers"),
+                       "gather": gather, "flops_per_step": flops,
+                       "tflops": flops / (ms / args.steps * 1e-3) / 1e12,
                        "parity_rel_l2": parity},
-            "roofline": {"bound": "hbm", "achieved": per_rank_achieved, "peak": peak, "unit": "GB/s",
-                         "frac": per_rank_achieved / peak, "traffic": None,
-                         "peak_source": f"{peak_kind} HBM copy bandwidth",
-                         "note": "per-rank shard bytes over the whole step time (all-gathers included)"},
+            "roofline": roof,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": a_host.numel() * 2,
                     "d2h_bytes_per_step": y_host.numel() * 4, "steps": e2e_steps, "entry": "ShardedMatMulNBits"},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": per_step_launches * args.steps,
             "clocks": clk.summary(),
         }
         print(json.dumps(out), flush=True)
