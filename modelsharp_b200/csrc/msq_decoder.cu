@@ -129,12 +129,27 @@ __global__ void rope_append_kernel(float* __restrict__ qkv, int heads, int kv, i
 constexpr int kGqaSplit = 8;   // blocks per cluster: one cluster per kv head
 constexpr int kGqaWarps = 16;  // warps per block
 
-// Half-split rotary of the float4s x (elements 128 j + 4 l .. + 3 of a d-row) at the table rows
-// cs / sn (d / 2 entries each). Element e pairs with e + d/2 (first half) or e - d/2: for
-// d <= 128 in lane l ^ (d / 8), for d = 256 in the other float4 of the same lane.
+// The rotary table entries (cos, sin) of the elements 128 j + 4 l .. + 3 of a d-row at the
+// table rows cs / sn (d / 2 entries each): element e uses entry e mod d/2.
 template <int DV>
-__device__ __forceinline__ void rope4(float4 (&x)[DV], int l, int d, const float* __restrict__ cs,
-                                      const float* __restrict__ sn) {
+__device__ __forceinline__ void rope_tables4(float4 (&cv)[DV], float4 (&sv)[DV], int l, int d,
+                                             const float* __restrict__ cs, const float* __restrict__ sn) {
+  const int half = d >> 1;
+#pragma unroll
+  for (int j = 0; j < DV; ++j) {
+    const int c = 128 * j + 4 * l;
+    const int e = c < half ? c : c - half;
+    cv[j] = c < d ? *reinterpret_cast<const float4*>(cs + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+    sv[j] = c < d ? *reinterpret_cast<const float4*>(sn + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+// Half-split rotary of the float4s x (elements 128 j + 4 l .. + 3 of a d-row) with their table
+// entries cv / sv. Element e pairs with e + d/2 (first half) or e - d/2: for d <= 128 in lane
+// l ^ (d / 8), for d = 256 in the other float4 of the same lane.
+template <int DV>
+__device__ __forceinline__ void rope4(float4 (&x)[DV], int l, int d, const float4 (&cvv)[DV],
+                                      const float4 (&svv)[DV]) {
   const int half = d >> 1;
   float4 pr[DV];
   if constexpr (DV == 1) {
@@ -152,8 +167,7 @@ __device__ __forceinline__ void rope4(float4 (&x)[DV], int l, int d, const float
     const int c = 128 * j + 4 * l;
     if (c < d) {
       const bool first = c < half;
-      const int e = first ? c : c - half;
-      const float4 cv = *reinterpret_cast<const float4*>(cs + e), sv = *reinterpret_cast<const float4*>(sn + e);
+      const float4 cv = cvv[j], sv = svv[j];
       const float sg = first ? -1.f : 1.f;
       x[j] = make_float4(x[j].x * cv.x + sg * (pr[j].x * sv.x), x[j].y * cv.y + sg * (pr[j].y * sv.y),
                          x[j].z * cv.z + sg * (pr[j].z * sv.z), x[j].w * cv.w + sg * (pr[j].w * sv.w));
@@ -246,7 +260,9 @@ __global__ void __launch_bounds__(kGqaWarps * 32) gqa_decode_kernel(
   const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
   const int half = d >> 1;
 
-  float4 qr[GM][DV];
+  // every load that does not depend on the cache is issued here, together
+  const bool owner = cur && r == kGqaSplit - 1 && w == 0;  // rotates, appends and attends the current key
+  float4 qr[GM][DV], cv[DV], sv[DV], kcur[DV], vcur[DV];
 #pragma unroll
   for (int h = 0; h < GM; ++h)
 #pragma unroll
@@ -254,9 +270,22 @@ __global__ void __launch_bounds__(kGqaWarps * 32) gqa_decode_kernel(
       const int c = 128 * j + 4 * l;
       qr[h][j] = (h < G && c < d) ? *reinterpret_cast<const float4*>(q + ((int64_t)g * G + h) * d + c) : z4;
     }
+#pragma unroll
+  for (int j = 0; j < DV; ++j) cv[j] = sv[j] = kcur[j] = vcur[j] = z4;
+  if (cur) rope_tables4<DV>(cv, sv, l, d, cos_t + pos * half, sin_t + pos * half);
+  if (owner) {
+#pragma unroll
+    for (int j = 0; j < DV; ++j) {
+      const int c = 128 * j + 4 * l;
+      if (c < d) {
+        kcur[j] = *reinterpret_cast<const float4*>(q + ((int64_t)heads + g) * d + c);
+        vcur[j] = *reinterpret_cast<const float4*>(q + ((int64_t)heads + kv + g) * d + c);
+      }
+    }
+  }
   if (cur) {
 #pragma unroll
-    for (int h = 0; h < GM; ++h) rope4<DV>(qr[h], l, d, cos_t + pos * half, sin_t + pos * half);
+    for (int h = 0; h < GM; ++h) rope4<DV>(qr[h], l, d, cv, sv);
   }
   float mw[GM], lw[GM];
   float4 acc[GM][DV];
@@ -280,24 +309,18 @@ __global__ void __launch_bounds__(kGqaWarps * 32) gqa_decode_kernel(
       }
     attend_batch<GM, DV, KB>(qr, kr, vr, min(KB, hi - t0), scale, mw, lw, acc);
   }
-  if (cur && r == kGqaSplit - 1 && w == 0) {  // the current key: rotate, append, attend
+  if (owner) {  // the current key: rotate, append, attend
     float4 kr[KB][DV], vr[KB][DV];
 #pragma unroll
     for (int i = 0; i < KB; ++i)
 #pragma unroll
       for (int j = 0; j < DV; ++j) kr[i][j] = vr[i][j] = z4;
 #pragma unroll
-    for (int j = 0; j < DV; ++j) {
-      const int c = 128 * j + 4 * l;
-      if (c < d) {
-        kr[0][j] = *reinterpret_cast<const float4*>(q + ((int64_t)heads + g) * d + c);
-        vr[0][j] = *reinterpret_cast<const float4*>(q + ((int64_t)heads + kv + g) * d + c);
-      }
-    }
+    for (int j = 0; j < DV; ++j) vr[0][j] = vcur[j];
     float4 k1[DV];
 #pragma unroll
-    for (int j = 0; j < DV; ++j) k1[j] = kr[0][j];
-    rope4<DV>(k1, l, d, cos_t + pos * half, sin_t + pos * half);
+    for (int j = 0; j < DV; ++j) k1[j] = kcur[j];
+    rope4<DV>(k1, l, d, cv, sv);
 #pragma unroll
     for (int j = 0; j < DV; ++j) {
       kr[0][j] = k1[j];
