@@ -1,0 +1,87 @@
+"""Host-side checks of the decoder around the op (no GPU).
+
+* the 7B shape's MatMulNBits bytes per decoded token (the unit of the decode roofline);
+* the CPU checker's decoder (oracle/decoder.py) against itself: a token decoded through the
+  KV cache gives the logits of a full pass over the whole sequence, so the cache, rotary
+  positions and causal masking of the checker are consistent before the GPU is compared
+  with it;
+* the algebra the fused decode GEMV relies on: RMSNorm folded in as x * gamma with the
+  1/rms scale applied to the dot product equals norm-then-MatMulNBits to fp32 rounding.
+"""
+import numpy as np
+import pytest
+
+from modelsharp_b200.decoder import DecoderConfig, make_weights, proj_shapes, weight_bytes_per_token, weights_to_host
+from oracle import decoder as od
+from oracle import oracle
+
+TINY = DecoderConfig(layers=2, hidden=64, heads=4, kv_heads=2, head_dim=16, inter=96, vocab=50, max_seq=24)
+
+
+def test_7b_bytes_per_token():
+    assert weight_bytes_per_token(DecoderConfig()) == 4_555_096_064
+
+
+def test_projection_shapes_agree_with_checker():
+    for cfg in (DecoderConfig(), TINY):
+        assert proj_shapes(cfg) == od.proj_shapes(cfg)
+
+
+@pytest.fixture(scope="module")
+def tiny_weights():
+    return weights_to_host(make_weights(TINY, 5, "cpu"))
+
+
+def _cache(cfg):
+    return {"k": np.zeros((cfg.layers, cfg.kv_heads, cfg.max_seq, cfg.head_dim), np.float32),
+            "v": np.zeros((cfg.layers, cfg.kv_heads, cfg.max_seq, cfg.head_dim), np.float32),
+            "rope": od.rope_tables(cfg)}
+
+
+def test_checker_cached_decoding_equals_full_pass(tiny_weights):
+    rng = np.random.default_rng(3)
+    tokens = rng.integers(0, TINY.vocab, 12)
+    full = od.forward(tiny_weights, TINY, tokens, 0, _cache(TINY))       # [12, vocab]
+    cache = _cache(TINY)
+    od.forward(tiny_weights, TINY, tokens[:7], 0, cache)
+    for p in range(7, 12):
+        step = od.forward(tiny_weights, TINY, tokens[p:p + 1], p, cache)[0]
+        assert oracle.rel_l2(step, full[p]) <= 1e-5
+
+
+def test_checker_generate_is_greedy(tiny_weights):
+    prompt = np.asarray([1, 7, 3, 9])
+    toks, logits = od.generate(tiny_weights, TINY, prompt, 5)
+    assert len(toks) == 5 and len(logits) == 5
+    for t, lg in zip(toks, logits):
+        assert t == int(np.argmax(lg))
+
+
+def test_rope_tables_and_single_key_attention():
+    cos, sin = od.rope_tables(TINY)
+    np.testing.assert_allclose(cos * cos + sin * sin, 1.0, rtol=1e-6)
+    np.testing.assert_array_equal(cos[0], 1.0)
+    np.testing.assert_array_equal(sin[0], 0.0)
+    rng = np.random.default_rng(4)
+    q = rng.standard_normal((1, TINY.heads * TINY.head_dim)).astype(np.float32)
+    kc = rng.standard_normal((TINY.kv_heads, TINY.max_seq, TINY.head_dim)).astype(np.float32)
+    vc = rng.standard_normal((TINY.kv_heads, TINY.max_seq, TINY.head_dim)).astype(np.float32)
+    out = od.attention(q, kc, vc, 0, TINY).reshape(TINY.heads, TINY.head_dim)
+    group = TINY.heads // TINY.kv_heads
+    for h in range(TINY.heads):  # one visible key: the output is its value row
+        np.testing.assert_allclose(out[h], vc[h // group, 0], rtol=1e-6)
+
+
+@pytest.mark.parametrize("bs", [32, 128])
+def test_rmsnorm_folded_into_the_dot_product(bs):
+    """(x * gamma) . W^T scaled by 1/rms equals rms_norm(x) . W^T to fp32 rounding."""
+    from modelsharp_b200 import synth
+    K, N_ = 512, 96
+    c = synth.make_case(9, 2, N_, K, 4, bs, "packed", scale_lo=0.001, scale_hi=0.01)
+    rng = np.random.default_rng(bs)
+    x = (rng.standard_normal((2, K)) * 3).astype(np.float32)
+    gamma = rng.uniform(0.8, 1.2, K).astype(np.float32)
+    ref = oracle.managed(dict(c, a=od.rms_norm(x, gamma, 1e-5), M=2))
+    inv = 1.0 / np.sqrt(np.mean(x.astype(np.float64) ** 2, axis=1, keepdims=True) + 1e-5)
+    folded = oracle.managed(dict(c, a=(x * gamma).astype(np.float32), M=2)) * inv
+    assert oracle.rel_l2(folded, ref) <= 1e-6
