@@ -373,7 +373,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
     // B fragments of this warp's units (digits of columns grp + 8j), held across row blocks
     uint32_t bf[UPW][STEPS][NT][2];
     float sv[UPW][UB][NT];    // block sums of a_int for this lane's A row(s), 0 on odd lanes
-    float sif[UPW][UB][NT];   // 2^-sigma of those blocks
+    float sv16[UPW][UB][NT];  // the same x 16, for the high-nibble rows' zero-point term
+    float gw0[UPW][UB][NT];   // 2^-sigma of those blocks x this lane's digit weight (1 or 2^16)
+    float gw1[UPW][UB][NT];   // the same / 16: undoes the 16 q of the high-nibble rows
 #pragma unroll
     for (int uu = 0; uu < UPW; ++uu) {
       const int u = warp + uu * kConsumers;
@@ -394,9 +396,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
         for (int nt = 0; nt < NT; ++nt) {
           const int m = nt * 2 + (tq >> 1);
           const bool okb = u < units && m < mc;
-          // the zero-point term rides on the lanes of digits 0 and 1 (even tq) only
+          // the zero-point term rides on the lanes of digits 0 and 1 (even tq) only; every
+          // factor below is the block scale times a power of two, so the products are exact
           sv[uu][bl][nt] = okb && (tq & 1) == 0 ? (float)sblk[m * nbp + kk0 / BS + bl] : 0.f;
-          sif[uu][bl][nt] = okb ? sinv[m * nbp + kk0 / BS + bl] : 0.f;
+          sv16[uu][bl][nt] = 16.f * sv[uu][bl][nt];
+          const float g = okb ? sinv[m * nbp + kk0 / BS + bl] : 0.f;
+          gw0[uu][bl][nt] = g * wdig;
+          gw1[uu][bl][nt] = g * wdig * 0.0625f;
         }
     }
 
@@ -408,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
         const float* scp = reinterpret_cast<const float*>(base + p.off_sc);
         // Both units of this warp as independent chains, each block's k32 steps split over
         // two accumulators, so the tensor-core latency overlaps; a missing second unit
-        // (kt < 32 units) reads unit 0's words and contributes nothing (its sif is 0).
+        // (kt < 32 units) reads unit 0's words and contributes nothing (its gw0 and gw1 are 0).
         uint32_t wv[UPW][4 * CH];
         float s0[UPW][UB], s1[UPW][UB], z0[UPW][UB], z1[UPW][UB];
 #pragma unroll
@@ -428,19 +434,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
           for (int bl = 0; bl < UB; ++bl) {
             const int blk_local = ul * UB + bl;
             s0[uu][bl] = scp[blk_local * 16 + grp];
-            s1[uu][bl] = scp[blk_local * 16 + grp + 8] * 0.0625f;  // undoes the 16 q
-            // z1 is for the high-nibble rows, whose products come out 16x (see below)
+            s1[uu][bl] = scp[blk_local * 16 + grp + 8];
+            // z1 is for the high-nibble rows, whose products come out 16x (sv16 carries the 16)
             if (p.zp_kind == ZP_PACKED) {
               const uint2 zw = reinterpret_cast<const uint2*>(base + p.off_zp)[blk_local];
               z0[uu][bl] = (float)((zw.x >> (4 * grp)) & 0xF);
-              z1[uu][bl] = (float)((zw.y >> (4 * grp)) & 0xF) * 16.f;
+              z1[uu][bl] = (float)((zw.y >> (4 * grp)) & 0xF);
             } else if (p.zp_kind == ZP_F32) {
               const float* zf = reinterpret_cast<const float*>(base + p.off_zp);
               z0[uu][bl] = zf[blk_local * 16 + grp];
-              z1[uu][bl] = zf[blk_local * 16 + grp + 8] * 16.f;
+              z1[uu][bl] = zf[blk_local * 16 + grp + 8];
             } else {
               z0[uu][bl] = 8.f;
-              z1[uu][bl] = 128.f;
+              z1[uu][bl] = 8.f;
             }
           }
         }
@@ -481,14 +487,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
 #pragma unroll
               for (int j = 0; j < 4; ++j) cc[j] = c[uu][bl][0][nt][j] + c[uu][bl][1][nt][j];
               // even lanes hold digits 0 and 1 (and the zero-point term), odd lanes digit 2
-              // and the always-zero fourth column: f = (c_a + 256 c_b) * wdig - z * S, the
-              // integer combination exact in s32 (|c| < 2^22 even for the 16x rows)
-              const float zs = sv[uu][bl][nt];
-              const float f0 = fmaf((float)(cc[0] + 256 * cc[1]), wdig, -z0[uu][bl] * zs);
-              const float f1 = fmaf((float)(cc[2] + 256 * cc[3]), wdig, -z1[uu][bl] * zs);
-              const float g = sif[uu][bl][nt];
-              y0[nt] = fmaf(s0[uu][bl] * g, f0, y0[nt]);
-              y1[nt] = fmaf(s1[uu][bl] * g, f1, y1[nt]);
+              // and the always-zero fourth column: y += s 2^-sigma wdig (c_a + 256 c_b - z S / wdig)
+              // with S = 0 on odd lanes, the integer combination exact in s32 (|c| < 2^22 even
+              // for the 16x rows)
+              const float f0 = fmaf(-z0[uu][bl], sv[uu][bl][nt], (float)(cc[0] + 256 * cc[1]));
+              const float f1 = fmaf(-z1[uu][bl], sv16[uu][bl][nt], (float)(cc[2] + 256 * cc[3]));
+              y0[nt] = fmaf(s0[uu][bl] * gw0[uu][bl][nt], f0, y0[nt]);
+              y1[nt] = fmaf(s1[uu][bl] * gw1[uu][bl][nt], f1, y1[nt]);
             }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
