@@ -45,9 +45,9 @@ WORKLOAD = ("7B decode GEMV sweep (BASELINE configs[1]) at M=1: (K,N) = (4096,40
             "(4096,14336), (14336,4096), (4096,32000); bits=4, block_size=128, packed zero points, fp32 A and "
             "scales")
 FALLBACK_HBM_GBS = 6650.0
-# dram bytes per algorithmic byte of the decode GEMV, from the ncu capture summarised in
-# profiles/gemv_q4_decode_7b_sweep.md (K=4096, N=14336, one launch).
-NCU_DRAM_PER_ALG_BYTE = 31505152 / 31424512
+# DRAM bytes (read + write) per algorithmic byte of the decode GEMV, measured by an ncu
+# capture of one K=4096, N=14336 launch of this bench's sweep.
+NCU_DRAM_PER_ALG_BYTE = 31474688 / 31424512
 
 
 def log(*a):
