@@ -21,6 +21,7 @@ import numpy as np
 import torch
 
 from . import _native as N
+from .errors import ModelSharpException
 from .weights import QuantizedWeights
 
 PROJ = ("q", "k", "v", "o", "gate", "up", "down")
@@ -231,3 +232,135 @@ class CudaDecoder:
             for name in ("qkv", "o", "gate_up", "down"):
                 lw[name].free()
         self.lm_head.free()
+
+
+# ---------------------------------------------------------------- the same decoder as a graph
+def build_decoder_graph(cfg: DecoderConfig, weights: dict, device: torch.device | str):
+    """The decoder as an in-memory graph of the op types an INT4 decoder export uses, for the
+    engine's node loop (one token per run).
+
+    Inputs: `input_ids` int64 [1, 1] and `seqlens_k` int64 [1] (the token's position), both on
+    the device. Outputs: `logits` [1, 1, vocab] and `next_token` int64 [1, 1] (greedy). Per
+    layer: SimplifiedLayerNormalization (layer 0) or SkipSimplifiedLayerNormalization (the
+    residual add of the previous layer), MatMulNBits of the packed q/k/v, GroupQueryAttention
+    (packed QKV, rotary in the op, the layer's KV cache as past/present), MatMulNBits o,
+    SkipSimplifiedLayerNormalization, MatMulNBits gate and up, Sigmoid and two Mul (SwiGLU),
+    MatMulNBits down; then the final SkipSimplifiedLayerNormalization, the LM head and ArgMax.
+    The KV caches are initializers the attention nodes update in place."""
+    from .kernels import GraphNode, ModelGraph
+    dev = torch.device(device)
+    n_q, n_kv = cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
+    init: dict = {"embed": weights["embed"], "final_norm": weights["norm_final"]}
+    half = cfg.head_dim // 2
+    inv = cfg.rope_theta ** (-np.arange(half, dtype=np.float64) * 2.0 / cfg.head_dim)
+    ang = np.arange(cfg.max_seq, dtype=np.float64)[:, None] * inv[None, :]
+    init["cos_cache"] = torch.from_numpy(np.cos(ang).astype(np.float32)).to(dev)
+    init["sin_cache"] = torch.from_numpy(np.sin(ang).astype(np.float32)).to(dev)
+    nodes: list = []
+
+    def mnb(name: str, a: str, w: dict, n: int, k: int, out: str) -> None:
+        init[f"{name}.B"] = w["b"]
+        init[f"{name}.scales"] = w["scales"].reshape(-1)
+        init[f"{name}.zero_points"] = w["zp"]
+        nodes.append(GraphNode("MatMulNBits", name, [a, f"{name}.B", f"{name}.scales", f"{name}.zero_points"], [out],
+                               {"N": n, "K": k, "bits": 4, "block_size": cfg.block_size}))
+
+    eps = {"epsilon": cfg.eps}
+    nodes.append(GraphNode("Gather", "embed", ["embed", "input_ids"], ["x_0"], {"axis": 0}))
+    resid, pending = "x_0", None  # pending: the previous layer's down-projection output
+    for li, lw in enumerate(weights["layers"]):
+        p = f"l{li}."
+        init[p + "attn_norm"], init[p + "mlp_norm"] = lw["norm_attn"], lw["norm_mlp"]
+        cache = (1, cfg.kv_heads, cfg.max_seq, cfg.head_dim)
+        init[p + "past_key"] = torch.zeros(cache, device=dev)
+        init[p + "past_value"] = torch.zeros(cache, device=dev)
+        if pending is None:
+            nodes.append(GraphNode("SimplifiedLayerNormalization", p + "attn_norm", [resid, p + "attn_norm"],
+                                   [p + "h"], eps))
+        else:
+            nodes.append(GraphNode("SkipSimplifiedLayerNormalization", p + "attn_norm",
+                                   [pending, resid, p + "attn_norm"], [p + "h", "", "", p + "resid_a"], eps))
+            resid = p + "resid_a"
+        mnb(p + "qkv", p + "h", _cat([lw["q"], lw["k"], lw["v"]]), n_q + 2 * n_kv, cfg.hidden, p + "qkv")
+        nodes.append(GraphNode("GroupQueryAttention", p + "attn",
+                               [p + "qkv", "", "", p + "past_key", p + "past_value", "seqlens_k", "",
+                                "cos_cache", "sin_cache"],
+                               [p + "attn", p + "present_key", p + "present_value"],
+                               {"num_heads": cfg.heads, "kv_num_heads": cfg.kv_heads, "do_rotary": 1}))
+        mnb(p + "o", p + "attn", lw["o"], cfg.hidden, n_q, p + "o")
+        nodes.append(GraphNode("SkipSimplifiedLayerNormalization", p + "mlp_norm", [p + "o", resid, p + "mlp_norm"],
+                               [p + "h2", "", "", p + "resid_b"], eps))
+        resid = p + "resid_b"
+        mnb(p + "gate", p + "h2", lw["gate"], cfg.inter, cfg.hidden, p + "gate")
+        mnb(p + "up", p + "h2", lw["up"], cfg.inter, cfg.hidden, p + "up")
+        nodes.append(GraphNode("Sigmoid", p + "sig", [p + "gate"], [p + "sig"]))
+        nodes.append(GraphNode("Mul", p + "silu", [p + "gate", p + "sig"], [p + "silu"]))
+        nodes.append(GraphNode("Mul", p + "act", [p + "silu", p + "up"], [p + "act"]))
+        mnb(p + "down", p + "act", lw["down"], cfg.hidden, cfg.inter, p + "down")
+        pending = p + "down"
+    nodes.append(GraphNode("SkipSimplifiedLayerNormalization", "final_norm", [pending, resid, "final_norm"],
+                           ["h_final", "", "", "resid_final"], eps))
+    mnb("lm_head", "h_final", weights["lm_head"], cfg.vocab, cfg.hidden, "logits")
+    nodes.append(GraphNode("ArgMax", "argmax", ["logits"], ["next_token"], {"axis": -1, "keepdims": 0}))
+    return ModelGraph(["input_ids", "seqlens_k"], ["logits", "next_token"], nodes, init)
+
+
+class EngineDecoder:
+    """Greedy decoding through the engine: the graph of build_decoder_graph run by CudaEngine
+    on the registry of llm_ops (MatMulNBits and the decoder's other op types on the device),
+    one token per run. The prompt goes through the same one-token runs, position by position."""
+
+    def __init__(self, cfg: DecoderConfig, weights: dict, device: torch.device | str):
+        from .engine import CudaEngine
+        from .llm_ops import create_decoder_registry
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.graph = build_decoder_graph(cfg, weights, self.device)
+        self.engine = CudaEngine(self.graph, create_decoder_registry(self.device))
+        self._graph = None
+
+    def step(self, tok: torch.Tensor, pos: int) -> dict:
+        """One run: tok int64 [1, 1] on the device at position pos."""
+        if self._graph is not None:
+            self._tok.copy_(tok.reshape(1, 1))
+            self._pos.fill_(pos)
+            self._graph.replay()
+            return self._out
+        p = torch.full((1,), pos, dtype=torch.int64, device=self.device)
+        return self.engine.run({"input_ids": tok, "seqlens_k": p})
+
+    def capture(self) -> None:
+        """Captures one engine run in a CUDA graph over fixed input buffers; later steps copy
+        the token and position in and replay it (every value of a run stays on the device and
+        the positions are read there, so the node loop's launches replay unchanged). The
+        warm-up run before the capture writes cache row 0, which the next prompt rewrites."""
+        self._tok = torch.zeros(1, 1, dtype=torch.int64, device=self.device)
+        self._pos = torch.zeros(1, dtype=torch.int64, device=self.device)
+        cur = torch.cuda.current_stream(self.device)
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(cur)
+        with torch.cuda.stream(s):
+            self.engine.run({"input_ids": self._tok, "seqlens_k": self._pos})
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                self._out = self.engine.run({"input_ids": self._tok, "seqlens_k": self._pos})
+        cur.wait_stream(s)
+        self._graph = g
+
+    def release(self) -> None:
+        self._graph, self._out = None, None
+
+    def generate(self, prompt: torch.Tensor, n_new: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """The n_new greedy tokens after the prompt, and the logits that chose the first."""
+        ids = prompt.to(self.device, torch.int64).reshape(-1)
+        if ids.numel() + n_new - 1 > self.cfg.max_seq:
+            raise ModelSharpException(f"prompt of {ids.numel()} tokens + {n_new} new exceeds max_seq {self.cfg.max_seq}")
+        out = None
+        for i in range(ids.numel()):
+            out = self.step(ids[i:i + 1].reshape(1, 1), i)
+        first_logits = out["logits"].reshape(-1).clone()
+        toks = [out["next_token"].reshape(1).clone()]
+        for j in range(1, n_new):
+            out = self.step(toks[-1].reshape(1, 1), ids.numel() + j - 1)
+            toks.append(out["next_token"].reshape(1).clone())
+        return torch.cat(toks), first_logits

@@ -85,3 +85,42 @@ def test_rmsnorm_folded_into_the_dot_product(bs):
     inv = 1.0 / np.sqrt(np.mean(x.astype(np.float64) ** 2, axis=1, keepdims=True) + 1e-5)
     folded = oracle.managed(dict(c, a=(x * gamma).astype(np.float32), M=2)) * inv
     assert oracle.rel_l2(folded, ref) <= 1e-6
+
+
+def test_decoder_graph_is_wired_for_the_engine():
+    """Every node input is a graph input, an initializer or an earlier node's output, and every
+    op type has a kernel in the decoder registry."""
+    from modelsharp_b200.decoder import build_decoder_graph
+    from modelsharp_b200.llm_ops import create_decoder_registry
+    w = make_weights(TINY, 5, "cpu")
+    g = build_decoder_graph(TINY, w, "cpu")
+    known = set(g.inputs) | set(g.initializers)
+    reg = create_decoder_registry("cpu")
+    for node in g.nodes:
+        for name in node.inputs:
+            assert name == "" or name in known, (node.name, name)
+        known |= {o for o in node.outputs if o}
+        assert reg.try_get(node.op_type)[0], node.op_type
+    assert set(g.outputs) <= known
+    ops = [n.op_type for n in g.nodes]
+    assert ops.count("MatMulNBits") == 5 * TINY.layers + 1
+    assert ops.count("GroupQueryAttention") == TINY.layers
+    assert g.initializers["l0.past_key"].shape == (1, TINY.kv_heads, TINY.max_seq, TINY.head_dim)
+
+
+def test_engine_rejects_unknown_ops_and_unsupported_forms():
+    from modelsharp_b200 import CudaEngine, GraphContext, GraphNode, ModelGraph, UnsupportedOperatorException
+    from modelsharp_b200.errors import ModelSharpException
+    from modelsharp_b200.llm_ops import GroupQueryAttentionKernel, create_decoder_registry
+    g = ModelGraph(["x"], ["y"], [GraphNode("RotaryEmbedding", "r", ["x"], ["y"])])
+    with pytest.raises(UnsupportedOperatorException):
+        CudaEngine(g, create_decoder_registry("cpu")).run({"x": np.zeros(4, np.float32)})
+    gqa = GroupQueryAttentionKernel()
+    base = {"num_heads": 4, "kv_num_heads": 2, "do_rotary": 1}
+    unpacked = GraphNode("GroupQueryAttention", "a", ["q", "k", "v", "pk", "pv", "s", "", "c", "n"], ["o"], base)
+    with pytest.raises(ModelSharpException, match="packed QKV"):
+        gqa.execute(unpacked, GraphContext({}))
+    no_rotary = GraphNode("GroupQueryAttention", "a", ["q", "", "", "pk", "pv", "s", "", "c", "n"], ["o"],
+                          dict(base, do_rotary=0))
+    with pytest.raises(ModelSharpException, match="do_rotary"):
+        gqa.execute(no_rotary, GraphContext({}))
