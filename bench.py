@@ -727,6 +727,124 @@ DECODE_WORKLOAD = ("synthetic 7B-shaped INT4 decoder (BASELINE configs[4]): 32 l
                    "the prompt pass")
 
 
+def decode_checks(host_w, cfg, prompt_h, generate, args):
+    """Greedy parity on a 16-token prompt (4 tokens from `generate(prompt, n)` against the CPU
+    checker) and the checker's own decode rate as the CPU baseline."""
+    from oracle import decoder as od
+    short = prompt_h[:16]
+    ref, _ = od.generate(host_w, cfg, short.numpy(), 4)
+    got = generate(short, 4)
+    match = f"{int((got == ref).sum())}/4 greedy tokens equal (16-token prompt, exact path)"
+    cache = {"k": np.zeros((cfg.layers, cfg.kv_heads, cfg.max_seq, cfg.head_dim), np.float32),
+             "v": np.zeros((cfg.layers, cfg.kv_heads, cfg.max_seq, cfg.head_dim), np.float32),
+             "rope": od.rope_tables(cfg)}
+    od.forward(host_w, cfg, short.numpy()[:8], 0, cache)
+    t_0, n = time.perf_counter(), 0
+    while n < 2 or time.perf_counter() - t_0 < max(args.cpu_seconds, 0.1):
+        od.forward(host_w, cfg, short.numpy()[8 + n:9 + n], 8 + n, cache)
+        n += 1
+    dt = (time.perf_counter() - t_0) / n
+    cpu = {"value": 1.0 / dt, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+           "sample": f"{n} decode steps of the CPU restatement (C MatMulNBits restatement on all host "
+                     "threads, numpy glue) at context 8..16"}
+    return cpu, match
+
+
+def run_decode_engine(args, rank: int, world: int, local_rank: int):
+    """configs[4] through the engine: the decoder as a graph (build_decoder_graph) run by
+    CudaEngine's node loop on the CUDA registry, one token per run, each run a replay of one
+    captured engine run. The prompt goes through the same runs token by token. value = decode
+    tokens/s over 127 steps per generation."""
+    import torch
+    import torch.distributed as dist
+
+    from modelsharp_b200 import _native as N
+    from modelsharp_b200.decoder import DecoderConfig, EngineDecoder, make_weights, weight_bytes_per_token
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    cfg = DecoderConfig(layers=args.layers)
+    w = make_weights(cfg, 0, dev)
+    eng = EngineDecoder(cfg, w, dev)
+    host_w = None
+    if rank == 0 and world == 1:
+        from modelsharp_b200.decoder import weights_to_host
+        host_w = weights_to_host(w)
+    n_prompt, n_new = 512, 128
+    prompt_h = torch.randint(0, cfg.vocab, (n_prompt,), generator=torch.Generator().manual_seed(1))
+    prompt = prompt_h.to(dev)
+    c0 = N.launch_count()
+    eng.capture()
+    per_run = (N.launch_count() - c0) // 2  # the warm-up run and the captured run
+    stream = torch.cuda.current_stream(dev)
+    reps = max(2, args.steps // n_new)
+    pre_ms, dec_ms = 0.0, 0.0
+    gen = torch.empty(reps, n_new, dtype=torch.long, device=dev)
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(local_rank) as clk:
+        for r in range(reps):
+            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            e0.record(stream)
+            out = None
+            for i in range(n_prompt):
+                out = eng.step(prompt[i:i + 1].reshape(1, 1), i)
+            tok = out["next_token"].clone()
+            gen[r, 0] = tok[0, 0]
+            e1.record(stream)
+            for j in range(1, n_new):
+                out = eng.step(tok, n_prompt + j - 1)
+                tok = out["next_token"].clone()
+                gen[r, j] = tok[0, 0]
+            e2.record(stream)
+            stream.synchronize()
+            pre_ms += e0.elapsed_time(e1)
+            dec_ms += e1.elapsed_time(e2)
+    if world > 1:
+        t = torch.tensor([pre_ms, dec_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        pre_ms, dec_ms = (float(v) for v in t.tolist())
+    steps = reps * (n_new - 1)
+    ms_tok = dec_ms / steps
+    # e2e: host prompt in, host tokens out, prompt runs included
+    t0 = time.perf_counter()
+    toks, _ = eng.generate(prompt_h.pin_memory().to(dev, non_blocking=True), n_new)
+    toks_h = toks.cpu()
+    e2e_value = world * n_new / (time.perf_counter() - t0)
+    peak, peak_kind = peaks()
+    wb = weight_bytes_per_token(cfg)
+    achieved = wb / (ms_tok * 1e-3) / 1e9
+    if rank == 0:
+        cpu, match = None, None
+        if host_w is not None:
+            cpu, match = decode_checks(host_w, cfg, prompt_h, lambda short, n: eng.generate(short, n)[0].cpu().numpy(),
+                                       args)
+        res = {
+            "metric": "7B INT4 decode tok/s", "value": world * 1e3 / ms_tok, "unit": "tok/s", "n_gpus": world,
+            "steps": steps, "warmup": 2, "ms_per_step": ms_tok, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32 activations, int4 weights", "data": "synthetic",
+            "config": {"workload": ("engine path of: " + DECODE_WORKLOAD) if cfg.layers == 32 else
+                       f"{cfg.layers}-layer cut of the engine path (a profiling case, not the 7B shape)",
+                       "entry": "EngineDecoder: build_decoder_graph + CudaEngine on the llm_ops registry, one "
+                                "captured engine run replayed per token (unfused nodes: norms, Sigmoid/Mul SwiGLU, "
+                                "separate gate and up MatMulNBits)",
+                       "prompt_tokens": n_prompt, "new_tokens": n_new, "generations": reps,
+                       "prompt_ms": pre_ms / reps, "weight_bytes_per_token": wb, "parallelism": f"replicas{world}",
+                       "l2": "4.5 GB of weights per token, far above L2", "greedy_parity": match,
+                       "tokens_repeatable": bool((gen.cpu() == toks_h.reshape(1, -1)).all())},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "peak_source": f"{peak_kind} HBM copy bandwidth",
+                         "note": "MatMulNBits weight bytes per token over the whole engine run"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": n_prompt * 8,
+                    "d2h_bytes_per_step": n_new * 8, "entry": "EngineDecoder.generate (prompt runs included)"},
+            "gpu_launches": per_run * reps * (n_prompt + n_new - 1),
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(res), flush=True)
+    eng.release()
+
+
 def run_decode(args, rank: int, world: int, local_rank: int):
     """Per rank: prompt (512 tokens, tensor-core GEMM) then 127 decode steps, each one CUDA-graph
     replay (the first token comes from the prompt pass). value = decode tokens/s; the prompt
@@ -828,24 +946,9 @@ def run_decode(args, rank: int, world: int, local_rank: int):
     if rank == 0:
         cpu, match = None, None
         if host_w is not None:
-            from oracle import decoder as od
-            # greedy tokens on the exact path (every projection on the decode GEMV) against the checker
-            short = prompt_h[:16]
-            ref, _ = od.generate(host_w, cfg, short.numpy(), 4)
-            got = dec.generate(short.to(dev), 4, N.PATH_GEMV).cpu().numpy()
-            match = f"{int((got == ref).sum())}/4 greedy tokens equal (16-token prompt, exact path)"
-            cache = {"k": np.zeros((cfg.layers, cfg.kv_heads, cfg.max_seq, cfg.head_dim), np.float32),
-                     "v": np.zeros((cfg.layers, cfg.kv_heads, cfg.max_seq, cfg.head_dim), np.float32),
-                     "rope": od.rope_tables(cfg)}
-            od.forward(host_w, cfg, short.numpy()[:8], 0, cache)
-            t_0, n = time.perf_counter(), 0
-            while n < 2 or time.perf_counter() - t_0 < max(args.cpu_seconds, 0.1):
-                od.forward(host_w, cfg, short.numpy()[8 + n:9 + n], 8 + n, cache)
-                n += 1
-            dt = (time.perf_counter() - t_0) / n
-            cpu = {"value": 1.0 / dt, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-                   "sample": f"{n} decode steps of the CPU restatement (C MatMulNBits restatement on all host "
-                             "threads, numpy glue) at context 8..16"}
+            cpu, match = decode_checks(host_w, cfg, prompt_h,
+                                       lambda short, n: dec.generate(short.to(dev), n, N.PATH_GEMV).cpu().numpy(),
+                                       args)
         res = {
             "metric": "7B INT4 decode tok/s", "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps,
             "warmup": 2, "ms_per_step": ms_tok, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -885,6 +988,9 @@ def main():
                          "prefix of its own options)")
     ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
                     help="nsplit70b: fused peer-store gather (M <= 4) or NCCL all-gather")
+    ap.add_argument("--engine", action="store_true",
+                    help="decode7b: run the decoder graph through the engine (CudaEngine node loop) instead of "
+                         "the fused decode step")
     ap.add_argument("--layers", type=int, default=32,
                     help="decode7b: decoder layers (32 = the 7B shape; fewer only for small profiling cases)")
     ap.add_argument("--shapes", default="",
@@ -917,7 +1023,7 @@ def main():
         elif args.workload == "prefill":
             run_prefill(args, rank, world, local_rank)
         elif args.workload == "decode7b":
-            run_decode(args, rank, world, local_rank)
+            (run_decode_engine if args.engine else run_decode)(args, rank, world, local_rank)
         else:
             run_ours(args, rank, world, local_rank)
     finally:
