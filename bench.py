@@ -825,9 +825,9 @@ def run_decode_engine(args, rank: int, world: int, local_rank: int):
             "vs_baseline": None, "dtype": "f32 activations, int4 weights", "data": "synthetic",
             "config": {"workload": ("engine path of: " + DECODE_WORKLOAD) if cfg.layers == 32 else
                        f"{cfg.layers}-layer cut of the engine path (a profiling case, not the 7B shape)",
-                       "entry": "EngineDecoder: build_decoder_graph + CudaEngine on the llm_ops registry, one "
-                                "captured engine run replayed per token (unfused nodes: norms, Sigmoid/Mul SwiGLU, "
-                                "separate gate and up MatMulNBits)",
+                       "entry": "EngineDecoder: build_decoder_graph, the graph_fusion pass (norms, SwiGLU and "
+                                "residual adds into MatMulNBitsFused nodes), CudaEngine on the llm_ops registry, one "
+                                "captured engine run replayed per token",
                        "prompt_tokens": n_prompt, "new_tokens": n_new, "generations": reps,
                        "prompt_ms": pre_ms / reps, "weight_bytes_per_token": wb, "parallelism": f"replicas{world}",
                        "l2": "4.5 GB of weights per token, far above L2", "greedy_parity": match,

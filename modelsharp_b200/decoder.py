@@ -308,14 +308,19 @@ def build_decoder_graph(cfg: DecoderConfig, weights: dict, device: torch.device 
 class EngineDecoder:
     """Greedy decoding through the engine: the graph of build_decoder_graph run by CudaEngine
     on the registry of llm_ops (MatMulNBits and the decoder's other op types on the device),
-    one token per run. The prompt goes through the same one-token runs, position by position."""
+    one token per run. The prompt goes through the same one-token runs, position by position.
+    With fuse (the default) the graph first goes through graph_fusion.fuse_decode_graph, which
+    folds the norms, SwiGLU and residual adds into MatMulNBitsFused nodes."""
 
-    def __init__(self, cfg: DecoderConfig, weights: dict, device: torch.device | str):
+    def __init__(self, cfg: DecoderConfig, weights: dict, device: torch.device | str, fuse: bool = True):
         from .engine import CudaEngine
+        from .graph_fusion import fuse_decode_graph
         from .llm_ops import create_decoder_registry
         self.cfg = cfg
         self.device = torch.device(device)
         self.graph = build_decoder_graph(cfg, weights, self.device)
+        if fuse:
+            self.graph = fuse_decode_graph(self.graph)
         self.engine = CudaEngine(self.graph, create_decoder_registry(self.device))
         self._graph = None
 

@@ -210,15 +210,76 @@ class ArgMaxKernel:
         ctx.set(node.outputs[0], idx.reshape(shape))
 
 
+class MatMulNBitsFusedKernel(CudaMatMulNBitsKernel):
+    """MatMulNBits with decode-step glue folded in, the node graph_fusion writes.
+
+    Inputs [A, B, scales, zero_points, gamma, residual] (gamma and residual optional), attributes
+    of MatMulNBits plus `swiglu` and `epsilon`. With gamma, A rows are RMSNorm inputs (the norm is
+    applied on the way in); with swiglu=1, A rows are [gate | up] of 2K and the product uses
+    silu(gate) * up; with residual, the product is added into that tensor in place (the fusion
+    pass proves no later node reads its old value) and the node's output is that tensor. Up to
+    16 rows of fp32 A run as one msq_matmul_fused launch; larger M runs the same steps unfused
+    (msq_add_rmsnorm / msq_swiglu, the MatMulNBits path, an add)."""
+
+    op_type = "MatMulNBitsFused"
+
+    def execute(self, node: GraphNode, ctx: GraphContext) -> None:
+        ins = list(node.inputs) + [""] * (6 - len(node.inputs))
+        n, k = int(node.attributes["N"]), int(node.attributes["K"])
+        bits, bs = int(node.attributes.get("bits", 4)), int(node.attributes.get("block_size", 0))
+        swiglu = int(node.attributes.get("swiglu", 0))
+        eps = float(node.attributes.get("epsilon", 1e-5))
+        a = _cuda_f32(ctx, ins[0], self.op_type)
+        kin = 2 * k if swiglu else k
+        if a.shape[-1] != kin:
+            raise ModelSharpException(f"MatMulNBitsFused: A rows of {a.shape[-1]}, expected {kin}.")
+        m = a.numel() // kin
+        gamma = _cuda_f32(ctx, ins[4], self.op_type) if ins[4] else None
+        if gamma is not None and swiglu:
+            raise ModelSharpException("MatMulNBitsFused: gamma and swiglu are exclusive.")
+        zp_raw = ctx.get_tensor(ins[3]) if ins[3] else None
+        w = self._weights(ctx.get_tensor(ins[1]), ctx.get_tensor(ins[2]), zp_raw, n, k, bits, bs, a.device)
+        self.calls += 1
+        if ins[5]:
+            out = ctx.get_tensor(ins[5])
+            if not out.is_cuda or out.dtype != torch.float32 or not out.is_contiguous() or out.numel() != m * n:
+                raise ModelSharpException("MatMulNBitsFused: the residual must be a contiguous float32 CUDA "
+                                          f"tensor of {m} x {n}.")
+        else:
+            out = torch.empty(*a.shape[:-1], n, dtype=torch.float32, device=a.device)
+        a2, o2 = a.reshape(m, kin), out.view(m, n)
+        aligned = k % 4 == 0 and a2.data_ptr() % 16 == 0 and (gamma is None or gamma.data_ptr() % 16 == 0)
+        if m <= 16 and aligned and bits == 4 and bs in (32, 64, 128):  # the decode GEMV's forms
+            w.matmul_fused(a2, o2, rms_gamma=gamma, rms_eps=eps, swiglu=bool(swiglu), accumulate=bool(ins[5]),
+                           stream=_stream(a))
+        else:
+            x = a2
+            if gamma is not None:
+                x = torch.empty_like(a2)
+                _ok(N.lib().msq_add_rmsnorm(None, _stream(a), a2.data_ptr(), None, gamma.data_ptr(), x.data_ptr(),
+                                            m, k, eps), self.op_type)
+            elif swiglu:
+                x = torch.empty(m, k, dtype=torch.float32, device=a.device)
+                for r in range(m):
+                    _ok(N.lib().msq_swiglu(None, _stream(a), a2[r].data_ptr(), x[r].data_ptr(), k), self.op_type)
+            y = w.matmul(x, path=self.path)
+            if ins[5]:
+                o2.add_(y)
+            else:
+                o2.copy_(y)
+        ctx.set(node.outputs[0], out)
+
+
 def create_decoder_registry(device=None) -> KernelRegistry:
-    """The CUDA registry with MatMulNBits and the decoder graph's other op types."""
-    reg = KernelRegistry().register(CudaMatMulNBitsKernel(device))
+    """The CUDA registry with MatMulNBits (plain and fused) and the decoder graph's other op
+    types."""
+    reg = KernelRegistry().register(CudaMatMulNBitsKernel(device)).register(MatMulNBitsFusedKernel(device))
     for k in (GatherKernel(), SimplifiedLayerNormalizationKernel(), SkipSimplifiedLayerNormalizationKernel(),
               GroupQueryAttentionKernel(), SigmoidKernel(), MulKernel(), ArgMaxKernel()):
         reg.register(k)
     return reg
 
 
-__all__ = ["create_decoder_registry", "GatherKernel", "SimplifiedLayerNormalizationKernel",
+__all__ = ["create_decoder_registry", "MatMulNBitsFusedKernel", "GatherKernel", "SimplifiedLayerNormalizationKernel",
            "SkipSimplifiedLayerNormalizationKernel", "GroupQueryAttentionKernel", "SigmoidKernel", "MulKernel",
            "ArgMaxKernel"]

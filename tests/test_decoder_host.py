@@ -124,3 +124,126 @@ def test_engine_rejects_unknown_ops_and_unsupported_forms():
                           dict(base, do_rotary=0))
     with pytest.raises(ModelSharpException, match="do_rotary"):
         gqa.execute(no_rotary, GraphContext({}))
+
+
+# ---- the engine-level fusion pass, checked with a CPU executor of the graph's op types
+def _np(t):
+    return t.numpy() if hasattr(t, "numpy") else np.asarray(t)
+
+
+def _ref_run(graph, feeds, cfg, state):
+    """Runs a decoder graph on the CPU with the checker's restatements (state: the KV caches)."""
+    env = {k: v for k, v in graph.initializers.items()}
+    env.update(state)
+    env.update(feeds)
+    cos, sin = od.rope_tables(cfg)
+
+    def mnb(node, a):
+        n, k, bs = (int(node.attributes[x]) for x in ("N", "K", "block_size"))
+        a2 = np.ascontiguousarray(np.asarray(a, np.float32).reshape(-1, k))
+        case = dict(a=a2, b=_np(env[node.inputs[1]]), scales=_np(env[node.inputs[2]]).reshape(-1),
+                    zp=_np(env[node.inputs[3]]), zp_kind="packed", M=a2.shape[0], N=n, K=k, bits=4, block_size=bs)
+        return oracle.managed(case).reshape(*np.asarray(a).shape[:-1], n)
+
+    for node in graph.nodes:
+        op, ins = node.op_type, node.inputs
+        if op == "Gather":
+            out = [_np(env[ins[0]])[np.asarray(env[ins[1]]).reshape(-1)].reshape(1, 1, -1)]
+        elif op == "SimplifiedLayerNormalization":
+            out = [od.rms_norm(env[ins[0]], _np(env[ins[1]]), node.attributes["epsilon"])]
+        elif op == "SkipSimplifiedLayerNormalization":
+            s = (env[ins[0]] + env[ins[1]]).astype(np.float32)
+            out = [od.rms_norm(s, _np(env[ins[2]]), node.attributes["epsilon"]), None, None, s]
+        elif op == "MatMulNBits":
+            out = [mnb(node, env[ins[0]])]
+        elif op == "MatMulNBitsFused":
+            x = np.asarray(env[ins[0]], np.float32)
+            if ins[4]:
+                x = od.rms_norm(x, _np(env[ins[4]]), node.attributes["epsilon"])
+            if int(node.attributes.get("swiglu", 0)):
+                k = int(node.attributes["K"])
+                gt, up = x[..., :k], x[..., k:]
+                x = (gt / (np.float32(1.0) + np.exp(-gt)) * up).astype(np.float32)
+            y = mnb(node, x)
+            out = [(env[ins[5]] + y).astype(np.float32) if len(ins) > 5 and ins[5] else y]
+        elif op == "GroupQueryAttention":
+            h, kvh, d = node.attributes["num_heads"], node.attributes["kv_num_heads"], cfg.head_dim
+            qkv = np.asarray(env[ins[0]]).reshape(1, -1)
+            pos = int(np.asarray(env[ins[5]]).reshape(-1)[0])
+            p = np.asarray([pos])
+            q = od.rope(qkv[:, :h * d], h, d, p, cos, sin)
+            k = od.rope(qkv[:, h * d:(h + kvh) * d], kvh, d, p, cos, sin)
+            kc, vc = env[ins[3]], env[ins[4]]
+            kc[0, :, pos] = k.reshape(kvh, d)
+            vc[0, :, pos] = qkv[0, (h + kvh) * d:].reshape(kvh, d)
+            out = [od.attention(q, kc[0], vc[0], pos, cfg).reshape(1, 1, -1), kc, vc]
+        elif op == "Sigmoid":
+            out = [(1.0 / (1.0 + np.exp(-env[ins[0]]))).astype(np.float32)]
+        elif op == "Mul":
+            out = [(env[ins[0]] * env[ins[1]]).astype(np.float32)]
+        elif op == "ArgMax":
+            out = [np.argmax(env[ins[0]], axis=-1)]
+        else:
+            raise AssertionError(op)
+        for name, v in zip(node.outputs, out):
+            if name:
+                env[name] = v
+    return {o: env[o] for o in graph.outputs}
+
+
+def _ref_generate(graph, cfg, prompt, n_new):
+    state = {k: np.zeros(tuple(v.shape), np.float32) for k, v in graph.initializers.items() if "past_" in k}
+    out, toks, logits = None, [], []
+    for i, t in enumerate(prompt):
+        out = _ref_run(graph, {"input_ids": np.asarray([[t]]), "seqlens_k": np.asarray([i])}, cfg, state)
+    for j in range(n_new):
+        toks.append(int(out["next_token"].reshape(-1)[0]))
+        logits.append(out["logits"].reshape(-1))
+        if j + 1 < n_new:
+            out = _ref_run(graph, {"input_ids": np.asarray([[toks[-1]]]), "seqlens_k": np.asarray([len(prompt) + j])},
+                           cfg, state)
+    return toks, logits
+
+
+def test_fusion_pass_structure_and_semantics():
+    from modelsharp_b200.decoder import build_decoder_graph
+    from modelsharp_b200.graph_fusion import fuse_decode_graph
+    from modelsharp_b200.llm_ops import create_decoder_registry
+    w = make_weights(TINY, 5, "cpu")
+    g = build_decoder_graph(TINY, w, "cpu")
+    f = fuse_decode_graph(g)
+    ops = [n.op_type for n in f.nodes]
+    assert ops.count("MatMulNBitsFused") == 4 * TINY.layers + 1
+    for gone in ("MatMulNBits", "SimplifiedLayerNormalization", "SkipSimplifiedLayerNormalization", "Sigmoid", "Mul"):
+        assert gone not in ops, gone
+    assert len(f.nodes) == 5 * TINY.layers + 3  # Gather, 5 per layer, LM head, ArgMax
+    assert [n.op_type for n in g.nodes].count("Sigmoid") == TINY.layers  # the source graph is untouched
+    known = set(f.inputs) | set(f.initializers)
+    reg = create_decoder_registry("cpu")
+    for node in f.nodes:
+        assert all(x == "" or x in known for x in node.inputs), node.name
+        known |= {o for o in node.outputs if o}
+        assert reg.try_get(node.op_type)[0]
+    prompt = [3, 17, 42, 8, 1]
+    t_plain, l_plain = _ref_generate(g, TINY, prompt, 3)
+    t_fused, l_fused = _ref_generate(f, TINY, prompt, 3)
+    assert t_plain == t_fused
+    for a, b in zip(l_plain, l_fused):
+        assert oracle.rel_l2(b, a) <= 1e-5
+    # the plain graph's CPU run is the checker's decoder
+    ref_tokens, _ = od.generate(weights_to_host(w), TINY, np.asarray(prompt), 3)
+    assert t_plain == list(ref_tokens)
+
+
+def test_fusion_keeps_a_residual_that_is_read_later():
+    """No in-place add into a value that a later node still reads."""
+    from modelsharp_b200 import GraphNode, ModelGraph
+    from modelsharp_b200.graph_fusion import fuse_decode_graph
+    mnb = {"N": 8, "K": 8, "bits": 4, "block_size": 32}
+    nodes = [GraphNode("MatMulNBits", "p", ["a", "B", "S", "Z"], ["y"], mnb),
+             GraphNode("SkipSimplifiedLayerNormalization", "n", ["y", "r", "g"], ["h", "", "", "s"], {}),
+             GraphNode("MatMulNBits", "c", ["h", "B", "S", "Z"], ["o"], mnb),
+             GraphNode("Mul", "late", ["r", "o"], ["z"])]
+    g = ModelGraph(["a", "r"], ["z"], nodes, {"B": 0, "S": 0, "Z": 0, "g": 0})
+    f = fuse_decode_graph(g)
+    assert [n.op_type for n in f.nodes] == [n.op_type for n in nodes]  # r is a graph input and read later

@@ -2,7 +2,8 @@
 
 build_decoder_graph turns the small Llama-shaped decoder into MatMulNBits, norm, attention,
 SwiGLU and ArgMax nodes; CudaEngine runs it one token at a time on the CUDA registry of
-llm_ops. Every projection takes the exact decode GEMV, so the greedy tokens must equal the
+llm_ops, as built and after graph_fusion folds norms, SwiGLU and residual adds into
+MatMulNBitsFused nodes. Every projection takes the exact decode GEMV, so the greedy tokens must equal the
 checker's and the CudaDecoder's, and the logits that chose the first token must agree with
 the checker's to 1e-5 relative L2.
 """
@@ -28,11 +29,14 @@ def setup(cuda_device):
     yield w, host, prompt
 
 
-def test_engine_tokens_and_logits_match_checker(cuda_device, setup):
+@pytest.mark.parametrize("fuse", [False, True])
+def test_engine_tokens_and_logits_match_checker(cuda_device, setup, fuse):
     w, host, prompt = setup
     n_new = 10
     ref_tokens, ref_logits = od.generate(host, SMALL, prompt.numpy(), n_new)
-    eng = EngineDecoder(SMALL, w, cuda_device)
+    eng = EngineDecoder(SMALL, w, cuda_device, fuse=fuse)
+    if fuse:
+        assert {n.op_type for n in eng.graph.nodes} == {"Gather", "MatMulNBitsFused", "GroupQueryAttention", "ArgMax"}
     tokens, first_logits = eng.generate(prompt.to(cuda_device), n_new)
     assert oracle.rel_l2(first_logits.cpu().numpy(), ref_logits[0]) <= 1e-5
     np.testing.assert_array_equal(tokens.cpu().numpy(), ref_tokens)
