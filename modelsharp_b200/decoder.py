@@ -308,11 +308,12 @@ def build_decoder_graph(cfg: DecoderConfig, weights: dict, device: torch.device 
 class EngineDecoder:
     """Greedy decoding through the engine: the graph of build_decoder_graph run by CudaEngine
     on the registry of llm_ops (MatMulNBits and the decoder's other op types on the device),
-    one token per run. The prompt goes through the same one-token runs, position by position.
+    one token per run after the prompt, which goes through one run of all its tokens.
     With fuse (the default) the graph first goes through graph_fusion.fuse_decode_graph, which
     folds the norms, SwiGLU and residual adds into MatMulNBitsFused nodes."""
 
-    def __init__(self, cfg: DecoderConfig, weights: dict, device: torch.device | str, fuse: bool = True):
+    def __init__(self, cfg: DecoderConfig, weights: dict, device: torch.device | str, fuse: bool = True,
+                 path: int = N.PATH_AUTO):
         from .engine import CudaEngine
         from .graph_fusion import fuse_decode_graph
         from .llm_ops import create_decoder_registry
@@ -321,7 +322,7 @@ class EngineDecoder:
         self.graph = build_decoder_graph(cfg, weights, self.device)
         if fuse:
             self.graph = fuse_decode_graph(self.graph)
-        self.engine = CudaEngine(self.graph, create_decoder_registry(self.device))
+        self.engine = CudaEngine(self.graph, create_decoder_registry(self.device, path))
         self._graph = None
 
     def step(self, tok: torch.Tensor, pos: int) -> dict:
@@ -355,14 +356,19 @@ class EngineDecoder:
     def release(self) -> None:
         self._graph, self._out = None, None
 
+    def prefill(self, ids: torch.Tensor) -> dict:
+        """The whole prompt (int64 [S] on the device) in one eager run from position 0; the last
+        position's `logits` [1, 1, vocab] and `next_token` [1, 1]."""
+        out = self.engine.run({"input_ids": ids.reshape(1, -1),
+                               "seqlens_k": torch.full((1,), ids.numel() - 1, dtype=torch.int64, device=self.device)})
+        return {"logits": out["logits"][:, -1:], "next_token": out["next_token"][:, -1:]}
+
     def generate(self, prompt: torch.Tensor, n_new: int) -> tuple[torch.Tensor, torch.Tensor]:
         """The n_new greedy tokens after the prompt, and the logits that chose the first."""
         ids = prompt.to(self.device, torch.int64).reshape(-1)
         if ids.numel() + n_new - 1 > self.cfg.max_seq:
             raise ModelSharpException(f"prompt of {ids.numel()} tokens + {n_new} new exceeds max_seq {self.cfg.max_seq}")
-        out = None
-        for i in range(ids.numel()):
-            out = self.step(ids[i:i + 1].reshape(1, 1), i)
+        out = self.prefill(ids)
         first_logits = out["logits"].reshape(-1).clone()
         toks = [out["next_token"].reshape(1).clone()]
         for j in range(1, n_new):

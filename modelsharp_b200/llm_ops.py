@@ -17,10 +17,12 @@ CPU kernels:
 * Sigmoid, Mul                    SigmoidKernel.cs:11, MulKernel.cs:8 (same-shape operands)
 * ArgMax                          ArgReduceKernels.cs:77 (last axis): msq_argmax
 
-GroupQueryAttention here is the decode form: one query token (batch 1), packed QKV, rotary
-in the op, and past_key / past_value preallocated to [1, kv_num_heads, max_seq, head_dim] and
-shared with present_key / present_value: the token's rotated k and v are written into row
-seqlens_k of the past buffers and the present outputs are those buffers. (The reference
+GroupQueryAttention takes batch 1, packed QKV, rotary in the op, and past_key / past_value
+preallocated to [1, kv_num_heads, max_seq, head_dim] and shared with present_key /
+present_value: the tokens' rotated k and v are written into the past buffers (rows up to
+seqlens_k) and the present outputs are those buffers. One query token runs as one
+msq_rope_gqa_decode launch; several (a prompt ending at seqlens_k) run as batched torch
+matmuls and a softmax over the cache. (The reference
 returns a fresh concatenated present each step; sharing the buffer keeps a decode step free
 of per-token copies of the cache.) Inputs outside these forms raise ModelSharpException.
 """
@@ -131,9 +133,8 @@ class GroupQueryAttentionKernel:
         if not (ins[3] and ins[4] and ins[5] and ins[7] and ins[8]):
             raise ModelSharpException(f"{op}: past_key, past_value, seqlens_k, cos_cache and sin_cache are required.")
         qkv = _cuda_f32(ctx, ins[0], op)
-        if qkv.dim() != 3 or qkv.shape[0] != 1 or qkv.shape[1] != 1:
-            raise ModelSharpException(f"{op}: the decode form takes one query token, [1, 1, hidden]; "
-                                      f"got {list(qkv.shape)}.")
+        if qkv.dim() != 3 or qkv.shape[0] != 1:
+            raise ModelSharpException(f"{op}: batch 1 query [1, S, hidden] only; got {list(qkv.shape)}.")
         unit = heads + 2 * kvh
         if qkv.shape[2] % unit:
             raise ModelSharpException(f"GroupQueryAttention packed-QKV hidden {qkv.shape[2]} not divisible by "
@@ -159,15 +160,51 @@ class GroupQueryAttentionKernel:
             raise ModelSharpException(f"{op}: seqlens_k must be one index on the CUDA device.")
         if pos.dtype != torch.int64:
             pos = pos.to(torch.int64)
-        out = torch.empty(1, 1, heads * d, dtype=torch.float32, device=qkv.device)
-        _ok(N.lib().msq_rope_gqa_decode(None, _stream(qkv), qkv.data_ptr(), heads, kvh, d, cos.data_ptr(),
-                                        sin.data_ptr(), pos.data_ptr(), pk.data_ptr(), pv.data_ptr(), out.data_ptr(),
-                                        max_seq), op)
+        if qkv.shape[1] > 1:
+            out = self._prompt(qkv, pos, pk, pv, cos, sin, heads, kvh, d, max_seq)
+        else:
+            out = torch.empty(1, 1, heads * d, dtype=torch.float32, device=qkv.device)
+            _ok(N.lib().msq_rope_gqa_decode(None, _stream(qkv), qkv.data_ptr(), heads, kvh, d, cos.data_ptr(),
+                                            sin.data_ptr(), pos.data_ptr(), pk.data_ptr(), pv.data_ptr(),
+                                            out.data_ptr(), max_seq), op)
         ctx.set(node.outputs[0], out)
         if len(node.outputs) > 1 and node.outputs[1]:
             ctx.set(node.outputs[1], pk)
         if len(node.outputs) > 2 and node.outputs[2]:
             ctx.set(node.outputs[2], pv)
+
+
+    @staticmethod
+    def _prompt(qkv, pos, pk, pv, cos, sin, heads, kvh, d, max_seq):
+        """S > 1 query tokens ending at position seqlens_k (a prompt): half-split rotary of q and k
+        at positions p0..p0+S-1, k and v appended to the cache, causal attention of each query
+        over cache rows 0..its position, 1/sqrt(d) scale. Batched torch matmuls and softmax over
+        the cache on the device; reads seqlens_k on the host."""
+        S = qkv.shape[1]
+        last = int(pos.reshape(-1)[0])
+        p0 = last - S + 1
+        if p0 < 0 or last >= max_seq:
+            raise ModelSharpException(f"GroupQueryAttention: {S} query tokens ending at position {last} do not fit "
+                                      f"a cache of {max_seq}.")
+        half = d // 2
+        x = qkv.reshape(S, heads + 2 * kvh, d)
+        c, sn = cos[p0:last + 1][:, None, :], sin[p0:last + 1][:, None, :]
+
+        def rot(t):
+            a, b = t[..., :half], t[..., half:]
+            return torch.cat((a * c - b * sn, b * c + a * sn), dim=-1)
+
+        q, k, v = rot(x[:, :heads]), rot(x[:, heads:heads + kvh]), x[:, heads + kvh:]
+        pk[0, :, p0:last + 1].copy_(k.transpose(0, 1))
+        pv[0, :, p0:last + 1].copy_(v.transpose(0, 1))
+        T = last + 1
+        qv = q.reshape(S, kvh, heads // kvh, d).permute(1, 2, 0, 3)                     # [kvh, G, S, d]
+        sc = torch.matmul(qv, pk[0, :, :T].unsqueeze(1).transpose(-1, -2)) / math.sqrt(d)  # [kvh, G, S, T]
+        keys = torch.arange(T, device=qkv.device)
+        mask = keys[None, :] <= (p0 + torch.arange(S, device=qkv.device))[:, None]
+        p = torch.softmax(sc.masked_fill(~mask, float("-inf")), dim=-1)
+        o = torch.matmul(p, pv[0, :, :T].unsqueeze(1))                                   # [kvh, G, S, d]
+        return o.permute(2, 0, 1, 3).reshape(1, S, heads * d).contiguous()
 
 
 class SigmoidKernel:
@@ -190,7 +227,8 @@ class MulKernel:
 
 
 class ArgMaxKernel:
-    """Index of the first maximum along the last axis (int64), keepdims as the attribute says."""
+    """Index of the first maximum along the last axis (int64), keepdims as the attribute says:
+    msq_argmax for one row, torch.argmax for several."""
 
     op_type = "ArgMax"
 
@@ -202,10 +240,11 @@ class ArgMaxKernel:
             raise ModelSharpException("ArgMax: select_last_index is not supported.")
         n = x.shape[-1]
         rows = x.numel() // n
-        idx = torch.empty(rows, dtype=torch.int64, device=x.device)
-        lib, st = N.lib(), _stream(x)
-        for r in range(rows):
-            _ok(lib.msq_argmax(None, st, x.data_ptr() + 4 * r * n, n, idx.data_ptr() + 8 * r, None), "ArgMax")
+        if rows == 1:
+            idx = torch.empty(1, dtype=torch.int64, device=x.device)
+            _ok(N.lib().msq_argmax(None, _stream(x), x.data_ptr(), n, idx.data_ptr(), None), "ArgMax")
+        else:  # a prompt's rows at once (torch also returns the first maximum)
+            idx = torch.argmax(x.reshape(rows, n), dim=1)
         shape = list(x.shape[:-1]) + ([1] if int(_attr(node, "keepdims", 1)) else [])
         ctx.set(node.outputs[0], idx.reshape(shape))
 
@@ -218,8 +257,8 @@ class MatMulNBitsFusedKernel(CudaMatMulNBitsKernel):
     applied on the way in); with swiglu=1, A rows are [gate | up] of 2K and the product uses
     silu(gate) * up; with residual, the product is added into that tensor in place (the fusion
     pass proves no later node reads its old value) and the node's output is that tensor. Up to
-    16 rows of fp32 A run as one msq_matmul_fused launch; larger M runs the same steps unfused
-    (msq_add_rmsnorm / msq_swiglu, the MatMulNBits path, an add)."""
+    16 rows of fp32 A run as one msq_matmul_fused launch; larger M (a prompt) runs the same steps
+    unfused (msq_add_rmsnorm or a torch SwiGLU, the MatMulNBits path of the registry, an add)."""
 
     op_type = "MatMulNBitsFused"
 
@@ -259,9 +298,8 @@ class MatMulNBitsFusedKernel(CudaMatMulNBitsKernel):
                 _ok(N.lib().msq_add_rmsnorm(None, _stream(a), a2.data_ptr(), None, gamma.data_ptr(), x.data_ptr(),
                                             m, k, eps), self.op_type)
             elif swiglu:
-                x = torch.empty(m, k, dtype=torch.float32, device=a.device)
-                for r in range(m):
-                    _ok(N.lib().msq_swiglu(None, _stream(a), a2[r].data_ptr(), x[r].data_ptr(), k), self.op_type)
+                gt, up = a2[:, :k], a2[:, k:]
+                x = (gt / (1.0 + torch.exp(-gt)) * up).contiguous()
             y = w.matmul(x, path=self.path)
             if ins[5]:
                 o2.add_(y)
@@ -270,10 +308,10 @@ class MatMulNBitsFusedKernel(CudaMatMulNBitsKernel):
         ctx.set(node.outputs[0], out)
 
 
-def create_decoder_registry(device=None) -> KernelRegistry:
+def create_decoder_registry(device=None, path: int = N.PATH_AUTO) -> KernelRegistry:
     """The CUDA registry with MatMulNBits (plain and fused) and the decoder graph's other op
-    types."""
-    reg = KernelRegistry().register(CudaMatMulNBitsKernel(device)).register(MatMulNBitsFusedKernel(device))
+    types. `path` pins the MatMulNBits route (PATH_GEMV: the exact decode GEMV for every M)."""
+    reg = KernelRegistry().register(CudaMatMulNBitsKernel(device, path)).register(MatMulNBitsFusedKernel(device, path))
     for k in (GatherKernel(), SimplifiedLayerNormalizationKernel(), SkipSimplifiedLayerNormalizationKernel(),
               GroupQueryAttentionKernel(), SigmoidKernel(), MulKernel(), ArgMaxKernel()):
         reg.register(k)

@@ -5,7 +5,8 @@ SwiGLU and ArgMax nodes; CudaEngine runs it one token at a time on the CUDA regi
 llm_ops, as built and after graph_fusion folds norms, SwiGLU and residual adds into
 MatMulNBitsFused nodes. Every projection takes the exact decode GEMV, so the greedy tokens must equal the
 checker's and the CudaDecoder's, and the logits that chose the first token must agree with
-the checker's to 1e-5 relative L2.
+the checker's to 1e-5 relative L2 (the prompt goes through one run of all its tokens); on the
+default route the prompt's projections take the tensor-core GEMM and its logits agree to 5e-3.
 """
 import numpy as np
 import pytest
@@ -34,7 +35,7 @@ def test_engine_tokens_and_logits_match_checker(cuda_device, setup, fuse):
     w, host, prompt = setup
     n_new = 10
     ref_tokens, ref_logits = od.generate(host, SMALL, prompt.numpy(), n_new)
-    eng = EngineDecoder(SMALL, w, cuda_device, fuse=fuse)
+    eng = EngineDecoder(SMALL, w, cuda_device, fuse=fuse, path=N.PATH_GEMV)
     if fuse:
         assert {n.op_type for n in eng.graph.nodes} == {"Gather", "MatMulNBitsFused", "GroupQueryAttention", "ArgMax"}
     tokens, first_logits = eng.generate(prompt.to(cuda_device), n_new)
@@ -48,7 +49,7 @@ def test_engine_matches_direct_decoder(cuda_device, setup):
     dec = CudaDecoder(SMALL, w, cuda_device)
     direct = dec.generate(prompt.to(cuda_device), 8, N.PATH_GEMV).cpu().numpy()
     dec.free()
-    eng = EngineDecoder(SMALL, w, cuda_device)
+    eng = EngineDecoder(SMALL, w, cuda_device, path=N.PATH_GEMV)
     tokens, _ = eng.generate(prompt.to(cuda_device), 8)
     np.testing.assert_array_equal(tokens.cpu().numpy(), direct)
 
@@ -67,10 +68,20 @@ def test_engine_step_writes_the_cache_row(cuda_device, setup):
 
 def test_engine_graph_replay_matches_eager(cuda_device, setup):
     w, _, prompt = setup
-    eng = EngineDecoder(SMALL, w, cuda_device)
+    eng = EngineDecoder(SMALL, w, cuda_device, path=N.PATH_GEMV)
     eager, eager_logits = eng.generate(prompt.to(cuda_device), 8)
     eng.capture()
     replayed, replay_logits = eng.generate(prompt.to(cuda_device), 8)
     eng.release()
     np.testing.assert_array_equal(replayed.cpu().numpy(), eager.cpu().numpy())
     assert torch.equal(replay_logits, eager_logits)
+
+
+def test_engine_prompt_on_tensor_cores(cuda_device, setup):
+    """The default route: the 20-token prompt's projections on the tensor-core GEMM (weights
+    entering as fp16), attention over the prompt in one run; logits within 5e-3."""
+    w, host, prompt = setup
+    _, ref_logits = od.generate(host, SMALL, prompt.numpy(), 1)
+    eng = EngineDecoder(SMALL, w, cuda_device)
+    out = eng.prefill(prompt.to(cuda_device))
+    assert oracle.rel_l2(out["logits"].reshape(-1).cpu().numpy(), ref_logits[0]) <= 5e-3
