@@ -247,3 +247,28 @@ def test_fusion_keeps_a_residual_that_is_read_later():
     g = ModelGraph(["a", "r"], ["z"], nodes, {"B": 0, "S": 0, "Z": 0, "g": 0})
     f = fuse_decode_graph(g)
     assert [n.op_type for n in f.nodes] == [n.op_type for n in nodes]  # r is a graph input and read later
+
+
+def test_fusion_leaves_unmatched_patterns_alone():
+    """Gate and up of different widths, a norm whose output is read by a non-MatMulNBits node and
+    a SwiGLU without zero points stay as they are."""
+    from modelsharp_b200 import GraphNode, ModelGraph
+    from modelsharp_b200.graph_fusion import fuse_decode_graph
+
+    def mnb(name, a, n, k, zp=True):
+        return GraphNode("MatMulNBits", name, [a, name + ".B", name + ".S"] + ([name + ".Z"] if zp else []), [name],
+                         {"N": n, "K": k, "bits": 4, "block_size": 32})
+
+    def swiglu(gate_n, up_n, zp=True):
+        return [mnb("gate", "h", gate_n, 64, zp), mnb("up", "h", up_n, 64, zp),
+                GraphNode("Sigmoid", "sg", ["gate"], ["sg"]), GraphNode("Mul", "si", ["gate", "sg"], ["si"]),
+                GraphNode("Mul", "act", ["si", "up"], ["act"]), mnb("down", "act", 64, gate_n, zp)]
+
+    inits = {f"{n}.{t}": 0 for n in ("gate", "up", "down") for t in ("B", "S", "Z")}
+    for nodes in (swiglu(128, 96), swiglu(128, 128, zp=False)):
+        g = ModelGraph(["h"], ["down"], nodes, dict(inits))
+        assert [n.op_type for n in fuse_decode_graph(g).nodes] == [n.op_type for n in nodes]
+    norm_read_elsewhere = [GraphNode("SimplifiedLayerNormalization", "n", ["x", "g"], ["h"], {"epsilon": 1e-5}),
+                           mnb("p", "h", 64, 64), GraphNode("Mul", "m", ["h", "p"], ["z"])]
+    g = ModelGraph(["x"], ["z"], norm_read_elsewhere, {"g": 0, "p.B": 0, "p.S": 0, "p.Z": 0})
+    assert [n.op_type for n in fuse_decode_graph(g).nodes] == [n.op_type for n in norm_read_elsewhere]
