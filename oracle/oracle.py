@@ -33,6 +33,16 @@ _oracle = None
 _ref = None
 
 
+def reference_root() -> str | None:
+    """The reference checkout whose native sources the _ref build compiles: $MODELSHARP_REFERENCE,
+    else a `reference` tree beside this repository; None when neither holds native/src/qgemm.cpp."""
+    cands = [os.environ.get("MODELSHARP_REFERENCE"), str(HERE.parent.parent / "reference")]
+    for c in cands:
+        if c and Path(c, "native", "src", "qgemm.cpp").exists():
+            return c
+    return None
+
+
 def build(ref_root: str | None = None) -> None:
     """Compiles the C restatement (and the reference kernel when its sources exist)."""
     env = dict(os.environ)

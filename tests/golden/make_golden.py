@@ -85,9 +85,10 @@ def digest(*arrays) -> str:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=None,
+                    help="reference checkout (default: $MODELSHARP_REFERENCE, else ../reference beside the repo)")
     args = ap.parse_args()
-    oracle.build(args.ref)
+    oracle.build(args.ref or oracle.reference_root())
     if not oracle.reference_available():
         raise SystemExit("reference kernel not built; is the reference tree present?")
 
