@@ -137,14 +137,32 @@ int msq_matmul_host(void* cu_ctx, void* stream, msq_weights_t w,
  * float32 / bfloat16 (or unaligned float16) A is staged as fp16 in a fixed device array of
  * MSQ_NOALLOC_SCRATCH_BYTES that the library holds on every GPU that loads it, until exit,
  * instead of in memory taken from a pool. Calls no cudaMalloc / cudaFree or other allocator.
- * Limit: M x round_up(K, 8) x 2 <= MSQ_NOALLOC_SCRATCH_BYTES (e.g. M <= 2048 at K = 4096),
+ * Limit: round_up(M x round_up(K, 8) x 2, 256) + 4 M <= MSQ_NOALLOC_SCRATCH_BYTES (fp16 rows
+ * plus one fp32 row scale per row; e.g. M <= 2047 at K = 4096),
  * else MSQ_E_INVALID; 16-byte-aligned float16 A with K % 8 == 0 needs no staging and has no
- * limit. The first call in a CUDA context looks up the array's address (set-up); make it
- * before any stream capture. All calls share the array: calls that overlap on the GPU race. */
+ * limit. The first staging call in a CUDA context looks up the array's address in that
+ * context (set-up; keyed by cuCtxGetId, so a context created after a reset or destroy gets its
+ * own lookup); make it before any stream capture. All calls share the array: calls that
+ * overlap on the GPU race.                                                              */
 #define MSQ_NOALLOC_SCRATCH_BYTES (16u << 20)
 int msq_matmul_noalloc(void* cu_ctx, void* stream, msq_weights_t w,
                        const void* d_a, int a_dtype, int64_t M,
                        float* d_y, int64_t ldy);
+
+/* Diagnostic counters of this process (the role of NativeCuda.cs:147-150's call counter),
+ * -1 for an unknown `which`:
+ *   MSQ_DIAG_POOL_ALLOCS      stream-ordered allocations the library has taken from its
+ *                             private scratch pool (fp32/bf16 GEMM staging, k-split partials,
+ *                             host-buffer calls);
+ *   MSQ_DIAG_NOALLOC_LOOKUPS  set-up lookups of the no-allocation array's device address
+ *                             (one per CUDA context that has called msq_matmul_noalloc with
+ *                             staging);
+ *   MSQ_DIAG_POOL_RESERVED    bytes the current device's scratch pool holds (0 before its first
+ *                             allocation).                                                    */
+#define MSQ_DIAG_POOL_ALLOCS 1
+#define MSQ_DIAG_NOALLOC_LOOKUPS 2
+#define MSQ_DIAG_POOL_RESERVED 3
+int64_t msq_diag_counter(int which);
 
 /* Synchronizes `stream` and reports whether any kernel of this library on the current
  * device gave up a bounded wait (a pipeline stage that never arrived) since the last call:

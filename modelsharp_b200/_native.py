@@ -26,6 +26,12 @@ DT_ABSENT, DT_F32, DT_F64, DT_F16, DT_I32, DT_I64, DT_I8, DT_U8, DT_BOOL, DT_BF1
 
 PATH_AUTO, PATH_GENERIC, PATH_GEMV, PATH_GEMM = 0, 1, 2, 3
 NOALLOC_SCRATCH_BYTES = 16 << 20  # MSQ_NOALLOC_SCRATCH_BYTES
+
+
+def noalloc_staging_bytes(M: int, K: int) -> int:
+    """Bytes msq_matmul_noalloc stages for M rows of float32/bfloat16 A: fp16 rows of K rounded
+    up to 8, padded to 256 bytes, then one fp32 row scale per row."""
+    return (M * ((K + 7) // 8 * 8) * 2 + 255) // 256 * 256 + 4 * M
 MAX_RANKS = 8  # MSQ_MAX_RANKS
 IPC_HANDLE_BYTES = 64  # MSQ_IPC_HANDLE_BYTES
 
@@ -48,6 +54,7 @@ class FusionT(C.Structure):
 
 
 PACK_DEFAULT, PACK_GENERIC_ONLY = 0, 1
+DIAG_POOL_ALLOCS, DIAG_NOALLOC_LOOKUPS, DIAG_POOL_RESERVED = 1, 2, 3  # MSQ_DIAG_*
 
 LIB_NAME = "libms_cuda_nbits.so"
 HEADER = Path(__file__).resolve().parent.parent / "include" / "ms_cuda_nbits.h"
@@ -63,6 +70,7 @@ SIGNATURES: dict[str, tuple] = {
     "msq_last_error": (C.c_char_p, []),
     "msq_launch_count": (_i64, []),
     "msq_last_path": (C.c_char_p, []),
+    "msq_diag_counter": (_i64, [_i32]),
     "msq_check_node": (_i32, [_i32, _i32, _i32, _i32, _i64, _i64, _i32, _i64, _vp, _i64, _vp, _i32, _vp]),
     "msq_pack": (_i32, [_vp, _vp, _vp, _i64, _vp, _i32, _i64, _vp, _i32, _i64, _i32, _i32, _i32, _i32,
                         _i32, _i32, _i32, _vp]),
@@ -133,6 +141,11 @@ def check(rc: int, what: str = "") -> None:
 
 def launch_count() -> int:
     return int(lib().msq_launch_count())
+
+
+def diag_counter(which: int) -> int:
+    """msq_diag_counter: DIAG_POOL_ALLOCS, DIAG_NOALLOC_LOOKUPS or DIAG_POOL_RESERVED."""
+    return int(lib().msq_diag_counter(which))
 
 
 def last_path() -> str:

@@ -34,16 +34,34 @@ def needs_rebuild() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
+    """Compiles every translation unit in parallel into _build/ and links the shared library."""
     if not force and not needs_rebuild():
         return LIB
+    from concurrent.futures import ThreadPoolExecutor
+
+    obj_dir = PKG / "_build"
+    obj_dir.mkdir(exist_ok=True)
+    flags = [*ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC"]
+
+    def compile_one(src: str) -> Path:
+        obj = obj_dir / (Path(src).stem + ".o")
+        cmd = [nvcc(), *flags, "-c", "-o", str(obj), str(CSRC / src)]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        r = subprocess.run(cmd, cwd=CSRC, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"nvcc failed on {src} ({r.returncode}):\n{r.stdout}\n{r.stderr}")
+        return obj
+
+    with ThreadPoolExecutor(max_workers=min(len(SOURCES), os.cpu_count() or 4)) as ex:
+        objs = list(ex.map(compile_one, SOURCES))
     tmp = LIB.with_suffix(".so.tmp")
-    cmd = [nvcc(), *ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
-           "-o", str(tmp), *[str(CSRC / s) for s in SOURCES]]
+    cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *map(str, objs)]
     if verbose:
         print(" ".join(cmd), flush=True)
     r = subprocess.run(cmd, cwd=CSRC, capture_output=True, text=True)
     if r.returncode != 0:
-        raise RuntimeError(f"nvcc failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
+        raise RuntimeError(f"nvcc link failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
     os.replace(tmp, LIB)
     return LIB
 

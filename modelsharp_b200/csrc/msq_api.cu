@@ -296,9 +296,46 @@ void note_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 namespace {
 std::mutex g_pool_mu;
 cudaMemPool_t g_pools[64] = {};
+std::atomic<int64_t> g_pool_allocs{0};
+std::atomic<int64_t> g_noalloc_lookups{0};
+
+using PFN_getcur = CUresult (*)(CUcontext*);
+using PFN_getid = CUresult (*)(CUcontext, unsigned long long*);
+PFN_getcur g_getcur = nullptr;
+PFN_getid g_getid = nullptr;
+std::once_flag g_ctxid_once;
 }  // namespace
 
+void note_noalloc_lookup() { g_noalloc_lookups.fetch_add(1, std::memory_order_relaxed); }
+
+int current_context_id(unsigned long long* id) {
+  std::call_once(g_ctxid_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_getcur = reinterpret_cast<PFN_getcur>(fn);
+    fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_getid = reinterpret_cast<PFN_getid>(fn);
+  });
+  if (!g_getcur || !g_getid) return fail(MSQ_E_CUDA, "cannot resolve cuCtxGetCurrent/cuCtxGetId from the driver");
+  CUcontext ctx = nullptr;
+  if (g_getcur(&ctx) != CUDA_SUCCESS) return fail(MSQ_E_CUDA, "cuCtxGetCurrent failed");
+  if (!ctx) {
+    // A thread that has made no CUDA call yet: bind the current device's primary context.
+    int dev = 0;
+    MSQ_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
+    MSQ_CUDA_TRY(cudaSetDevice(dev), "cudaSetDevice");
+    if (g_getcur(&ctx) != CUDA_SUCCESS || !ctx) return fail(MSQ_E_CUDA, "no current CUDA context");
+  }
+  if (g_getid(ctx, id) != CUDA_SUCCESS) return fail(MSQ_E_CUDA, "cuCtxGetId failed");
+  return MSQ_OK;
+}
+
 int scratch_alloc(void** p, size_t bytes, cudaStream_t st) {
+  g_pool_allocs.fetch_add(1, std::memory_order_relaxed);
   int dev = 0;
   MSQ_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
   cudaMemPool_t pool = nullptr;
@@ -363,6 +400,27 @@ int msq_available(void) {
 }
 
 const char* msq_last_error(void) { return t_last_error.c_str(); }
+
+int64_t msq_diag_counter(int which) {
+  switch (which) {
+    case MSQ_DIAG_POOL_ALLOCS: return g_pool_allocs.load();
+    case MSQ_DIAG_NOALLOC_LOOKUPS: return g_noalloc_lookups.load();
+    case MSQ_DIAG_POOL_RESERVED: {
+      int dev = 0;
+      if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -1;
+      cudaMemPool_t pool;
+      {
+        std::lock_guard<std::mutex> lk(g_pool_mu);
+        pool = g_pools[dev];
+      }
+      if (!pool) return 0;
+      uint64_t v = 0;
+      if (cudaMemPoolGetAttribute(pool, cudaMemPoolAttrReservedMemCurrent, &v) != cudaSuccess) return -1;
+      return (int64_t)v;
+    }
+    default: return -1;
+  }
+}
 int64_t msq_launch_count(void) { return g_launches.load(); }
 const char* msq_last_path(void) { return t_last_path; }
 

@@ -70,6 +70,8 @@ struct GemmArgs {
   int vec_store;
   int kper;              // k-stages per CTA: blockIdx.z takes stages [z kper, (z + 1) kper)
   int64_t split_stride;  // with several k-splits: elements between their partial outputs
+  const float* row_scale;  // staged A: row m entered the tensor core as a * 2^e_m; Y row m is
+                           // multiplied by row_scale[m] = 2^-e_m (exact). nullptr: A as given
 };
 
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -293,6 +295,11 @@ __global__ void __launch_bounds__(Plan<TM, BN>::kThreads, 1)
         ptx::tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)tcol, v);
         ptx::tmem_ld_wait();
         if (m < p.M) {
+          if (p.row_scale) {
+            const float rs = p.row_scale[m];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) * rs);
+          }
           float* yrow = p.y + blockIdx.z * p.split_stride + (int64_t)m * p.ldy + n0 + col;
           if (p.vec_store && n0 + col + 32 <= p.n_rows) {
 #pragma unroll
@@ -317,13 +324,33 @@ __global__ void __launch_bounds__(Plan<TM, BN>::kThreads, 1)
   }
 }
 
-// fp32 / bf16 / unaligned fp16 activations -> fp16 [M][lda] (k < K only).
-__global__ void to_half_kernel(const void* __restrict__ a, int dt, int64_t M, int K, __half* __restrict__ out,
-                               int64_t lda) {
-  const int64_t total = M * (int64_t)K;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t m = i / K, k = i - m * K;
-    out[m * lda + k] = __float2half_rn(load_act(a, dt, i));
+// fp32 / bf16 / unaligned fp16 activations -> fp16 [M][lda] (k < K only), one warp per row.
+// fp16 holds magnitudes up to 65504 and keeps full precision only above 2^-14, while the
+// reference computes in fp32; so each row is scaled by a power of two 2^e chosen from its
+// largest finite magnitude (that maximum lands in [2^14, 2^15)) before the rounding, and
+// row_scale[m] = 2^-e undoes it exactly in the GEMM's epilogue. Infinities and NaNs pass
+// through unchanged, so they propagate through the tensor core as in the fp32 reference.
+__global__ void to_half_rows_kernel(const void* __restrict__ a, int dt, int64_t M, int K, __half* __restrict__ out,
+                                    int64_t lda, float* __restrict__ row_scale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t m = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); m < M; m += warps) {
+    const int64_t base = m * (int64_t)K;
+    float mx = 0.f;
+    for (int k = lane; k < K; k += 32) {
+      const float v = fabsf(load_act(a, dt, base + k));
+      if (v <= 3.402823466e38f) mx = fmaxf(mx, v);  // finite only (false for NaN and inf)
+    }
+    mx = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(mx)));
+    int e = 0;
+    if (mx > 0.f) {
+      int ex;
+      frexpf(mx, &ex);               // mx = f 2^ex, f in [0.5, 1)
+      e = max(-120, min(120, 15 - ex));  // mx 2^e in [2^14, 2^15)
+    }
+    const float up = ldexpf(1.f, e);
+    for (int k = lane; k < K; k += 32) out[m * lda + k] = __float2half_rn(load_act(a, dt, base + k) * up);
+    if (lane == 0) row_scale[m] = ldexpf(1.f, -e);
   }
 }
 
@@ -387,14 +414,13 @@ struct GemmState {
 template <int TM, int BN, int ZPK>
 int launch(cudaStream_t st, const CUtensorMap& tmA, const WeightMaps& wm, const GemmArgs& a, dim3 grid) {
   auto kern = gemm_tc_kernel<TM, BN, ZPK>;
-  static bool configured[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !configured[dev]) {
+  static ContextOnce configured;
+  int rc = configured.run([&] {
     MSQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Plan<TM, BN>::kSmem),
                  "gemm smem attribute");
-    configured[dev] = true;
-  }
+    return MSQ_OK;
+  });
+  if (rc != MSQ_OK) return rc;
   kern<<<grid, Plan<TM, BN>::kThreads, Plan<TM, BN>::kSmem, st>>>(tmA, wm.p, wm.s, wm.z, a);
   note_launch();
   MSQ_CUDA_TRY(cudaGetLastError(), "gemm launch");
@@ -444,7 +470,7 @@ int choose_splits(int ctas, int sms, int ksteps, int64_t M, int64_t ldw) {
 // K is split across CTAs whose partial tiles go to stream-ordered scratch and are summed in a
 // fixed order into Y (deterministic).
 int launch_gemm(cudaStream_t st, const Weights& w, const WeightMaps& m128, const void* a16, int64_t lda,
-                int64_t M, float* d_y, int64_t ldy, bool allow_split) {
+                const float* row_scale, int64_t M, float* d_y, int64_t ldy, bool allow_split) {
   const int tm = M >= 4 * BM ? 4 : M > BM ? 2 : 1;
   const int rows = tm * BM;
   CUtensorMap tmA;
@@ -454,6 +480,7 @@ int launch_gemm(cudaStream_t st, const Weights& w, const WeightMaps& m128, const
   GemmArgs g{};
   g.y = d_y;
   g.ldy = ldy;
+  g.row_scale = row_scale;
   g.M = (int)M;
   g.n_rows = w.n_rows;
   g.K = w.K;
@@ -525,43 +552,71 @@ bool needs_staging(const Weights& w, const void* d_a, int a_dtype) {
   return a_dtype != MSQ_DT_F16 || (w.K % 8) != 0 || (reinterpret_cast<uintptr_t>(d_a) & 15) != 0;
 }
 
+// Staged A: fp16 rows [M][staged_lda] (16-byte rows for TMA), then M fp32 row scales at a
+// 256-byte-aligned offset.
+int64_t staged_lda(const Weights& w) { return (w.K + 7) / 8 * 8; }
+size_t staged_scale_offset(const Weights& w, int64_t M) {
+  return (sizeof(__half) * (size_t)M * (size_t)staged_lda(w) + 255) / 256 * 256;
+}
+
+int stage_rows(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M, void* staging,
+               const float** row_scale) {
+  float* rs = reinterpret_cast<float*>(static_cast<uint8_t*>(staging) + staged_scale_offset(w, M));
+  const int64_t blocks = std::min<int64_t>((M + 7) / 8, 16 * (int64_t)num_sms(w.device));
+  to_half_rows_kernel<<<(unsigned)blocks, 256, 0, st>>>(d_a, a_dtype, M, w.K, static_cast<__half*>(staging),
+                                                        staged_lda(w), rs);
+  note_launch();
+  MSQ_CUDA_TRY(cudaGetLastError(), "staging launch");
+  *row_scale = rs;
+  return MSQ_OK;
+}
+
 }  // namespace
 
 int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t M, float* d_y, int64_t ldy) {
   if (!w.fast4) return fail(MSQ_E_UNSUPPORTED, "GEMM path needs bits=4 and a power-of-two block_size >= 32");
   if (M <= 0) return MSQ_OK;
   if (M > 0x7fffffff) return fail(MSQ_E_INVALID, "GEMM: M too large");
-  static std::mutex state_mu;  // first calls on one handle from several threads
-  std::lock_guard<std::mutex> lk(state_mu);
-  GemmState* gs = static_cast<GemmState*>(w.gemm_state);
+  // The tensor maps are built once per handle (under the handle's own lock, so first calls on
+  // different handles do not wait for each other) and only read afterwards.
+  GemmState* gs = static_cast<GemmState*>(w.gemm_state.load(std::memory_order_acquire));
   if (!gs) {
-    gs = new GemmState();
-    int rc = make_weight_maps(w, &gs->m128);
-    if (rc != MSQ_OK) {
-      delete gs;
-      return rc;
+    std::lock_guard<std::mutex> lk(w.state_mu);
+    gs = static_cast<GemmState*>(w.gemm_state.load(std::memory_order_relaxed));
+    if (!gs) {
+      gs = new GemmState();
+      int rc = make_weight_maps(w, &gs->m128);
+      if (rc != MSQ_OK) {
+        delete gs;
+        return rc;
+      }
+      w.gemm_state.store(gs, std::memory_order_release);
     }
-    w.gemm_state = gs;
   }
   const void* a16 = d_a;
   int64_t lda = w.K;
   void* scratch = nullptr;
-  if (needs_staging(w, d_a, a_dtype)) {
-    lda = (w.K + 7) / 8 * 8;
-    const int arc = scratch_alloc(&scratch, sizeof(__half) * (size_t)M * lda, st);
+  const float* row_scale = nullptr;
+  const size_t need = gemm_staging_bytes(w, d_a, a_dtype, M);
+  if (need) {
+    const int arc = scratch_alloc(&scratch, need, st);
     if (arc != MSQ_OK) return arc;
-    to_half_kernel<<<num_sms(w.device) * 4, 256, 0, st>>>(d_a, a_dtype, M, w.K, static_cast<__half*>(scratch), lda);
-    note_launch();
+    lda = staged_lda(w);
+    const int src = stage_rows(st, w, d_a, a_dtype, M, scratch, &row_scale);
+    if (src != MSQ_OK) {
+      scratch_free(scratch, st);
+      return src;
+    }
     a16 = scratch;
   }
-  const int rc = launch_gemm(st, w, gs->m128, a16, lda, M, d_y, ldy, true);
+  const int rc = launch_gemm(st, w, gs->m128, a16, lda, row_scale, M, d_y, ldy, true);
   scratch_free(scratch, st);
   return rc;
 }
 
 size_t gemm_staging_bytes(const Weights& w, const void* d_a, int a_dtype, int64_t M) {
   if (M <= 0 || !needs_staging(w, d_a, a_dtype)) return 0;
-  return sizeof(__half) * (size_t)M * (size_t)((w.K + 7) / 8 * 8);
+  return staged_scale_offset(w, M) + sizeof(float) * (size_t)M;
 }
 
 int run_gemm_staged(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M, float* d_y,
@@ -574,22 +629,21 @@ int run_gemm_staged(cudaStream_t st, const Weights& w, const void* d_a, int a_dt
   if (rc != MSQ_OK) return rc;
   const void* a16 = d_a;
   int64_t lda = w.K;
+  const float* row_scale = nullptr;
   const size_t need = gemm_staging_bytes(w, d_a, a_dtype, M);
   if (need) {
     if (need > staging_bytes || !staging)
       return fail(MSQ_E_INVALID, "GEMM staging needs %zu bytes; %zu available", need, staging_bytes);
-    lda = (w.K + 7) / 8 * 8;
-    to_half_kernel<<<num_sms(w.device) * 4, 256, 0, st>>>(d_a, a_dtype, M, w.K, static_cast<__half*>(staging), lda);
-    note_launch();
-    MSQ_CUDA_TRY(cudaGetLastError(), "staging launch");
+    lda = staged_lda(w);
+    rc = stage_rows(st, w, d_a, a_dtype, M, staging, &row_scale);
+    if (rc != MSQ_OK) return rc;
     a16 = staging;
   }
-  return launch_gemm(st, w, m128, a16, lda, M, d_y, ldy, false);  // no scratch for k-splits here
+  return launch_gemm(st, w, m128, a16, lda, row_scale, M, d_y, ldy, false);  // no scratch for k-splits here
 }
 
 void release_gemm_state(Weights& w) {
-  delete static_cast<GemmState*>(w.gemm_state);
-  w.gemm_state = nullptr;
+  delete static_cast<GemmState*>(w.gemm_state.exchange(nullptr));
 }
 
 int read_gemm_errors(cudaStream_t st, int* flags) {

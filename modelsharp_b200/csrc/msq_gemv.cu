@@ -235,14 +235,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q4_kernel(const GemvArgs p) 
 template <int MR, int R, int ZPK>
 int launch_one(cudaStream_t st, GemvArgs a, int grid, size_t smem) {
   auto kern = gemv_q4_kernel<MR, R, ZPK>;
-  static int configured_smem[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && configured_smem[dev] < (int)smem) {
+  static ContextOnce configured;
+  const int rc = configured.run([&] {
     MSQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget + 16384),
                  "gemv smem attribute");
-    configured_smem[dev] = kSmemBudget + 16384;
-  }
+    return MSQ_OK;
+  });
+  if (rc != MSQ_OK) return rc;
   kern<<<grid, kThreads, smem, st>>>(a);
   note_launch();
   MSQ_CUDA_TRY(cudaGetLastError(), "gemv kernel launch");

@@ -199,6 +199,44 @@ __device__ __forceinline__ int frexp_exponent(float x) {
 }
 __device__ __forceinline__ float exp2i(int s) { return __int_as_float((s + 127) << 23); }
 
+// W[row, k] = (q - zp) * s in fp32, read back from the stream records in global memory
+// (layout in msq_internal.cuh): the slow path of rows of A that hold inf or NaN.
+template <int BS>
+__device__ float stream_weight(const Args& p, int64_t row, int k) {
+  const int64_t b = row >> 4;
+  const int r = (int)(row & 15);
+  const int t = k / p.kt, kk = k - t * p.kt;
+  const uint8_t* rec = p.strm + (b * p.ntiles + t) * (int64_t)p.stage_bytes;
+  const int o = kk & 63;
+  const int word = (o >> 5) * 2 + ((o >> 4) & 1);
+  const int ln = (r & 7) * 4 + ((o & 15) >> 2);
+  const uint8_t v = rec[(kk >> 6) * 512 + ln * 16 + word * 4 + (o & 3)];
+  const int q = r < 8 ? (v & 0xF) : (v >> 4);
+  const int bl = kk / BS;
+  const float sc = reinterpret_cast<const float*>(rec + p.off_sc)[bl * 16 + r];
+  float z = 8.f;
+  if (p.zp_kind == ZP_PACKED)
+    z = (float)((reinterpret_cast<const unsigned long long*>(rec + p.off_zp)[bl] >> (4 * r)) & 0xF);
+  else if (p.zp_kind == ZP_F32)
+    z = reinterpret_cast<const float*>(rec + p.off_zp)[bl * 16 + r];
+  return ((float)q - z) * sc;
+}
+
+// Sum over the k where A row m is inf or NaN of a[m, k] * W[row, k] in fp32: inf, -inf or NaN
+// exactly as the reference's fp32 sum gets them (a NaN term, inf * 0 or inf - inf give NaN),
+// which is what the row's output then is.
+template <int BS, bool FU>
+__device__ float nonfinite_terms(const Args& p, int m, int64_t row) {
+  const int64_t base = (p.m0 + m) * (FU ? p.lda : (int64_t)p.K);
+  float t = 0.f;
+  for (int k = 0; k < p.K; ++k) {
+    float a = load_act(p.a, p.a_dtype, base + k);
+    if (FU && p.swiglu) a = silu_mul(a, load_act(p.a, p.a_dtype, base + p.K + k));
+    if (!(fabsf(a) <= 3.402823466e38f)) t += a * stream_weight<BS>(p, row, k);
+  }
+  return t;
+}
+
 // BS = quantisation block size (32 / 64 / 128); NT = n8 tiles of B (1: M <= 2, 2: M <= 4);
 // XG = the column-split form (outputs to every rank's full-Y buffer, optional wait for a
 // gathered input); FU = the decode-step fusion forms (RMSNorm / SwiGLU input, accumulate). A "unit" is max(BS, 64) k: one or two 64-k chunks (a uint4 of code words
@@ -218,6 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
   float* sinv = reinterpret_cast<float*>(sblk + p.mc * (p.kp / BS));  // [mc][kp/BS] 2^-sigma_b
   float* ysum = reinterpret_cast<float*>(smem + p.off_ysum);  // [rows_cta][mc][33]: per warp
   float* rowsq = reinterpret_cast<float*>(smem + 64);         // [kConsumers][kMaxM] sums of x^2
+  volatile int* nonfin = reinterpret_cast<volatile int*>(smem);  // [kMaxM]: A row holds inf / NaN
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bar);
   uint64_t* empty = full + kMaxSlots;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kMaxSlots);
@@ -233,6 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
       ptx::mbar_init(&empty[s], kConsumers);
     }
     *abort_flag = 0;
+    for (int m = 0; m < kMaxM; ++m) nonfin[m] = 0;
     ptx::fence_mbar_init();
     griddep_launch_dependents();
   }
@@ -325,7 +365,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
     for (int u = 0; u < U; ++u) {
       if (u < nu) {
         const int f = base + tid + u * kC;
-        float bmax = fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w)));
+        // |x| as bits orders like the values, with inf and NaN above every finite value
+        uint32_t ub = max(max(__float_as_uint(fabsf(v[u].x)), __float_as_uint(fabsf(v[u].y))),
+                          max(__float_as_uint(fabsf(v[u].z)), __float_as_uint(fabsf(v[u].w))));
+        if (ub >= 0x7F800000u) {
+          // inf / NaN: the integer path takes 0 for them and the row's outputs get their exact
+          // fp32 terms at the end (nonfinite_terms), so they propagate as in the reference
+          if (f < n4) nonfin[f / n4row] = 1;
+          v[u].x = fabsf(v[u].x) <= 3.402823466e38f ? v[u].x : 0.f;
+          v[u].y = fabsf(v[u].y) <= 3.402823466e38f ? v[u].y : 0.f;
+          v[u].z = fabsf(v[u].z) <= 3.402823466e38f ? v[u].z : 0.f;
+          v[u].w = fabsf(v[u].w) <= 3.402823466e38f ? v[u].w : 0.f;
+          ub = max(max(__float_as_uint(fabsf(v[u].x)), __float_as_uint(fabsf(v[u].y))),
+                   max(__float_as_uint(fabsf(v[u].z)), __float_as_uint(fabsf(v[u].w))));
+        }
+        float bmax = __uint_as_float(ub);
         if constexpr (GL == 32) {  // one block per warp: non-negative floats order as their bits
           bmax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(bmax)));
         } else {
@@ -540,6 +594,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
       const int b = blockIdx.x + (r >> 4) * grid;
       const int64_t row = (int64_t)b * 16 + (r & 15);
       if (b < p.nblk && row < p.n_rows) {
+        if (nonfin[m]) {
+          // RMSNorm of a row holding inf / NaN is NaN everywhere (inf / inf, 0 * inf)
+          if (FU && p.gamma) acc = __int_as_float(0x7FC00000);
+          else acc += nonfinite_terms<BS, FU>(p, m, row);
+        }
         if constexpr (XG) {
           for (int r = 0; r < p.nranks; ++r) p.gy[r][(p.m0 + m) * p.gldy + p.gcol0 + row] = acc;
         } else {
@@ -586,14 +645,13 @@ __global__ void wait_gathered_kernel(const unsigned long long* arr, const unsign
 template <int BS, int NT, bool XG, bool FU>
 int launch(cudaStream_t st, const Args& a, int grid, size_t smem) {
   auto kern = gemv_mma_kernel<BS, NT, XG, FU>;
-  static bool configured[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !configured[dev]) {
+  static ContextOnce configured;
+  const int rc = configured.run([&] {
     MSQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax),
                  "mma gemv smem attribute");
-    configured[dev] = true;
-  }
+    return MSQ_OK;
+  });
+  if (rc != MSQ_OK) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);

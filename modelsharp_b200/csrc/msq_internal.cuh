@@ -6,6 +6,8 @@
 #include <cuda_bf16.h>
 #include <atomic>
 #include <cstdint>
+#include <mutex>
+#include <vector>
 
 #include "../../include/ms_cuda_nbits.h"
 
@@ -59,7 +61,8 @@ struct Weights {
   uint8_t* zp_ref_u8 = nullptr;
   float* zp_ref_f32 = nullptr;
   int64_t device_bytes = 0;
-  void* gemm_state = nullptr;
+  std::atomic<void*> gemm_state{nullptr};  // GEMM tensor maps, built by the first GEMM call
+  std::mutex state_mu;                     // guards that first build on this handle only
   cudaEvent_t packed_ev = nullptr;   // recorded on the packing stream after the repack kernels
   std::atomic<bool> settled{false};  // the host has seen packed_ev complete: kernels may read
                                      // the weights before their programmatic-dependency wait
@@ -75,6 +78,39 @@ int scratch_alloc(void** p, size_t bytes, cudaStream_t st);
 void scratch_free(void* p, cudaStream_t st);
 void note_path(const char* name);
 int num_sms(int device);
+
+// Identity of the CUDA context current on this thread (binding the current device's primary
+// context when the thread has none). It is cuCtxGetId's value, unique for the life of the
+// process: a CUcontext handle can come back for a new context after cudaDeviceReset or
+// cuCtxDestroy, with the library's module (and its __device__ arrays and function
+// attributes) loaded afresh, so per-context caches key on this id, not on the handle.
+int current_context_id(unsigned long long* id);
+
+// One-time set-up per CUDA context (a kernel's function attributes, a symbol's address):
+// run(fn) calls fn() the first time it meets the current context and again only in a new
+// context; fn's status is returned, and a failed fn is retried by the next call.
+class ContextOnce {
+ public:
+  template <class F>
+  int run(F&& fn) {
+    unsigned long long id = 0;
+    int rc = current_context_id(&id);
+    if (rc != 0) return rc;
+    std::lock_guard<std::mutex> lk(mu_);
+    for (unsigned long long d : done_)
+      if (d == id) return 0;
+    rc = fn();
+    if (rc == 0) done_.push_back(id);
+    return rc;
+  }
+
+ private:
+  std::mutex mu_;
+  std::vector<unsigned long long> done_;
+};
+
+// Diagnostic counters behind msq_diag_counter.
+void note_noalloc_lookup();
 
 #define MSQ_CUDA_TRY(expr, what)                         \
   do {                                                   \

@@ -10,9 +10,9 @@
 //
 //   - Size: kNoallocScratchBytes = MSQ_NOALLOC_SCRATCH_BYTES (16 MiB) per device, held from
 //     the time the library's device code is loaded on a GPU until the process exits.
-//   - Set-up: the first call in a CUDA context looks up the array's device address with
-//     cudaGetSymbolAddress (with that context current) and caches it; that first call should
-//     come before any stream capture.
+//   - Set-up: the first call that stages A in a CUDA context looks up the array's device
+//     address with cudaGetSymbolAddress (with that context current) and caches it under the
+//     context's id; that first call should come before any stream capture.
 //   - Sharing: every call in a context uses the same array, which keeps the last call's
 //     contents. Each call rewrites the whole staged region before the GEMM reads it, so
 //     nothing needs to start at zero; calls that overlap on the GPU (two streams, or two host
@@ -22,6 +22,7 @@
 #include <cuda.h>
 
 #include <mutex>
+#include <vector>
 
 namespace msq {
 namespace {
@@ -32,48 +33,32 @@ constexpr size_t kNoallocScratchBytes = MSQ_NOALLOC_SCRATCH_BYTES;
 // symbol, not a device address: it is only ever passed to cudaGetSymbolAddress.
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
 
-using PFN_getcur = CUresult (*)(CUcontext*);
-
 struct ScratchSlot {
-  CUcontext ctx;
+  unsigned long long ctx_id;  // cuCtxGetId of the context the address belongs to
   void* ptr;
 };
 
 std::mutex g_mu;
-ScratchSlot g_slots[64];
-int g_nslots = 0;
-PFN_getcur g_getcur = nullptr;
-bool g_getcur_tried = false;
+std::vector<ScratchSlot> g_slots;
 
-// Device address of g_noalloc_scratch in the current context (looked up once per context).
+// Device address of g_noalloc_scratch in the current context, looked up once per context.
+// Keyed by the context's id, not its CUcontext handle: after cudaDeviceReset or cuCtxDestroy
+// a new context may get the old handle while the module (and this array) is loaded afresh,
+// possibly at another address.
 int scratch_address(void** out) {
+  unsigned long long id = 0;
+  int rc = current_context_id(&id);
+  if (rc != MSQ_OK) return rc;
   std::lock_guard<std::mutex> lk(g_mu);
-  if (!g_getcur_tried) {
-    g_getcur_tried = true;
-    void* fn = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      g_getcur = reinterpret_cast<PFN_getcur>(fn);
-  }
-  if (!g_getcur) return fail(MSQ_E_CUDA, "cannot resolve cuCtxGetCurrent");
-  CUcontext ctx = nullptr;
-  if (g_getcur(&ctx) != CUDA_SUCCESS) return fail(MSQ_E_CUDA, "cuCtxGetCurrent failed");
-  if (!ctx) {
-    // A thread that has made no CUDA call yet: bind the current device's primary context.
-    int dev = 0;
-    MSQ_CUDA_TRY(cudaGetDevice(&dev), "cudaGetDevice");
-    MSQ_CUDA_TRY(cudaSetDevice(dev), "cudaSetDevice");
-    if (g_getcur(&ctx) != CUDA_SUCCESS || !ctx) return fail(MSQ_E_CUDA, "no current CUDA context");
-  }
-  for (int i = 0; i < g_nslots; ++i)
-    if (g_slots[i].ctx == ctx) {
-      *out = g_slots[i].ptr;
+  for (const ScratchSlot& s : g_slots)
+    if (s.ctx_id == id) {
+      *out = s.ptr;
       return MSQ_OK;
     }
   void* ptr = nullptr;
   MSQ_CUDA_TRY(cudaGetSymbolAddress(&ptr, g_noalloc_scratch), "cudaGetSymbolAddress(no-allocation scratch)");
-  if (g_nslots < 64) g_slots[g_nslots++] = {ctx, ptr};
+  note_noalloc_lookup();
+  g_slots.push_back({id, ptr});
   *out = ptr;
   return MSQ_OK;
 }
@@ -86,7 +71,8 @@ int run_gemm_noalloc(cudaStream_t st, const Weights& w, const void* d_a, int a_d
   const size_t need = gemm_staging_bytes(w, d_a, a_dtype, M);
   if (need > kNoallocScratchBytes)
     return fail(MSQ_E_INVALID,
-                "msq_matmul_noalloc: staging A as fp16 needs %zu bytes (M=%lld x K=%d rounded up to 8) but the "
+                "msq_matmul_noalloc: staging A as fp16 needs %zu bytes (M=%lld rows of K=%d rounded up to 8 plus a row "
+                "scale each) but the "
                 "fixed scratch holds %zu; split M into smaller calls or pass 16-byte-aligned float16 A with "
                 "K %% 8 == 0, which needs no staging",
                 need, (long long)M, w.K, kNoallocScratchBytes);
