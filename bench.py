@@ -1,23 +1,33 @@
-"""MatMulNBits INT4 decode benchmark on B200 (one JSON line on rank 0).
+"""MatMulNBits INT4 benchmark on B200 (one JSON line on rank 0).
 
-Workload: the 7B-shaped decode GEMV sweep at M=1, block_size 128,
-fp32 A ~ N(0,1), packed uint4 zero points, fp32 scales U[0.001, 0.01], shapes (K, N) =
-(4096, 4096), (4096, 1024), (4096, 14336), (14336, 4096), (4096, 32000). One step = one
-MatMulNBits op per shape (5 ops, 144 216 064 algorithmic bytes: weights + scales + zero
-points as the reference stores them). Value = algorithmic GB/s over all ranks.
+Headline: the 7B-shaped decode GEMV sweep at M=1, block_size 128, fp32
+A ~ N(0,1), packed uint4 zero points, fp32 scales U[0.001, 0.01], shapes (K, N) = (4096, 4096),
+(4096, 1024), (4096, 14336), (14336, 4096), (4096, 32000). One step = one MatMulNBits op per
+shape (5 ops, 144 216 064 algorithmic bytes: weights + scales + zero points as the reference
+stores them). value = algorithmic GB/s of the whole job.
 
-* value     inputs resident in HBM; each step is one CUDA-graph replay of the 5 launches;
-            4 weight replicas rotate so the 577 MB working set exceeds the 126 MB L2.
+* value     inputs resident in HBM; each step is one CUDA-graph replay of the 5 launches; 4
+            weight replicas rotate so the 577 MB working set exceeds the 126 MB L2. Timed as
+            --windows windows of exactly --steps steps (each bracketed by a barrier and a
+            synchronize); value from the median window, the spread in config.timing.
+* per_M     the same sweep at M = 4 and M = 16 (configs[1]'s batched rows; same weight bytes).
 * e2e       the same ops through the C-ABI host-buffer entry (msq_matmul_host): pinned host
             A copied in and Y copied out inside the timed region, synchronous per op.
 * roofline  the decode GEMV kernel: algorithmic bytes / its CUDA-event launch duration vs
             the measured HBM copy bandwidth (MEASURED_PEAKS.json).
 * cpu_baseline  the reference's own ms_qgemm_nbits (oracle/_ref, built from the reference
             sources) on this host's cores over whole sweeps for ~10 s.
+* sub       at N = 1 the other two headline metrics, each a full record of its own (timing,
+            clocks, parity, roofline, CPU baseline, e2e): "prefill" (configs[2], TFLOP/s of the
+            tcgen05 GEMM at M = 512 / 2048 / 8192) and "decode7b" (configs[4], tok/s of the
+            synthetic 7B decoder, 128 greedy tokens after a 512-token prompt, every token checked
+            against the CPU checker). --no-sub skips them.
 
---impl reference times that reference CPU kernel as the arm itself (rank 0 only).
-Multi-GPU (torchrun): every rank runs its own copy of the sweep (weak scaling, no
-collective); timing is the max over ranks.
+Multi-GPU (torchrun, N > 1): the sweep column-split over the ranks: every shape's rows are
+sharded, each shard's GEMV stores its outputs into every rank's full Y over NVLink, and each op
+waits on the device for all ranks' shards of the previous op's Y (strong scaling, max over
+ranks). --impl reference times the reference CPU kernel as the arm itself (rank 0 only, all host
+threads). --workload prefill / nsplit70b / decode7b run one of the other configs alone.
 """
 from __future__ import annotations
 
@@ -85,6 +95,52 @@ def tensor_peak() -> tuple[float, str]:
         except Exception:
             pass
     return 1400.0, "fallback sustained bf16"
+
+
+def burst_tensor_peak() -> tuple[float, str]:
+    """Dense bf16 tensor peak for a kernel timed in isolation: the measured burst cuBLAS rate."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured burst cuBLAS bf16"
+        except Exception:
+            pass
+    return 1590.0, "fallback burst bf16"
+
+
+def timed_windows(args, world: int, dev, stream, replay) -> list[float]:
+    """args.windows timed windows of exactly args.steps calls of replay(i) on `stream`, each
+    bracketed by a barrier and a synchronize; CUDA-event ms per window, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    out = []
+    i = 0
+    for _ in range(args.windows):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(args.steps):
+                replay(i)
+                i += 1
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        out.append(e0.elapsed_time(e1))
+    if world > 1:
+        t = torch.tensor(out, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        out = [float(v) for v in t.tolist()]
+    return out
+
+
+def window_stats(wins: list[float]) -> tuple[float, dict]:
+    """Median window (ms) and the spread of all windows in ms per window."""
+    srt = sorted(wins)
+    q = lambda f: srt[min(len(srt) - 1, int(f * (len(srt) - 1) + 0.5))]
+    return statistics.median(srt), {"windows": len(srt), "ms_per_window": {
+        "median": statistics.median(srt), "min": srt[0], "p10": q(0.1), "p90": q(0.9), "max": srt[-1]}}
 
 
 # ---------------------------------------------------------------- clocks (NVML, in-process)
@@ -162,9 +218,24 @@ def time_reference_sweep(cases, budget_s: float, min_reps: int = 2):
     return statistics.median(times), len(times), kind
 
 
+def use_all_host_threads() -> int:
+    """OpenMP over every host thread for the CPU reference, also under torchrun (which sets
+    OMP_NUM_THREADS=1 for its workers): the env var for libraries not yet loaded, and
+    omp_set_num_threads for the process's libgomp."""
+    n = os.cpu_count() or 1
+    os.environ["OMP_NUM_THREADS"] = str(n)
+    try:
+        gomp = C.CDLL("libgomp.so.1")
+        gomp.omp_set_num_threads(n)
+        return int(gomp.omp_get_max_threads())
+    except OSError:
+        return n
+
+
 def run_reference_arm(args, rank: int, world: int):
     if rank != 0:
         return
+    threads = use_all_host_threads()
     cases = make_cases()
     nbytes = step_bytes()
     from oracle import oracle
@@ -179,11 +250,12 @@ def run_reference_arm(args, rank: int, world: int):
             fn(c)
     dt = time.perf_counter() - t0
     value = nbytes * args.steps / dt / 1e9
-    cores = os.cpu_count()
+    cores = threads
     out = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
         "config": {"workload": WORKLOAD, "bytes_per_step": nbytes},
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": kind,
                          "sample": f"{args.steps} whole sweeps of ms_qgemm_nbits, OpenMP over all {cores} host "
@@ -247,25 +319,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     # Parity spot check of this exact data (not timed).
     y_chk = [y.cpu().numpy() for y in y_dev]
 
-    # ---- timed region: K graph replays
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # ---- timed region: args.windows windows of exactly K graph replays, each bracketed by a
+    # barrier and a synchronize; value from the median window (max over ranks per window)
     with ClockSampler(local_rank) as clk:
-        ev0.record(stream)
-        with torch.cuda.stream(stream):
-            for i in range(args.steps):
-                graphs[i % REPLICAS].replay()
-        ev1.record(stream)
-        torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    ms = ev0.elapsed_time(ev1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        wins = timed_windows(args, world, dev, stream, lambda i: graphs[i % REPLICAS].replay())
+    ms, spread = window_stats(wins)
     value = world * nbytes * args.steps / (ms * 1e-3) / 1e9
 
     # ---- roofline. Every launch of the timed region is the decode GEMV, so its average
@@ -308,6 +366,44 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                 "peak_source": f"{peak_kind} HBM copy bandwidth", "kernel": path,
                 "bytes_per_launch": bytes_per_launch, "launch_us": launch_us, "per_shape": per_shape}
 
+    # ---- configs[1] at M = 4 and 16: the same sweep, weights and bytes, more A rows; one CUDA
+    # graph per replica, timed like the step (median of windows)
+    per_m = []
+    y_chk_m = {}
+    for M in (4, 16):
+        a_m = [torch.from_numpy(synth.make_case(50 + i, M, c["N"], c["K"], 4, BS, "packed")["a"]).to(dev)
+               for i, c in enumerate(cases)]
+        y_m = [torch.empty(M, c["N"], device=dev) for c in cases]
+
+        def step_m(r: int):
+            for w, a, y, c in zip(reps[r], a_m, y_m, cases):
+                rc = lib.msq_matmul(None, sptr, w.handle, a.data_ptr(), N.DT_F32, M, y.data_ptr(), c["N"])
+                if rc:
+                    N.check(rc)
+
+        with torch.cuda.stream(stream):
+            step_m(0)
+        stream.synchronize()
+        path_m = N.last_path()
+        c0 = N.launch_count()
+        gm = []
+        for r in range(REPLICAS):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                step_m(r)
+            gm.append(g)
+        launches_m = (N.launch_count() - c0) // REPLICAS
+        with torch.cuda.stream(stream):
+            for i in range(3):
+                gm[i % REPLICAS].replay()
+        wins_m = timed_windows(argparse.Namespace(windows=5, steps=args.steps), world, dev, stream,
+                               lambda i: gm[i % REPLICAS].replay())
+        ms_m = statistics.median(wins_m)
+        y_chk_m[M] = (a_m, [y.cpu().numpy() for y in y_m])
+        per_m.append({"M": M, "ms_per_step": ms_m / args.steps, "GB/s": world * nbytes * args.steps / (ms_m * 1e-3) / 1e9,
+                      "launches_per_step": launches_m, "path": path_m})
+        del gm
+
     # ---- e2e: host buffers through the C ABI, copies inside the timed region
     a_host = [torch.from_numpy(c["a"]).pin_memory() for c in cases]
     y_host = [torch.empty(1, c["N"]).pin_memory() for c in cases]
@@ -346,6 +442,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     if rank == 0:
         from oracle import oracle
         parity = max(oracle.rel_l2(y, oracle.managed(c)) for y, c in zip(y_chk, cases))
+        for pm in per_m:
+            a_m, ys = y_chk_m[pm["M"]]
+            pm["parity_rel_l2"] = max(oracle.rel_l2(y, oracle.managed(dict(c, a=a.cpu().numpy(), M=pm["M"])))
+                                      for y, a, c in zip(ys, a_m, cases))
         if world == 1:
             med, reps_done, kind = time_reference_sweep(cases, budget_s=args.cpu_seconds)
             cores = os.cpu_count()
@@ -362,7 +462,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                        "l2": f"inputs larger than L2: {REPLICAS} weight replicas rotate, "
                              f"{REPLICAS * nbytes / 1e6:.0f} MB working set vs 126 MB L2",
                        "launch": "one CUDA graph replay per step", "parity_rel_l2": parity,
-                       "parallelism": f"replicas{world}"},
+                       "parallelism": f"replicas{world}", "timing": spread,
+                       "per_M": per_m},
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -370,12 +471,152 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk.summary(),
         }
-        print(json.dumps(out), flush=True)
+    else:
+        out = None
     for g in graphs:
         del g
     for rr in reps:
         for w in rr:
             w.free()
+    return out
+
+
+# ---------------------------------------------------------------- the sweep column-split (N > 1)
+def run_split_sweep(args, rank: int, world: int, local_rank: int):
+    """The configs[1] sweep split over the ranks (the default under torchrun): every shape's
+    rows are sharded over the ranks (ShardedMatMulNBits), each shard's decode GEMV stores its
+    outputs into every rank's full Y over NVLink (msq_matmul_gather, plain peer stores), and
+    each op waits on the device for all ranks' shards of the previous op's Y before it starts,
+    as a layer that reads that Y would; the step's last Y is waited for by the next step's first
+    op. value = the sweep's algorithmic bytes per step over the max-over-ranks step time
+    (strong scaling: the total work is fixed)."""
+    import torch
+    import torch.distributed as dist
+
+    from modelsharp_b200 import QuantizedWeights, synth
+    from modelsharp_b200 import _native as N
+    from modelsharp_b200.nsplit import ShardedMatMulNBits
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    nbytes = step_bytes()
+    cases = make_cases()
+    ops = [ShardedMatMulNBits(c["b"], c["scales"], c["zp"], c["N"], c["K"], 4, BS, device=dev, gather="p2p")
+           for c in cases]
+    shard_bytes = nbytes / world
+    reps_n = max(REPLICAS, -(-int(480e6) // int(shard_bytes)))  # the rotation exceeds L2 on every rank
+    reps_n += reps_n % 2  # even: each op's two exchange buffers alternate across the graphs' wrap-around
+    # weight replicas of this rank's shards; replica 0 is the op's own
+    reps = [[op.weights] + [QuantizedWeights(c["b"], c["scales"], c["zp"], c["N"], c["K"], 4, BS,
+                                             rows=(op.n0, op.n1), device=dev) for _ in range(reps_n - 1)]
+            for op, c in zip(ops, cases)]
+    a_dev = [torch.from_numpy(c["a"]).to(dev) for c in cases]
+    stream = torch.cuda.Stream(dev)
+    outs = [None] * len(ops)
+
+    def step(r: int):
+        for si, op in enumerate(ops):
+            op.weights = reps[si][r]
+            prev = ops[si - 1].out_wait  # the previous op's gathered Y (the last op's, for op 0)
+            outs[si] = op(a_dev[si], wait=prev)
+
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            step(i % reps_n)
+    stream.synchronize()
+    c0 = N.launch_count()
+    graphs = []
+    for r in range(reps_n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step(r)
+        graphs.append(g)
+    launches_per_step = (N.launch_count() - c0) // reps_n
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            graphs[i % reps_n].replay()
+        ops[-1].wait_gathered()
+    stream.synchronize()
+    with ClockSampler(local_rank) as clk:
+        wins = timed_windows(args, world, dev, stream, lambda i: graphs[i % reps_n].replay())
+    ms, spread = window_stats(wins)
+    value = nbytes * args.steps / (ms * 1e-3) / 1e9
+    with torch.cuda.stream(stream):
+        for op in ops:
+            op.wait_gathered()
+    stream.synchronize()
+    y_chk = [o.cpu().numpy().copy() for o in outs]
+
+    # e2e: pinned host A in and every op's gathered Y out, each step, timed with events
+    a_host = [torch.from_numpy(c["a"]).pin_memory() for c in cases]
+    y_host = [torch.empty(1, c["N"]).pin_memory() for c in cases]
+    e2e_steps = max(1, min(args.steps, 500))
+
+    def e2e_step(i: int):
+        r = i % reps_n
+        with torch.cuda.stream(stream):
+            for si, op in enumerate(ops):
+                op.weights = reps[si][r]
+                y = op(a_host[si].to(dev, non_blocking=True), wait=ops[si - 1].out_wait)
+                op.wait_gathered()
+                y_host[si].copy_(y, non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(e2e_steps):
+        e2e_step(i)
+    e1.record(stream)
+    stream.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = nbytes * e2e_steps / (e2e_ms * 1e-3) / 1e9
+    peak, peak_kind = peaks()
+    per_rank = shard_bytes / (ms / args.steps * 1e-3) / 1e9
+    out = None
+    if rank == 0:
+        from oracle import oracle
+        parity = max(oracle.rel_l2(y, oracle.managed(c)) for y, c in zip(y_chk, cases))
+        out = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD + f"; every shape column-split over {world} ranks, Y assembled on every "
+                                              "rank by peer stores", "bytes_per_step": nbytes,
+                       "weights": "u4 (int4 codes)", "parallelism": f"nsplit{world}",
+                       "l2": f"inputs larger than L2: {reps_n} replicas of each rank's shards rotate "
+                             f"({reps_n * shard_bytes / 1e6:.0f} MB per rank vs 126 MB L2)",
+                       "launch": f"one CUDA graph replay per step: {launches_per_step} decode-GEMV launches, each "
+                                 "storing its shard into every rank's Y over NVLink and waiting on the device for "
+                                 "all ranks' shards of the previous op's Y",
+                       "gather": "p2p peer stores (msq_matmul_gather), no multicast", "timing": spread,
+                       "parity_rel_l2": parity, "parity_of": "rank 0's assembled full Y of every op vs the checker"},
+            "roofline": {"bound": "hbm", "achieved": per_rank, "peak": peak, "unit": "GB/s", "frac": per_rank / peak,
+                         "traffic": None, "peak_source": f"{peak_kind} HBM copy bandwidth",
+                         "note": "per-rank shard bytes over the whole step time (peer stores and waits included)"},
+            "cpu_baseline": None,
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": sum(a.numel() * 4 for a in a_host),
+                    "d2h_bytes_per_step": sum(y.numel() * 4 for y in y_host), "steps": e2e_steps,
+                    "entry": "ShardedMatMulNBits (pinned host A in, gathered Y out)"},
+            "gpu_launches": launches_per_step * args.steps * args.windows,
+            "clocks": clk.summary(),
+        }
+    for g in graphs:
+        del g
+    graphs.clear()
+    for si, op in enumerate(ops):
+        op.weights = reps[si][0]
+        for w in reps[si][1:]:
+            w.free()
+        op.free()
+    return out
 
 
 # ---------------------------------------------------------------- N-split workload (configs[3])
@@ -405,6 +646,7 @@ def run_nsplit(args, rank: int, world: int, local_rank: int):
     shard_bytes = nbytes / world
     # enough replicas of this rank's shards that the rotation exceeds L2 (>= 320 MB per rank)
     reps_n = max(2, -(-int(320e6) // int(shard_bytes)))
+    reps_n += reps_n % 2  # even: each layer's two exchange buffers alternate across the graphs' wrap-around
     full = [[torch.from_numpy(np.ascontiguousarray(x)).to(dev) if x is not None else None
              for x in (c["b"], c["scales"], c["zp"])] for c in cases]
     gather = args.gather if M <= 4 else "nccl"
@@ -535,13 +777,15 @@ def run_nsplit(args, rank: int, world: int, local_rank: int):
             "gpu_launches": per_step_launches * args.steps,
             "clocks": clk.summary(),
         }
-        print(json.dumps(out), flush=True)
+    else:
+        out = None
     for g in graphs:
         del g
     graphs.clear()
     for rr in reps:
         for sh in rr:
             sh.free()
+    return out
 
 
 # ---------------------------------------------------------------- prefill GEMM workload
@@ -675,8 +919,9 @@ def run_prefill(args, rank: int, world: int, local_rank: int):
             cw = dict(wb, a=c["a"], M=m)  # every GEMM runs on the first case's weights
             par.append(oracle.rel_l2(np.concatenate([yy[r] for r in rows]),
                                      np.concatenate([oracle.managed(cw, rows=r) for r in rows])))
-        pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
-        peak = float(pk.get("bf16_tflops_sustained", 1400.0))
+        # each GEMM launch of the step is timed as it runs, back to back in a 1.5 ms step: the
+        # burst cuBLAS rate is the matching denominator
+        peak, peak_src = burst_tensor_peak()
         cpu = None
         if world == 1:
             c = cases[0]
@@ -702,8 +947,7 @@ def run_prefill(args, rank: int, world: int, local_rank: int):
                        "parity_rel_l2_sampled_rows": max(par)},
             "roofline": {"bound": "tensor", "achieved": value / world, "peak": peak, "unit": "TFLOP/s",
                          "frac": value / world / peak, "traffic": None,
-                         "peak_source": "measured cuBLAS bf16, sustained" if pk else "fallback",
-                         "per_M": per_m},
+                         "peak_source": peak_src, "per_M": per_m},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": sum(a.numel() * 2 for a in a_host),
@@ -712,10 +956,12 @@ def run_prefill(args, rank: int, world: int, local_rank: int):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk.summary(),
         }
-        print(json.dumps(out), flush=True)
+    else:
+        out = None
     graphs.clear()
     for w in reps:
         w.free()
+    return out
 
 
 # ---------------------------------------------------------------- end-to-end decoder
@@ -727,14 +973,18 @@ DECODE_WORKLOAD = ("synthetic 7B-shaped INT4 decoder (BASELINE configs[4]): 32 l
                    "the prompt pass")
 
 
-def decode_checks(host_w, cfg, prompt_h, generate, args):
-    """Greedy parity on a 16-token prompt (4 tokens from `generate(prompt, n)` against the CPU
-    checker) and the checker's own decode rate as the CPU baseline."""
+def decode_checks(host_w, cfg, prompt_h, tokens, args):
+    """Greedy parity of the timed generation's 128 tokens against the CPU checker (one
+    teacher-forced pass over the prompt and the generated tokens, with the checker's top-2 logit
+    margin per step), and the checker's own decode rate as the CPU baseline."""
     from oracle import decoder as od
+    t0 = time.perf_counter()
+    r = od.greedy_check(host_w, cfg, prompt_h.numpy(), np.asarray(tokens))
+    match = {"tokens_equal": r["matches"], "of": r["steps"], "first_mismatch": r["first_mismatch"],
+             "min_top2_margin": r["min_margin"], "min_margin_step": r["min_margin_step"],
+             "check": f"teacher-forced CPU pass of oracle/decoder.py over the {len(prompt_h)}-token prompt and the "
+                      f"generated tokens ({time.perf_counter() - t0:.0f} s)"}
     short = prompt_h[:16]
-    ref, _ = od.generate(host_w, cfg, short.numpy(), 4)
-    got = generate(short, 4)
-    match = f"{int((got == ref).sum())}/4 greedy tokens equal (16-token prompt, exact path)"
     cache = {"k": np.zeros((cfg.layers, cfg.kv_heads, cfg.max_seq, cfg.head_dim), np.float32),
              "v": np.zeros((cfg.layers, cfg.kv_heads, cfg.max_seq, cfg.head_dim), np.float32),
              "rope": od.rope_tables(cfg)}
@@ -819,8 +1069,7 @@ def run_decode_engine(args, rank: int, world: int, local_rank: int):
     if rank == 0:
         cpu, match = None, None
         if host_w is not None:
-            cpu, match = decode_checks(host_w, cfg, prompt_h, lambda short, n: eng.generate(short, n)[0].cpu().numpy(),
-                                       args)
+            cpu, match = decode_checks(host_w, cfg, prompt_h, gen[0].cpu().numpy(), args)
         res = {
             "metric": "7B INT4 decode tok/s", "value": world * 1e3 / ms_tok, "unit": "tok/s", "n_gpus": world,
             "steps": steps, "warmup": 2, "ms_per_step": ms_tok, "higher_is_better": True, "scaling": "weak",
@@ -843,8 +1092,10 @@ def run_decode_engine(args, rank: int, world: int, local_rank: int):
             "gpu_launches": prompt_launches + per_run * reps * (n_new - 1),
             "clocks": clk.summary(),
         }
-        print(json.dumps(res), flush=True)
+    else:
+        res = None
     eng.release()
+    return res
 
 
 def run_decode(args, rank: int, world: int, local_rank: int):
@@ -948,9 +1199,7 @@ def run_decode(args, rank: int, world: int, local_rank: int):
     if rank == 0:
         cpu, match = None, None
         if host_w is not None:
-            cpu, match = decode_checks(host_w, cfg, prompt_h,
-                                       lambda short, n: dec.generate(short.to(dev), n, N.PATH_GEMV).cpu().numpy(),
-                                       args)
+            cpu, match = decode_checks(host_w, cfg, prompt_h, tokens[0], args)
         res = {
             "metric": "7B INT4 decode tok/s", "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps,
             "warmup": 2, "ms_per_step": ms_tok, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -972,9 +1221,11 @@ def run_decode(args, rank: int, world: int, local_rank: int):
             "gpu_launches": launches,
             "clocks": clk.summary(),
         }
-        print(json.dumps(res), flush=True)
+    else:
+        res = None
     del g
     dec.free()
+    return res
 
 
 def main():
@@ -995,6 +1246,10 @@ def main():
                          "the fused decode step")
     ap.add_argument("--layers", type=int, default=32,
                     help="decode7b: decoder layers (32 = the 7B shape; fewer only for small profiling cases)")
+    ap.add_argument("--windows", type=int, default=30,
+                    help="timed windows of --steps steps each (sweep workloads); value from the median window")
+    ap.add_argument("--no-sub", action="store_true",
+                    help="N = 1 sweep only: skip the prefill and 7B decode sub-records")
     ap.add_argument("--shapes", default="",
                     help="restrict the step to these KxN shapes (comma separated), for profiling one shape")
     args = ap.parse_args()
@@ -1021,13 +1276,26 @@ def main():
                                 device_id=torch.device("cuda", local_rank))
     try:
         if args.workload == "nsplit70b":
-            run_nsplit(args, rank, world, local_rank)
+            out = run_nsplit(args, rank, world, local_rank)
         elif args.workload == "prefill":
-            run_prefill(args, rank, world, local_rank)
+            out = run_prefill(args, rank, world, local_rank)
         elif args.workload == "decode7b":
-            (run_decode_engine if args.engine else run_decode)(args, rank, world, local_rank)
+            out = (run_decode_engine if args.engine else run_decode)(args, rank, world, local_rank)
+        elif world > 1:
+            out = run_split_sweep(args, rank, world, local_rank)
         else:
-            run_ours(args, rank, world, local_rank)
+            out = run_ours(args, rank, world, local_rank)
+            if not args.no_sub:
+                # the other two headline metrics (BASELINE metric: prefill TFLOPS, 7B decode tok/s),
+                # each with its own timing, clocks, parity, roofline and CPU baseline
+                log("sub-record: prefill (configs[2])")
+                pre = run_prefill(args, rank, world, local_rank)
+                log("sub-record: 7B decode (configs[4])")
+                dec = run_decode(args, rank, world, local_rank)
+                if out is not None:
+                    out["sub"] = {"prefill": pre, "decode7b": dec}
+        if rank == 0 and out is not None:
+            print(json.dumps(out), flush=True)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -149,6 +149,14 @@ int msq_matmul_noalloc(void* cu_ctx, void* stream, msq_weights_t w,
                        const void* d_a, int a_dtype, int64_t M,
                        float* d_y, int64_t ldy);
 
+/* Sets how long a device-side wait of this library's kernels (a pipeline stage to arrive or
+ * to free up, tensor-core completion, copies in flight, other ranks' shards of a gathered
+ * input) may last before the kernel gives up, leaves and reports MSQ_E_TIMEOUT through
+ * msq_device_status; ns <= 0 restores the default of 2 s. Applies to the current device's
+ * context, for launches made after the call. No counterpart in the reference (its kernels
+ * have no device-side waits).                                                            */
+int msq_set_wait_budget(void* cu_ctx, int64_t ns);
+
 /* Diagnostic counters of this process (the role of NativeCuda.cs:147-150's call counter),
  * -1 for an unknown `which`:
  *   MSQ_DIAG_POOL_ALLOCS      stream-ordered allocations the library has taken from its

@@ -83,6 +83,7 @@ SIGNATURES: dict[str, tuple] = {
     "msq_matmul_host": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp]),
     "msq_matmul_noalloc": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp, _i64]),
     "msq_device_status": (_i32, [_vp, _vp]),
+    "msq_set_wait_budget": (_i32, [_vp, _i64]),
     "msq_xbuf_alloc": (_i32, [_vp, _i64, _vp]),
     "msq_xbuf_free": (_i32, [_vp, _vp]),
     "msq_ipc_handle": (_i32, [_vp, _vp, _vp]),

@@ -584,6 +584,15 @@ int msq_matmul_noalloc(void* cu_ctx, void* stream, msq_weights_t h, const void* 
   return run_gemm_noalloc(static_cast<cudaStream_t>(stream), *w, d_a, a_dtype, M, d_y, ldy);
 }
 
+int msq_set_wait_budget(void* cu_ctx, int64_t ns) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  const unsigned long long v = ns > 0 ? (unsigned long long)ns : 2000000000ull;
+  int rc = set_wait_budget_gemv(v);
+  if (rc == MSQ_OK) rc = set_wait_budget_gemm(v);
+  return rc;
+}
+
 int msq_device_status(void* cu_ctx, void* stream) {
   CtxGuard g(cu_ctx);
   if (g.rc != MSQ_OK) return g.rc;

@@ -87,7 +87,7 @@ __device__ __forceinline__ bool wait_abort(uint64_t* bar, uint32_t parity, volat
     if (ptx::mbar_try_wait_sleep(bar, parity)) return true;
     if ((i & 7u) == 0) {
       if (*abort_flag) return false;
-      if (ptx::globaltimer() - t0 > ptx::kWaitBudgetNs) {
+      if (ptx::globaltimer() - t0 > ptx::wait_budget_ns()) {
         *abort_flag = 1;
         atomicCAS(&g_gemm_err, 0, code);
         return false;
@@ -188,7 +188,7 @@ __global__ void __launch_bounds__(Plan<TM, BN>::kThreads, 1)
         const int last = s + (issued - 1 - s) / S * S;
         const unsigned long long t0 = ptx::globaltimer();
         while (!ptx::mbar_try_wait(&full[s], (last / S) & 1)) {
-          if (ptx::globaltimer() - t0 > ptx::kWaitBudgetNs) {
+          if (ptx::globaltimer() - t0 > ptx::wait_budget_ns()) {
             atomicCAS(&g_gemm_err, 0, ptx::kErrTimeoutDrain);
             break;
           }
@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(Plan<TM, BN>::kThreads, 1)
       // the accumulator (and every MMA reading shared memory) must be done before exit
       const unsigned long long t0 = ptx::globaltimer();
       while (!ptx::mbar_try_wait(accum, 0)) {
-        if (ptx::globaltimer() - t0 > ptx::kWaitBudgetNs) {
+        if (ptx::globaltimer() - t0 > ptx::wait_budget_ns()) {
           atomicCAS(&g_gemm_err, 0, ptx::kErrTimeoutMma);
           break;
         }
@@ -644,6 +644,11 @@ int run_gemm_staged(cudaStream_t st, const Weights& w, const void* d_a, int a_dt
 
 void release_gemm_state(Weights& w) {
   delete static_cast<GemmState*>(w.gemm_state.exchange(nullptr));
+}
+
+int set_wait_budget_gemm(unsigned long long ns) {
+  MSQ_CUDA_TRY(cudaMemcpyToSymbol(ptx::g_wait_budget_ns, &ns, sizeof ns), "set GEMM wait budget");
+  return MSQ_OK;
 }
 
 int read_gemm_errors(cudaStream_t st, int* flags) {

@@ -87,7 +87,7 @@ __device__ __forceinline__ bool wait_arrivals(const unsigned long long* arr, con
     unsigned long long v;
     asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(arr) : "memory");
     if (v >= target) return true;
-    if (ptx::globaltimer() - t0 > ptx::kWaitBudgetNs) {
+    if (ptx::globaltimer() - t0 > ptx::wait_budget_ns()) {
       atomicCAS(&g_mma_err, 0, kErrTimeoutPeer);
       return false;
     }
@@ -103,7 +103,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
     if (ptx::mbar_try_wait_sleep(bar, parity)) return true;
     if ((i & 7u) == 0) {
       if (*abort_flag) return false;
-      if (ptx::globaltimer() - t0 > ptx::kWaitBudgetNs) {
+      if (ptx::globaltimer() - t0 > ptx::wait_budget_ns()) {
         *abort_flag = 1;
         atomicCAS(&g_mma_err, 0, code);
         return false;
@@ -307,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
         const int last = q + (issued - 1 - q) / p.nslots * p.nslots;
         const unsigned long long t0 = ptx::globaltimer();
         while (!ptx::mbar_try_wait(&full[q], (last / p.nslots) & 1)) {
-          if (ptx::globaltimer() - t0 > ptx::kWaitBudgetNs) {
+          if (ptx::globaltimer() - t0 > ptx::wait_budget_ns()) {
             atomicCAS(&g_mma_err, 0, ptx::kErrTimeoutDrain);
             break;
           }
@@ -825,6 +825,11 @@ int run_wait_gathered(cudaStream_t st, const msq_wait_t* wt) {
   wait_gathered_kernel<<<1, 32, 0, st>>>(wt->arrivals, wt->produced, wt->nranks);
   note_launch();
   MSQ_CUDA_TRY(cudaGetLastError(), "wait kernel launch");
+  return MSQ_OK;
+}
+
+int set_wait_budget_gemv(unsigned long long ns) {
+  MSQ_CUDA_TRY(cudaMemcpyToSymbol(ptx::g_wait_budget_ns, &ns, sizeof ns), "set decode GEMV wait budget");
   return MSQ_OK;
 }
 

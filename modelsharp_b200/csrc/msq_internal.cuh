@@ -126,6 +126,9 @@ int repack_stream(cudaStream_t st, Weights& w, const uint8_t* d_b, int n_begin,
 void plan_stream(Weights& w);
 int read_gemv_mma_errors(cudaStream_t st, int* flags);
 int read_gemm_errors(cudaStream_t st, int* flags);
+// Bounded-wait budgets of the decode GEMV's and the GEMM's modules on the current device.
+int set_wait_budget_gemv(unsigned long long ns);
+int set_wait_budget_gemm(unsigned long long ns);
 int repack_reference(cudaStream_t st, Weights& w, const uint8_t* d_b, int n_begin,
                      const void* d_scales, int scales_dtype, const void* d_zp);
 

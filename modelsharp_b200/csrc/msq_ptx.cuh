@@ -1,7 +1,7 @@
 // Inline-PTX helpers for sm_100a: mbarriers with bounded waits, bulk / tensor async copies,
 // and the tcgen05 (5th-generation tensor core + TMEM) instructions used by the kernels.
 //
-// Every wait is bounded: after kWaitBudgetNs of global time without the phase flipping it
+// Every wait is bounded: after wait_budget_ns() of global time without the phase flipping it
 // records an error code in the caller's device error word and returns false, so a kernel can
 // leave instead of hanging the GPU. Callers then skip their remaining work.
 #pragma once
@@ -10,7 +10,15 @@
 namespace msq {
 namespace ptx {
 
-constexpr unsigned long long kWaitBudgetNs = 2000000000ull;  // 2 s
+constexpr unsigned long long kDefaultWaitBudgetNs = 2000000000ull;  // 2 s
+
+// The wait budget in force for the kernels of the including translation unit (each is its own
+// module, with its own copy of this word per CUDA context); the host sets it through
+// msq_set_wait_budget, so a test can make a wait run out in milliseconds.
+static __device__ unsigned long long g_wait_budget_ns = kDefaultWaitBudgetNs;
+__device__ __forceinline__ unsigned long long wait_budget_ns() {
+  return *reinterpret_cast<volatile unsigned long long*>(&g_wait_budget_ns);
+}
 
 // Error codes written into a kernel's device error word.
 constexpr int kErrTimeoutFull = 1;   // consumer gave up waiting for data
@@ -78,7 +86,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   const unsigned long long t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait_sleep(bar, parity)) return true;
-    if ((i & 7u) == 0 && globaltimer() - t0 > kWaitBudgetNs) {
+    if ((i & 7u) == 0 && globaltimer() - t0 > wait_budget_ns()) {
       if (err) atomicCAS(err, 0, code);
       return false;
     }

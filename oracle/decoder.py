@@ -127,3 +127,77 @@ def generate(weights: dict, cfg, prompt: np.ndarray, n_new: int) -> tuple[np.nda
         all_logits.append(logits)
         pos += 1
     return np.asarray(out), all_logits
+
+
+def _dense(w: dict, n: int, k: int, cfg) -> np.ndarray:
+    """W [n, k] in fp32, (q - zp) * scale (oracle.dequant)."""
+    return oracle.dequant(dict(b=w["b"], scales=w["scales"], zp=w["zp"], zp_kind="packed", N=n, K=k, bits=4,
+                               block_size=cfg.block_size))
+
+
+def causal_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, cfg) -> np.ndarray:
+    """attention() over a whole sequence from position 0 at once: q [S, H*d], k / v [S, Hkv*d];
+    row i attends to positions 0..i with the same scale, max-subtracted exp and normalisation."""
+    s, d, hq, hkv = q.shape[0], cfg.head_dim, cfg.heads, cfg.kv_heads
+    group = hq // hkv
+    scale = np.float32(1.0 / np.sqrt(d))
+    qv, kv, vv = q.reshape(s, hq, d), k.reshape(s, hkv, d), v.reshape(s, hkv, d)
+    future = np.triu(np.ones((s, s), dtype=bool), 1)
+    out = np.empty((s, hq, d), dtype=np.float32)
+    for h in range(hq):
+        g = h // group
+        sc = (qv[:, h] @ kv[:, g].T) * scale
+        sc[future] = -np.inf
+        e = np.exp(sc - sc.max(axis=1, keepdims=True))
+        out[:, h] = (e / e.sum(axis=1, keepdims=True)) @ vv[:, g]
+    return out.reshape(s, hq * d)
+
+
+def teacher_forced_logits(weights: dict, cfg, tokens: np.ndarray, score_from: int) -> np.ndarray:
+    """Logits [len(tokens) - score_from, vocab] of positions score_from.. of one pass over the
+    whole sequence (the ops of forward(), every projection a dense fp32 product with the
+    dequantised weight; agreement with forward() is to fp32 rounding).
+
+    Greedy decoding that produced `tokens` from the prompt tokens[:score_from + 1] is what
+    this checker would itself have generated exactly when argmax(logits[i]) ==
+    tokens[score_from + 1 + i] for every i: each step's context is then the checker's own."""
+    shapes = proj_shapes(cfg)
+    cos, sin = rope_tables(cfg)
+    tokens = np.asarray(tokens)
+    pos = np.arange(len(tokens))
+    x = weights["embed"][tokens].astype(np.float32)
+    d = cfg.head_dim
+    for li in range(cfg.layers):
+        lw = weights["layers"][li]
+        h = rms_norm(x, lw["norm_attn"], cfg.eps)
+        q = rope(h @ _dense(lw["q"], *shapes["q"], cfg).T, cfg.heads, d, pos, cos, sin)
+        kk = rope(h @ _dense(lw["k"], *shapes["k"], cfg).T, cfg.kv_heads, d, pos, cos, sin)
+        vv = h @ _dense(lw["v"], *shapes["v"], cfg).T
+        x = x + causal_attention(q, kk, vv, cfg) @ _dense(lw["o"], *shapes["o"], cfg).T
+        h = rms_norm(x, lw["norm_mlp"], cfg.eps)
+        gate = h @ _dense(lw["gate"], *shapes["gate"], cfg).T
+        up = h @ _dense(lw["up"], *shapes["up"], cfg).T
+        act = (gate / (np.float32(1.0) + np.exp(-gate)) * up).astype(np.float32)
+        x = x + act @ _dense(lw["down"], *shapes["down"], cfg).T
+    h = rms_norm(x[score_from:], weights["norm_final"], cfg.eps)
+    return h @ _dense(weights["lm_head"], cfg.vocab, cfg.hidden, cfg).T
+
+
+def greedy_check(weights: dict, cfg, prompt: np.ndarray, generated: np.ndarray, return_logits: bool = False) -> dict:
+    """Checks `generated` (greedy tokens after `prompt`) with one teacher-forced pass.
+
+    Returns matches (tokens equal to the checker's argmax), first_mismatch (step or None), and
+    per step the checker's top-2 logit margin (top1 - top2), the smallest margin and the step
+    it falls on (and the checker's logits [steps, vocab] under "logits" when asked)."""
+    seq = np.concatenate([np.asarray(prompt), np.asarray(generated)[:-1]])
+    logits = teacher_forced_logits(weights, cfg, seq, len(prompt) - 1)
+    want = logits.argmax(axis=1)
+    top2 = np.sort(logits, axis=1)[:, -2:]
+    margins = (top2[:, 1] - top2[:, 0]).astype(float)
+    eq = want == np.asarray(generated)
+    bad = np.flatnonzero(~eq)
+    return {"matches": int(eq.sum()), "steps": int(len(eq)),
+            "first_mismatch": int(bad[0]) if len(bad) else None,
+            "margins": margins.tolist(), "min_margin": float(margins.min()),
+            "min_margin_step": int(margins.argmin()), "checker_tokens": want.tolist(),
+            **({"logits": logits} if return_logits else {})}

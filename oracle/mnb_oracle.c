@@ -171,3 +171,33 @@ int mnb_ref_f64(const float* a, const uint8_t* b, const float* scales, int zp_ki
     }
     return 0;
 }
+
+/* The dequantised weight matrix out[n][k] = (q - zp) * scale in fp32, one rounding each,
+ * as DequantBlock4 / DequantBlock8 produce it block by block (MatMulNBitsSimd.cs:40-96);
+ * used by the batched decoder checker, which multiplies whole matrices. */
+int mnb_dequant(const uint8_t* b, const float* scales, int zp_kind, const void* zp, float* out,
+                int N, int K, int bits, int block_size, int nthreads) {
+    if (N <= 0 || K <= 0 || block_size <= 0 || (bits != 4 && bits != 8)) return -1;
+    const int nb = (K + block_size - 1) / block_size;
+    const int blob = (block_size * bits + 7) / 8;
+    const int zp_row_bytes = (nb * bits + 7) / 8;
+    const long b_row_bytes = (long)nb * blob;
+#ifdef _OPENMP
+    if (nthreads > 0) omp_set_num_threads(nthreads);
+#else
+    (void)nthreads;
+#endif
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < N; ++n) {
+        float* row = out + (long)n * K;
+        for (int bk = 0; bk < nb; ++bk) {
+            const float scale = scales[(long)n * nb + bk];
+            const float z = zero_point(zp_kind, zp, n, nb, zp_row_bytes, bk, bits);
+            const long blob_base = (long)n * b_row_bytes + (long)bk * blob;
+            const int ks = bk * block_size;
+            const int ke = ks + block_size < K ? ks + block_size : K;
+            for (int k = ks; k < ke; ++k) row[k] = ((float)unpack_nbit(b, blob_base, k - ks, bits) - z) * scale;
+        }
+    }
+    return 0;
+}

@@ -65,6 +65,9 @@ def _lib():
             f.restype = C.c_int
             f.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
                           C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]
+        L.mnb_dequant.restype = C.c_int
+        L.mnb_dequant.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                  C.c_int, C.c_int, C.c_int]
         _oracle = L
     return _oracle
 
@@ -112,6 +115,17 @@ def _run(fn_name: str, case: dict, threads: int = 0, rows: slice | None = None) 
 
 def managed(case: dict, threads: int = 0, rows: slice | None = None) -> np.ndarray:
     return _run("mnb_ref_managed", case, threads, rows)
+
+
+def dequant(case: dict, threads: int = 0) -> np.ndarray:
+    """The fp32 weight matrix W[N, K] = (q - zp) * scale (mnb_dequant)."""
+    _, b, s, kind, z = _inputs(dict(case, a=np.zeros((1, case["K"]), np.float32)))
+    out = np.empty((case["N"], case["K"]), dtype=np.float32)
+    rc = _lib().mnb_dequant(b.ctypes.data, s.ctypes.data, kind, z.ctypes.data if z is not None else None,
+                            out.ctypes.data, case["N"], case["K"], case["bits"], case["block_size"], threads)
+    if rc != 0:
+        raise ValueError("mnb_dequant rejected the case")
+    return out
 
 
 def f64(case: dict, threads: int = 0, rows: slice | None = None) -> np.ndarray:

@@ -39,3 +39,12 @@ def test_reference_arm_prints_one_contract_line():
 def test_reference_arm_other_ranks_print_nothing():
     env = dict(os.environ, RANK="1", WORLD_SIZE="2", LOCAL_RANK="1")
     assert _run("--impl", "reference", "--steps", "1", "--warmup", "1", "--cpu-seconds", "0", env=env) == []
+
+
+def test_reference_arm_uses_every_host_thread_under_torchrun():
+    """torchrun sets OMP_NUM_THREADS=1 for its workers; the reference arm still times the CPU
+    kernel on all host threads, so a multi-GPU line is not compared with one CPU thread."""
+    env = dict(os.environ, RANK="0", WORLD_SIZE="2", LOCAL_RANK="0", OMP_NUM_THREADS="1")
+    d = json.loads(_run("--impl", "reference", "--steps", "1", "--warmup", "1", "--cpu-seconds", "0", env=env)[0])
+    assert d["cpu_baseline"]["cores"] == os.cpu_count()
+    assert d["scaling"] == "strong"
