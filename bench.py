@@ -969,8 +969,8 @@ DECODE_WORKLOAD = ("synthetic 7B-shaped INT4 decoder (BASELINE configs[4]): 32 l
                    "8 key-value heads of 128, SwiGLU 14336, vocabulary 32000, every projection MatMulNBits bits=4 "
                    "block_size=32 with zero points; greedy decode of 128 tokens after a 512-token prompt of uniform "
                    "random ids; q/k/v and gate/up packed into one MatMulNBits each; fp32 glue: the library's "
-                   "fused decode kernels (add+RMSNorm, rotary+KV append, split-K GQA, SwiGLU, argmax), torch for "
-                   "the prompt pass")
+                   "fused decode kernels (add+RMSNorm, rotary+KV append, split-K GQA, SwiGLU, argmax); the prompt's "
+                   "projections on the split-operand tcgen05 GEMM (MSQ_PATH_GEMM_SPLIT), torch glue for the prompt pass")
 
 
 def decode_checks(host_w, cfg, prompt_h, tokens, args):

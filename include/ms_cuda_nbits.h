@@ -55,6 +55,13 @@ extern "C" {
 #define MSQ_PATH_GENERIC  1  /* any bits / block size / zero-point form, reference layout  */
 #define MSQ_PATH_GEMV     2  /* bits=4, block_size a power of two >= 32                   */
 #define MSQ_PATH_GEMM     3  /* bits=4, block_size a power of two >= 32, tcgen05 + TMEM   */
+/* The tcgen05 GEMM with split operands: weights (q - zp) * s computed in fp32 from the fp32
+ * scales and A (row-scaled) each enter as two fp16 parts, hi = fp16(x) and lo = fp16(x - hi),
+ * three MMAs per k-step (hi.hi + hi.lo + lo.hi) into the fp32 accumulator: products good to
+ * about 2^-22 instead of fp16's 2^-11, for prompts whose greedy decoding must follow the fp32
+ * reference; about a third of MSQ_PATH_GEMM's throughput.                                */
+#define MSQ_PATH_GEMM_SPLIT 4
+#define MSQ_PATH_AUTO_SPLIT 5  /* as MSQ_PATH_AUTO, with MSQ_PATH_GEMM_SPLIT for M >= 17       */
 
 /* ---- msq_pack flags ----------------------------------------------------------------- */
 #define MSQ_PACK_DEFAULT       0

@@ -259,15 +259,16 @@ int matmul_impl(cudaStream_t st, Weights* w, const void* d_a, int a_dtype, int64
   if (dev != w->device)
     return fail(MSQ_E_INVALID, "weights handle lives on device %d but the current device is %d", w->device, dev);
   refresh_settled(*w, st);
-  if (path == MSQ_PATH_AUTO) {
+  if (path == MSQ_PATH_AUTO || path == MSQ_PATH_AUTO_SPLIT) {
     if (!w->fast4) path = MSQ_PATH_GENERIC;
-    else if (M >= 17 && w->K >= 64) path = MSQ_PATH_GEMM;
+    else if (M >= 17 && w->K >= 64) path = path == MSQ_PATH_AUTO ? MSQ_PATH_GEMM : MSQ_PATH_GEMM_SPLIT;
     else path = MSQ_PATH_GEMV;
   }
   switch (path) {
     case MSQ_PATH_GENERIC: return run_generic(st, *w, d_a, a_dtype, M, d_y, ldy);
     case MSQ_PATH_GEMV: return run_gemv(st, *w, d_a, a_dtype, M, d_y, ldy);
     case MSQ_PATH_GEMM: return run_gemm(st, *w, d_a, a_dtype, M, d_y, ldy);
+    case MSQ_PATH_GEMM_SPLIT: return run_gemm(st, *w, d_a, a_dtype, M, d_y, ldy, true);
     default: return fail(MSQ_E_INVALID, "msq_matmul_ex: unknown path %d", path);
   }
 }

@@ -37,20 +37,28 @@ constexpr int BK = 64;
 
 __device__ int g_gemm_err;
 
-template <int TM, int BN>
+// SPLIT: the operands enter the tensor core as two fp16 parts each, hi = fp16(x) and
+// lo = fp16(x - hi), and each k-step issues hi.hi + hi.lo + lo.hi (the lo.lo term is below fp32
+// rounding): products good to ~2^-22 instead of fp16's 2^-11, at three MMAs per step and a
+// second dequantised tile. Weights are (q - zp) * s computed in fp32 from the exact fp32 scales.
+template <int TM, int BN, bool SPLIT = false>
 struct Plan {
+  static constexpr int kParts = SPLIT ? 2 : 1;        // fp16 parts per operand tile (hi, lo)
   static constexpr int kRows = BM * TM;               // activation rows of a tile
   static constexpr int kCols = TM * BN;               // TMEM columns (the TM accumulators)
   static constexpr int kDeq = BN / 16;                // dequant warps: one thread per half row
   static constexpr int kThreads = (kDeq + 2) * 32;    // + TMA warp + MMA warp
   static constexpr int kTmaWarp = kDeq;
   static constexpr int kMmaWarp = kDeq + 1;
-  static constexpr int kStages = TM == 1 ? 4 : TM == 2 ? 3 : 2;  // what fits in 227 KB
-  static constexpr int kABytes = kRows * BK * 2;      // 16 or 32 KB
-  static constexpr int kABoxes = kRows > 256 ? kRows / 256 : 1;  // activation TMA boxes per stage
-  static constexpr int kBBytes = BN * BK * 2;         // dequantised fp16 weights
+  // what fits in 227 KB (SPLIT: TM <= 2)
+  static constexpr int kStages = SPLIT ? (TM == 1 ? 3 : 2) : (TM == 1 ? 4 : TM == 2 ? 3 : 2);
+  static constexpr int kAPart = kRows * BK * 2;       // one fp16 activation tile: 16 / 32 / 64 KB
+  static constexpr int kABytes = kAPart * kParts;     // hi tile, then lo tile
+  static constexpr int kABoxes = kRows > 256 ? kRows / 256 : 1;  // activation TMA boxes per part
+  static constexpr int kBPart = BN * BK * 2;          // one dequantised fp16 weight tile
+  static constexpr int kBBytes = kBPart * kParts;
   static constexpr int kPBytes = BN * BK / 2;         // packed int4 weights
-  static constexpr int kSBytes = BN * 16;             // 8 fp16 scales per row
+  static constexpr int kSBytes = BN * 16;             // 8 fp16 (SPLIT: 4 fp32) scales per row
   static constexpr int kZBytes = BN * 16;             // 32 packed or 4 fp32 zero points per row
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kOffA + kStages * kABytes;
@@ -72,6 +80,8 @@ struct GemmArgs {
   int64_t split_stride;  // with several k-splits: elements between their partial outputs
   const float* row_scale;  // staged A: row m entered the tensor core as a * 2^e_m; Y row m is
                            // multiplied by row_scale[m] = 2^-e_m (exact). nullptr: A as given
+  int a_lo_row;            // SPLIT: row of the activation map where the lo parts start (M), or 0
+                           // when A has no lo part (fp16 A: hi alone is exact)
 };
 
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -82,12 +92,12 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 __device__ __forceinline__ bool wait_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code) {
   if (*abort_flag) return false;
   if (ptx::mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = ptx::globaltimer();
+  const unsigned long long t0 = ptx::globaltimer(), budget = ptx::wait_budget_ns();
   for (uint32_t i = 1;; ++i) {
     if (ptx::mbar_try_wait_sleep(bar, parity)) return true;
     if ((i & 7u) == 0) {
       if (*abort_flag) return false;
-      if (ptx::globaltimer() - t0 > ptx::wait_budget_ns()) {
+      if (ptx::globaltimer() - t0 > budget) {
         *abort_flag = 1;
         atomicCAS(&g_gemm_err, 0, code);
         return false;
@@ -110,12 +120,23 @@ __device__ __forceinline__ uint32_t deq_pair_f32(uint32_t bits, float z, float s
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-template <int TM, int BN, int ZPK>
-__global__ void __launch_bounds__(Plan<TM, BN>::kThreads, 1)
+// A code pair's weights (q - zp) * s in fp32, as fp16 hi parts and fp16 lo = w - hi parts.
+__device__ __forceinline__ void deq_split(uint32_t bits, float z, float s, uint32_t& hi, uint32_t& lo) {
+  const float w0 = ((float)(bits & 0xF) - z) * s;
+  const float w1 = ((float)((bits >> 16) & 0xF) - z) * s;
+  const __half2 h = __floats2half2_rn(w0, w1);
+  const float2 hf = __half22float2(h);
+  const __half2 l = __floats2half2_rn(w0 - hf.x, w1 - hf.y);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+template <int TM, int BN, int ZPK, bool SPLIT>
+__global__ void __launch_bounds__(Plan<TM, BN, SPLIT>::kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmP,
                    const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmZ,
                    const GemmArgs p) {
-  using PL = Plan<TM, BN>;
+  using PL = Plan<TM, BN, SPLIT>;
   constexpr int S = PL::kStages;
   constexpr int kDeqWarps = PL::kDeq;
   constexpr int kTmaWarp = PL::kTmaWarp;
@@ -170,14 +191,21 @@ __global__ void __launch_bounds__(Plan<TM, BN>::kThreads, 1)
         if (i >= S && !wait_abort(&empty[s], (u - 1) & 1, abort_flag, ptx::kErrTimeoutEmpty)) break;
         // scales / zero points: the 16-byte-aligned column holding the stage's block(s)
         const int blk0 = (kt * BK) >> p.bs_shift;
-        ptx::mbar_arrive_expect_tx(&full[s],
-                                   PL::kABytes + PL::kPBytes + PL::kSBytes + (ZPK != ZP_NONE ? PL::kZBytes : 0));
+        const bool lo = SPLIT && p.a_lo_row > 0;
+        ptx::mbar_arrive_expect_tx(&full[s], PL::kAPart * (lo ? 2 : 1) + PL::kPBytes + PL::kSBytes +
+                                                 (ZPK != ZP_NONE ? PL::kZBytes : 0));
 #pragma unroll
         for (int h = 0; h < PL::kABoxes; ++h)  // a box is at most 256 rows
-          ptx::tma_load_2d(smem + PL::kOffA + s * PL::kABytes + h * (PL::kABytes / PL::kABoxes), &tmA, &full[s],
+          ptx::tma_load_2d(smem + PL::kOffA + s * PL::kABytes + h * (PL::kAPart / PL::kABoxes), &tmA, &full[s],
                            kt * BK, m0 + h * (PL::kRows / PL::kABoxes));
+        if (lo) {
+#pragma unroll
+          for (int h = 0; h < PL::kABoxes; ++h)
+            ptx::tma_load_2d(smem + PL::kOffA + s * PL::kABytes + PL::kAPart + h * (PL::kAPart / PL::kABoxes), &tmA,
+                             &full[s], kt * BK, p.a_lo_row + m0 + h * (PL::kRows / PL::kABoxes));
+        }
         ptx::tma_load_2d(smem + PL::kOffP + s * PL::kPBytes, &tmP, &full[s], kt * (BK / 2), n0);
-        ptx::tma_load_2d(smem + PL::kOffS + s * PL::kSBytes, &tmS, &full[s], blk0 & ~7, n0);
+        ptx::tma_load_2d(smem + PL::kOffS + s * PL::kSBytes, &tmS, &full[s], SPLIT ? (blk0 & ~3) : (blk0 & ~7), n0);
         if (ZPK == ZP_PACKED)
           ptx::tma_load_2d(smem + PL::kOffZ + s * PL::kZBytes, &tmZ, &full[s], (blk0 >> 1) & ~15, n0);
         else if (ZPK == ZP_F32)
@@ -186,9 +214,9 @@ __global__ void __launch_bounds__(Plan<TM, BN>::kThreads, 1)
       }
       for (int s = 0; s < S && s < issued; ++s) {  // drain copies in flight
         const int last = s + (issued - 1 - s) / S * S;
-        const unsigned long long t0 = ptx::globaltimer();
+        const unsigned long long t0 = ptx::globaltimer(), budget = ptx::wait_budget_ns();
         while (!ptx::mbar_try_wait(&full[s], (last / S) & 1)) {
-          if (ptx::globaltimer() - t0 > ptx::wait_budget_ns()) {
+          if (ptx::globaltimer() - t0 > budget) {
             atomicCAS(&g_gemm_err, 0, ptx::kErrTimeoutDrain);
             break;
           }
@@ -213,14 +241,27 @@ __global__ void __launch_bounds__(Plan<TM, BN>::kThreads, 1)
 #pragma unroll
           for (int j = 0; j < BK / 16; ++j)
             ptx::mma_f16(tmem + (uint32_t)(t * BN), ad + 2 * j, bd + 2 * j, idesc, (i | j) != 0);
+          if constexpr (SPLIT) {
+            const uint64_t bdl = sw128_desc(ptx::smem_u32(smem + PL::kOffB + s * PL::kBBytes + PL::kBPart));
+#pragma unroll
+            for (int j = 0; j < BK / 16; ++j)
+              ptx::mma_f16(tmem + (uint32_t)(t * BN), ad + 2 * j, bdl + 2 * j, idesc, 1u);
+            if (p.a_lo_row > 0) {
+              const uint64_t adl =
+                  sw128_desc(ptx::smem_u32(smem + PL::kOffA + s * PL::kABytes + PL::kAPart + t * BM * 128));
+#pragma unroll
+              for (int j = 0; j < BK / 16; ++j)
+                ptx::mma_f16(tmem + (uint32_t)(t * BN), adl + 2 * j, bd + 2 * j, idesc, 1u);
+            }
+          }
         }
         ptx::mma_commit(&empty[s]);
       }
       ptx::mma_commit(accum);
       // the accumulator (and every MMA reading shared memory) must be done before exit
-      const unsigned long long t0 = ptx::globaltimer();
+      const unsigned long long t0 = ptx::globaltimer(), budget = ptx::wait_budget_ns();
       while (!ptx::mbar_try_wait(accum, 0)) {
-        if (ptx::globaltimer() - t0 > ptx::wait_budget_ns()) {
+        if (ptx::globaltimer() - t0 > budget) {
           atomicCAS(&g_gemm_err, 0, ptx::kErrTimeoutMma);
           break;
         }
@@ -241,8 +282,10 @@ __global__ void __launch_bounds__(Plan<TM, BN>::kThreads, 1)
         const uint4 w4 = *reinterpret_cast<const uint4*>(smem + PL::kOffP + s * PL::kPBytes + tid * 16);
         const int blk0 = (kt * BK) >> p.bs_shift;
         const int blk = (kt * BK + c * 32) >> p.bs_shift;
-        const float sf = __half2float(
-            reinterpret_cast<const __half*>(smem + PL::kOffS + s * PL::kSBytes + r * 16)[blk - (blk0 & ~7)]);
+        const float sf =
+            SPLIT ? reinterpret_cast<const float*>(smem + PL::kOffS + s * PL::kSBytes + r * 16)[blk - (blk0 & ~3)]
+                  : __half2float(
+                        reinterpret_cast<const __half*>(smem + PL::kOffS + s * PL::kSBytes + r * 16)[blk - (blk0 & ~7)]);
         float zf = 8.f;
         if (ZPK == ZP_PACKED) {
           const uint8_t zb = (smem + PL::kOffZ + s * PL::kZBytes + r * 16)[(blk >> 1) - ((blk0 >> 1) & ~15)];
@@ -257,6 +300,17 @@ __global__ void __launch_bounds__(Plan<TM, BN>::kThreads, 1)
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const uint32_t x = words[j];
+          const int wi = 4 * c + j;  // 8-k group of the row
+          if constexpr (SPLIT) {
+            uint4 oh, ol;
+            deq_split(x, zf, sf, oh.x, ol.x);
+            deq_split(x >> 4, zf, sf, oh.y, ol.y);
+            deq_split(x >> 8, zf, sf, oh.z, ol.z);
+            deq_split(x >> 12, zf, sf, oh.w, ol.w);
+            *reinterpret_cast<uint4*>(brow + ((wi ^ (r & 7)) << 4)) = oh;
+            *reinterpret_cast<uint4*>(brow + PL::kBPart + ((wi ^ (r & 7)) << 4)) = ol;
+            continue;
+          }
           uint4 o;
           if (ZPK == ZP_F32) {
             o.x = deq_pair_f32(x, zf, sf);
@@ -269,7 +323,6 @@ __global__ void __launch_bounds__(Plan<TM, BN>::kThreads, 1)
             o.z = deq_pair(x >> 8, zc, s2);
             o.w = deq_pair(x >> 12, zc, s2);
           }
-          const int wi = 4 * c + j;  // 8-k group of the row
           *reinterpret_cast<uint4*>(brow + ((wi ^ (r & 7)) << 4)) = o;
         }
       }
@@ -330,8 +383,9 @@ __global__ void __launch_bounds__(Plan<TM, BN>::kThreads, 1)
 // largest finite magnitude (that maximum lands in [2^14, 2^15)) before the rounding, and
 // row_scale[m] = 2^-e undoes it exactly in the GEMM's epilogue. Infinities and NaNs pass
 // through unchanged, so they propagate through the tensor core as in the fp32 reference.
+// With out_lo (the split GEMM), also the fp16 remainder lo = fp16(a 2^e - hi) of every element.
 __global__ void to_half_rows_kernel(const void* __restrict__ a, int dt, int64_t M, int K, __half* __restrict__ out,
-                                    int64_t lda, float* __restrict__ row_scale) {
+                                    int64_t lda, float* __restrict__ row_scale, __half* __restrict__ out_lo) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   for (int64_t m = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); m < M; m += warps) {
@@ -349,7 +403,12 @@ __global__ void to_half_rows_kernel(const void* __restrict__ a, int dt, int64_t 
       e = max(-120, min(120, 15 - ex));  // mx 2^e in [2^14, 2^15)
     }
     const float up = ldexpf(1.f, e);
-    for (int k = lane; k < K; k += 32) out[m * lda + k] = __float2half_rn(load_act(a, dt, base + k) * up);
+    for (int k = lane; k < K; k += 32) {
+      const float v = load_act(a, dt, base + k) * up;
+      const __half h = __float2half_rn(v);
+      out[m * lda + k] = h;
+      if (out_lo) out_lo[m * lda + k] = __float2half_rn(v - __half2float(h));
+    }
     if (lane == 0) row_scale[m] = ldexpf(1.f, -e);
   }
 }
@@ -408,32 +467,35 @@ struct WeightMaps {
 };
 
 struct GemmState {
-  WeightMaps m128;
+  WeightMaps m128;   // fp16 scales (the fast path)
+  WeightMaps m128s;  // fp32 scales (the split path)
 };
 
-template <int TM, int BN, int ZPK>
+template <int TM, int BN, int ZPK, bool SPLIT>
 int launch(cudaStream_t st, const CUtensorMap& tmA, const WeightMaps& wm, const GemmArgs& a, dim3 grid) {
-  auto kern = gemm_tc_kernel<TM, BN, ZPK>;
+  using PL = Plan<TM, BN, SPLIT>;
+  static_assert(PL::kSmem <= 227 * 1024, "GEMM plan exceeds the 227 KB of shared memory a CTA may use");
+  auto kern = gemm_tc_kernel<TM, BN, ZPK, SPLIT>;
   static ContextOnce configured;
   int rc = configured.run([&] {
-    MSQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Plan<TM, BN>::kSmem),
+    MSQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PL::kSmem),
                  "gemm smem attribute");
     return MSQ_OK;
   });
   if (rc != MSQ_OK) return rc;
-  kern<<<grid, Plan<TM, BN>::kThreads, Plan<TM, BN>::kSmem, st>>>(tmA, wm.p, wm.s, wm.z, a);
+  kern<<<grid, PL::kThreads, PL::kSmem, st>>>(tmA, wm.p, wm.s, wm.z, a);
   note_launch();
   MSQ_CUDA_TRY(cudaGetLastError(), "gemm launch");
   return MSQ_OK;
 }
 
-template <int TM, int BN>
+template <int TM, int BN, bool SPLIT = false>
 int launch_zp(cudaStream_t st, int zp_kind, const CUtensorMap& tmA, const WeightMaps& wm, const GemmArgs& a,
               dim3 grid) {
   switch (zp_kind) {
-    case ZP_PACKED: return launch<TM, BN, ZP_PACKED>(st, tmA, wm, a, grid);
-    case ZP_F32: return launch<TM, BN, ZP_F32>(st, tmA, wm, a, grid);
-    default: return launch<TM, BN, ZP_NONE>(st, tmA, wm, a, grid);
+    case ZP_PACKED: return launch<TM, BN, ZP_PACKED, SPLIT>(st, tmA, wm, a, grid);
+    case ZP_F32: return launch<TM, BN, ZP_F32, SPLIT>(st, tmA, wm, a, grid);
+    default: return launch<TM, BN, ZP_NONE, SPLIT>(st, tmA, wm, a, grid);
   }
 }
 
@@ -469,18 +531,22 @@ int choose_splits(int ctas, int sms, int ksteps, int64_t M, int64_t ldw) {
 // 256 x 128 for M > 128, else 128 x 128. When the tiles leave SMs idle and `allow_split`,
 // K is split across CTAs whose partial tiles go to stream-ordered scratch and are summed in a
 // fixed order into Y (deterministic).
+// operand_split: the split (hi/lo) GEMM; a_lo: A has lo rows after its M hi rows.
 int launch_gemm(cudaStream_t st, const Weights& w, const WeightMaps& m128, const void* a16, int64_t lda,
-                const float* row_scale, int64_t M, float* d_y, int64_t ldy, bool allow_split) {
-  const int tm = M >= 4 * BM ? 4 : M > BM ? 2 : 1;
+                const float* row_scale, int64_t M, float* d_y, int64_t ldy, bool allow_split,
+                bool operand_split = false, bool a_lo = false) {
+  const int tm = M >= 4 * BM && !operand_split ? 4 : M > BM ? 2 : 1;
   const int rows = tm * BM;
   CUtensorMap tmA;
-  int rc = make_map_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, const_cast<void*>(a16), (uint64_t)w.K, (uint64_t)M,
-                       (uint64_t)lda * 2, BK, std::min(rows, 256), CU_TENSOR_MAP_SWIZZLE_128B);
+  int rc = make_map_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, const_cast<void*>(a16), (uint64_t)w.K,
+                       (uint64_t)M * (a_lo ? 2 : 1), (uint64_t)lda * 2, BK, std::min(rows, 256),
+                       CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != MSQ_OK) return rc;
   GemmArgs g{};
   g.y = d_y;
   g.ldy = ldy;
   g.row_scale = row_scale;
+  g.a_lo_row = a_lo ? (int)M : 0;
   g.M = (int)M;
   g.n_rows = w.n_rows;
   g.K = w.K;
@@ -502,9 +568,13 @@ int launch_gemm(cudaStream_t st, const Weights& w, const WeightMaps& m128, const
   }
   g.vec_store = (g.ldy % 4 == 0) && ((reinterpret_cast<uintptr_t>(g.y) & 15) == 0);
   const dim3 grid(gx, gy, splits);
-  rc = tm == 4   ? launch_zp<4, 128>(st, w.zp_kind, tmA, m128, g, grid)
-       : tm == 2 ? launch_zp<2, 128>(st, w.zp_kind, tmA, m128, g, grid)
-                 : launch_zp<1, 128>(st, w.zp_kind, tmA, m128, g, grid);
+  if (operand_split)
+    rc = tm == 2 ? launch_zp<2, 128, true>(st, w.zp_kind, tmA, m128, g, grid)
+                 : launch_zp<1, 128, true>(st, w.zp_kind, tmA, m128, g, grid);
+  else
+    rc = tm == 4   ? launch_zp<4, 128>(st, w.zp_kind, tmA, m128, g, grid)
+         : tm == 2 ? launch_zp<2, 128>(st, w.zp_kind, tmA, m128, g, grid)
+                   : launch_zp<1, 128>(st, w.zp_kind, tmA, m128, g, grid);
   if (rc == MSQ_OK && splits > 1) {
     const int64_t total = M * w.n_rows;
     const int blocks = (int)std::min<int64_t>((total + 255) / 256, 8 * (int64_t)num_sms(w.device));
@@ -516,20 +586,25 @@ int launch_gemm(cudaStream_t st, const Weights& w, const WeightMaps& m128, const
   }
   scratch_free(ws, st);
   if (rc == MSQ_OK) {
-    if (splits > 1)
-      note_path(tm == 4 ? "gemm_tc_m512_n128_splitk" : tm == 2 ? "gemm_tc_m256_n128_splitk" : "gemm_tc_m128_n128_splitk");
-    else
-      note_path(tm == 4 ? "gemm_tc_m512_n128" : tm == 2 ? "gemm_tc_m256_n128" : "gemm_tc_m128_n128");
+    static const char* names[2][2][3] = {
+        {{"gemm_tc_m128_n128", "gemm_tc_m256_n128", "gemm_tc_m512_n128"},
+         {"gemm_tc_m128_n128_splitk", "gemm_tc_m256_n128_splitk", "gemm_tc_m512_n128_splitk"}},
+        {{"gemm_tc_x3_m128_n128", "gemm_tc_x3_m256_n128", "gemm_tc_x3_m512_n128"},
+         {"gemm_tc_x3_m128_n128_splitk", "gemm_tc_x3_m256_n128_splitk", "gemm_tc_x3_m512_n128_splitk"}}};
+    note_path(names[operand_split ? 1 : 0][splits > 1 ? 1 : 0][tm == 4 ? 2 : tm == 2 ? 1 : 0]);
   }
   return rc;
 }
 
 // Codes [n_rows][KP/2] in boxes of 32 bytes x BN rows; scales [n_rows][sc_pitch] fp16 and zero
 // points (packed [n_rows][zp_pitch] bytes or fp32 [n_rows][sc_pitch]) in 16-byte x BN boxes.
-int make_maps(const Weights& w, int bn, WeightMaps* m) {
+int make_maps(const Weights& w, int bn, WeightMaps* m, bool f32_scales = false) {
   int rc = make_map_2d(&m->p, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.nib, (uint64_t)w.nib_pitch, (uint64_t)w.n_rows,
                        (uint64_t)w.nib_pitch, BK / 2, bn, CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (rc == MSQ_OK)
+  if (rc == MSQ_OK && f32_scales)
+    rc = make_map_2d(&m->s, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w.sc, (uint64_t)w.sc_pitch, (uint64_t)w.n_rows,
+                     (uint64_t)w.sc_pitch * 4, 4, bn, CU_TENSOR_MAP_SWIZZLE_NONE);
+  else if (rc == MSQ_OK)
     rc = make_map_2d(&m->s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, w.sc16, (uint64_t)w.sc_pitch, (uint64_t)w.n_rows,
                      (uint64_t)w.sc_pitch * 2, 8, bn, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc != MSQ_OK) return rc;
@@ -543,8 +618,8 @@ int make_maps(const Weights& w, int bn, WeightMaps* m) {
   return MSQ_OK;
 }
 
-int make_weight_maps(const Weights& w, WeightMaps* m128) {
-  return make_maps(w, 128, m128);
+int make_weight_maps(const Weights& w, WeightMaps* m128, bool f32_scales = false) {
+  return make_maps(w, 128, m128, f32_scales);
 }
 
 // fp16 activations with 16-byte rows feed TMA directly; anything else is staged as fp16.
@@ -552,19 +627,24 @@ bool needs_staging(const Weights& w, const void* d_a, int a_dtype) {
   return a_dtype != MSQ_DT_F16 || (w.K % 8) != 0 || (reinterpret_cast<uintptr_t>(d_a) & 15) != 0;
 }
 
-// Staged A: fp16 rows [M][staged_lda] (16-byte rows for TMA), then M fp32 row scales at a
-// 256-byte-aligned offset.
+// Staged A: fp16 rows [M][staged_lda] (16-byte rows for TMA) -- for the split GEMM the hi rows
+// and then the lo rows, [2M][staged_lda] -- then M fp32 row scales at a 256-byte-aligned offset.
 int64_t staged_lda(const Weights& w) { return (w.K + 7) / 8 * 8; }
-size_t staged_scale_offset(const Weights& w, int64_t M) {
-  return (sizeof(__half) * (size_t)M * (size_t)staged_lda(w) + 255) / 256 * 256;
+size_t staged_scale_offset(const Weights& w, int64_t M, int parts = 1) {
+  return (sizeof(__half) * (size_t)parts * (size_t)M * (size_t)staged_lda(w) + 255) / 256 * 256;
+}
+size_t staging_bytes(const Weights& w, const void* d_a, int a_dtype, int64_t M, int parts) {
+  if (M <= 0 || !needs_staging(w, d_a, a_dtype)) return 0;
+  return staged_scale_offset(w, M, parts) + sizeof(float) * (size_t)M;
 }
 
 int stage_rows(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M, void* staging,
-               const float** row_scale) {
-  float* rs = reinterpret_cast<float*>(static_cast<uint8_t*>(staging) + staged_scale_offset(w, M));
+               const float** row_scale, int parts = 1) {
+  float* rs = reinterpret_cast<float*>(static_cast<uint8_t*>(staging) + staged_scale_offset(w, M, parts));
   const int64_t blocks = std::min<int64_t>((M + 7) / 8, 16 * (int64_t)num_sms(w.device));
-  to_half_rows_kernel<<<(unsigned)blocks, 256, 0, st>>>(d_a, a_dtype, M, w.K, static_cast<__half*>(staging),
-                                                        staged_lda(w), rs);
+  __half* hi = static_cast<__half*>(staging);
+  to_half_rows_kernel<<<(unsigned)blocks, 256, 0, st>>>(d_a, a_dtype, M, w.K, hi, staged_lda(w), rs,
+                                                        parts == 2 ? hi + M * staged_lda(w) : nullptr);
   note_launch();
   MSQ_CUDA_TRY(cudaGetLastError(), "staging launch");
   *row_scale = rs;
@@ -573,7 +653,8 @@ int stage_rows(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, 
 
 }  // namespace
 
-int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t M, float* d_y, int64_t ldy) {
+int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t M, float* d_y, int64_t ldy,
+             bool operand_split) {
   if (!w.fast4) return fail(MSQ_E_UNSUPPORTED, "GEMM path needs bits=4 and a power-of-two block_size >= 32");
   if (M <= 0) return MSQ_OK;
   if (M > 0x7fffffff) return fail(MSQ_E_INVALID, "GEMM: M too large");
@@ -586,6 +667,7 @@ int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t 
     if (!gs) {
       gs = new GemmState();
       int rc = make_weight_maps(w, &gs->m128);
+      if (rc == MSQ_OK) rc = make_weight_maps(w, &gs->m128s, true);
       if (rc != MSQ_OK) {
         delete gs;
         return rc;
@@ -597,26 +679,27 @@ int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t 
   int64_t lda = w.K;
   void* scratch = nullptr;
   const float* row_scale = nullptr;
-  const size_t need = gemm_staging_bytes(w, d_a, a_dtype, M);
+  const int parts = operand_split ? 2 : 1;
+  const size_t need = staging_bytes(w, d_a, a_dtype, M, parts);
   if (need) {
     const int arc = scratch_alloc(&scratch, need, st);
     if (arc != MSQ_OK) return arc;
     lda = staged_lda(w);
-    const int src = stage_rows(st, w, d_a, a_dtype, M, scratch, &row_scale);
+    const int src = stage_rows(st, w, d_a, a_dtype, M, scratch, &row_scale, parts);
     if (src != MSQ_OK) {
       scratch_free(scratch, st);
       return src;
     }
     a16 = scratch;
   }
-  const int rc = launch_gemm(st, w, gs->m128, a16, lda, row_scale, M, d_y, ldy, true);
+  const int rc = launch_gemm(st, w, operand_split ? gs->m128s : gs->m128, a16, lda, row_scale, M, d_y, ldy, true,
+                             operand_split, operand_split && need != 0);
   scratch_free(scratch, st);
   return rc;
 }
 
 size_t gemm_staging_bytes(const Weights& w, const void* d_a, int a_dtype, int64_t M) {
-  if (M <= 0 || !needs_staging(w, d_a, a_dtype)) return 0;
-  return staged_scale_offset(w, M) + sizeof(float) * (size_t)M;
+  return staging_bytes(w, d_a, a_dtype, M, 1);
 }
 
 int run_gemm_staged(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M, float* d_y,

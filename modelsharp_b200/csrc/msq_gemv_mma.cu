@@ -82,12 +82,12 @@ __device__ __forceinline__ bool wait_arrivals(const unsigned long long* arr, con
                                               int nranks) {
   const unsigned long long target =
       *reinterpret_cast<const volatile unsigned long long*>(prod) * (unsigned long long)nranks;
-  const unsigned long long t0 = ptx::globaltimer();
+  const unsigned long long t0 = ptx::globaltimer(), budget = ptx::wait_budget_ns();
   for (;;) {
     unsigned long long v;
     asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(arr) : "memory");
     if (v >= target) return true;
-    if (ptx::globaltimer() - t0 > ptx::wait_budget_ns()) {
+    if (ptx::globaltimer() - t0 > budget) {
       atomicCAS(&g_mma_err, 0, kErrTimeoutPeer);
       return false;
     }
@@ -98,12 +98,12 @@ __device__ __forceinline__ bool wait_arrivals(const unsigned long long* arr, con
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int code) {
   if (*abort_flag) return false;
   if (ptx::mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = ptx::globaltimer();
+  const unsigned long long t0 = ptx::globaltimer(), budget = ptx::wait_budget_ns();
   for (uint32_t i = 1;; ++i) {
     if (ptx::mbar_try_wait_sleep(bar, parity)) return true;
     if ((i & 7u) == 0) {
       if (*abort_flag) return false;
-      if (ptx::globaltimer() - t0 > ptx::wait_budget_ns()) {
+      if (ptx::globaltimer() - t0 > budget) {
         *abort_flag = 1;
         atomicCAS(&g_mma_err, 0, code);
         return false;
@@ -305,9 +305,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
         }
       for (int q = 0; q < p.nslots && q < issued; ++q) {  // in-flight copies must land before exit
         const int last = q + (issued - 1 - q) / p.nslots * p.nslots;
-        const unsigned long long t0 = ptx::globaltimer();
+        const unsigned long long t0 = ptx::globaltimer(), budget = ptx::wait_budget_ns();
         while (!ptx::mbar_try_wait(&full[q], (last / p.nslots) & 1)) {
-          if (ptx::globaltimer() - t0 > ptx::wait_budget_ns()) {
+          if (ptx::globaltimer() - t0 > budget) {
             atomicCAS(&g_mma_err, 0, ptx::kErrTimeoutDrain);
             break;
           }

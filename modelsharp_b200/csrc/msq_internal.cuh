@@ -152,8 +152,9 @@ struct Fusion {
 };
 int run_gemv_fused(cudaStream_t st, const Weights& w, const float* d_a, int64_t M, float* d_y, int64_t ldy,
                    const Fusion& f);
+// operand_split: the split-operand (three fp16 MMAs per step) form of the GEMM.
 int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t M,
-             float* d_y, int64_t ldy);
+             float* d_y, int64_t ldy, bool operand_split = false);
 void release_gemm_state(Weights& w);
 // Bytes of fp16 activation staging the GEMM needs for this call (0 when A feeds TMA as is).
 size_t gemm_staging_bytes(const Weights& w, const void* d_a, int a_dtype, int64_t M);

@@ -16,9 +16,9 @@ constexpr unsigned long long kDefaultWaitBudgetNs = 2000000000ull;  // 2 s
 // module, with its own copy of this word per CUDA context); the host sets it through
 // msq_set_wait_budget, so a test can make a wait run out in milliseconds.
 static __device__ unsigned long long g_wait_budget_ns = kDefaultWaitBudgetNs;
-__device__ __forceinline__ unsigned long long wait_budget_ns() {
-  return *reinterpret_cast<volatile unsigned long long*>(&g_wait_budget_ns);
-}
+// A plain load: waits read it once, on entering their slow path, and first compare against it
+// after several polls, so the load's latency hides behind the wait.
+__device__ __forceinline__ unsigned long long wait_budget_ns() { return g_wait_budget_ns; }
 
 // Error codes written into a kernel's device error word.
 constexpr int kErrTimeoutFull = 1;   // consumer gave up waiting for data
@@ -83,10 +83,10 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 // Waits for the phase with the given parity to complete; false (and *err set) on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer();
+  const unsigned long long t0 = globaltimer(), budget = wait_budget_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait_sleep(bar, parity)) return true;
-    if ((i & 7u) == 0 && globaltimer() - t0 > wait_budget_ns()) {
+    if ((i & 7u) == 0 && globaltimer() - t0 > budget) {
       if (err) atomicCAS(err, 0, code);
       return false;
     }

@@ -164,8 +164,12 @@ class CudaDecoder:
         out = torch.matmul(p, self.vc[li].unsqueeze(1))                          # [Hkv, G, S, d]
         return out.permute(2, 0, 1, 3).reshape(s, cfg.heads * d)
 
-    def prefill(self, tokens: torch.Tensor, path: int = N.PATH_AUTO) -> torch.Tensor:
-        """Runs the prompt from position 0; returns the last position's logits [vocab]."""
+    def prefill(self, tokens: torch.Tensor, path: int = N.PATH_AUTO_SPLIT) -> torch.Tensor:
+        """Runs the prompt from position 0; returns the last position's logits [vocab]. The
+        default route puts the prompt's projections on the split-operand tcgen05 GEMM (products
+        good to ~2^-22): the greedy tokens that follow must be the fp32 reference's, and this
+        decoder amplifies a projection's error about a hundredfold through its 32 layers, which
+        the fp16 GEMM's 2^-11 operands (PATH_AUTO) do not survive."""
         cfg = self.cfg
         s = tokens.shape[0]
         cos, sin = self.cos[:s], self.sin[:s]
@@ -216,7 +220,7 @@ class CudaDecoder:
         ok(lib.msq_argmax(None, st, self.blogits.data_ptr(), cfg.vocab, tok.data_ptr(), pos.data_ptr()), "msq_argmax")
         return self.blogits[0]
 
-    def generate(self, prompt: torch.Tensor, n_new: int, path: int = N.PATH_AUTO) -> torch.Tensor:
+    def generate(self, prompt: torch.Tensor, n_new: int, path: int = N.PATH_AUTO_SPLIT) -> torch.Tensor:
         """Greedy: the prompt in one pass, then n_new - 1 decode steps; the new tokens [n_new]."""
         logits = self.prefill(prompt, path)
         tok = torch.argmax(logits).view(1)
@@ -313,7 +317,7 @@ class EngineDecoder:
     folds the norms, SwiGLU and residual adds into MatMulNBitsFused nodes."""
 
     def __init__(self, cfg: DecoderConfig, weights: dict, device: torch.device | str, fuse: bool = True,
-                 path: int = N.PATH_AUTO):
+                 path: int = N.PATH_AUTO_SPLIT):
         from .engine import CudaEngine
         from .graph_fusion import fuse_decode_graph
         from .llm_ops import create_decoder_registry

@@ -19,11 +19,21 @@ class UnsupportedOperatorException(ModelSharpException):
 
 
 class CudaEngine:
-    def __init__(self, graph: ModelGraph, kernels: KernelRegistry | None = None, device=None):
+    """preload=True packs every MatMulNBits node's weight initializers on the device when the
+    engine is built (load time) instead of on the node's first run."""
+
+    def __init__(self, graph: ModelGraph, kernels: KernelRegistry | None = None, device=None,
+                 preload: bool = False):
         if graph is None:
             raise ValueError("graph")
         self.graph = graph
         self.kernels = kernels or KernelRegistry.create_default(device)
+        self.preloaded = 0
+        if preload:
+            from .onnx_loader import preload_matmulnbits
+            ok, k = self.kernels.try_get("MatMulNBits")
+            if ok and hasattr(k, "preload"):
+                self.preloaded = preload_matmulnbits(graph, k, device)
 
     def run(self, feeds: dict) -> dict:
         env = dict(self.graph.initializers)

@@ -75,6 +75,35 @@ class GraphContext:
 class IKernel(Protocol):
     op_type: str
 
+    def preload(self, node: GraphNode, initializers: dict, device=None) -> int:
+        """Load-time residency: validates the node and packs its B / scales / zero-point
+        initializers on `device` now, so runs only move A and Y (IlgpuEngine.cs:3392-3429 keeps
+        quantized initializers resident by name the same way). Returns 1 when it packed, 0 when
+        that initializer triple was already resident."""
+        names = node.inputs[1:4]
+        b_raw, s_raw = initializers[names[0]], initializers[names[1]]
+        zp_raw = initializers[names[2]] if len(names) > 2 and names[2] else None
+        b = as_torch(b_raw)
+        if b.dtype != torch.uint8:
+            raise ModelSharpException(f"Tensor dtype is {_et_name(b)}; expected UInt8.")
+        N_, K = _attr_int(node, "N", 0), _attr_int(node, "K", 0)
+        bits, bs = _attr_int(node, "bits", 4), _attr_int(node, "block_size", 0)
+        s_t, z_t = as_torch(s_raw), as_torch(zp_raw) if zp_raw is not None else None
+        rc = N.lib().msq_check_node(N_, K, bits, bs, b.numel(), s_t.numel(),
+                                    dtype_code(z_t) if z_t is not None else N.DT_ABSENT,
+                                    z_t.numel() if z_t is not None else 0, None, 0,
+                                    np.asarray([K], np.int64).ctypes.data, 1, None)
+        N.check(rc, "MatMulNBits validation")
+        dev = torch.device(device) if device is not None else (
+            self.device or torch.device("cuda", torch.cuda.current_device()))
+        key = (id(b_raw), id(s_raw), id(zp_raw) if zp_raw is not None else None, N_, K, bits, bs, str(dev))
+        with self._lock:
+            if key in self._cache:
+                return 0
+        self._weights(b_raw, s_raw, zp_raw, N_, K, bits, bs, dev)
+        self.preloaded[tuple(names) + (str(dev),)] = key
+        return 1
+
     def execute(self, node: GraphNode, ctx: GraphContext) -> None: ...
 
 
@@ -120,6 +149,7 @@ class CudaMatMulNBitsKernel:
         self._cache: dict[tuple, QuantizedWeights] = {}
         self._lock = threading.Lock()
         self.calls = 0  # diagnostics, like NativeCuda.CtxCalls (NativeCuda.cs:147)
+        self.preloaded: dict[tuple, tuple] = {}  # (B, scales, zp initializer names, device) -> cache key
 
     def _weights(self, b, scales, zp, N_, K, bits, bs, dev) -> QuantizedWeights:
         key = (id(b), id(scales), id(zp) if zp is not None else None, N_, K, bits, bs, str(dev))
@@ -131,6 +161,35 @@ class CudaMatMulNBitsKernel:
                 w._sources = (b, scales, zp)
                 self._cache[key] = w
             return w
+
+    def preload(self, node: GraphNode, initializers: dict, device=None) -> int:
+        """Load-time residency: validates the node and packs its B / scales / zero-point
+        initializers on `device` now, so runs only move A and Y (IlgpuEngine.cs:3392-3429 keeps
+        quantized initializers resident by name the same way). Returns 1 when it packed, 0 when
+        that initializer triple was already resident."""
+        names = node.inputs[1:4]
+        b_raw, s_raw = initializers[names[0]], initializers[names[1]]
+        zp_raw = initializers[names[2]] if len(names) > 2 and names[2] else None
+        b = as_torch(b_raw)
+        if b.dtype != torch.uint8:
+            raise ModelSharpException(f"Tensor dtype is {_et_name(b)}; expected UInt8.")
+        N_, K = _attr_int(node, "N", 0), _attr_int(node, "K", 0)
+        bits, bs = _attr_int(node, "bits", 4), _attr_int(node, "block_size", 0)
+        s_t, z_t = as_torch(s_raw), as_torch(zp_raw) if zp_raw is not None else None
+        rc = N.lib().msq_check_node(N_, K, bits, bs, b.numel(), s_t.numel(),
+                                    dtype_code(z_t) if z_t is not None else N.DT_ABSENT,
+                                    z_t.numel() if z_t is not None else 0, None, 0,
+                                    np.asarray([K], np.int64).ctypes.data, 1, None)
+        N.check(rc, "MatMulNBits validation")
+        dev = torch.device(device) if device is not None else (
+            self.device or torch.device("cuda", torch.cuda.current_device()))
+        key = (id(b_raw), id(s_raw), id(zp_raw) if zp_raw is not None else None, N_, K, bits, bs, str(dev))
+        with self._lock:
+            if key in self._cache:
+                return 0
+        self._weights(b_raw, s_raw, zp_raw, N_, K, bits, bs, dev)
+        self.preloaded[tuple(names) + (str(dev),)] = key
+        return 1
 
     def execute(self, node: GraphNode, ctx: GraphContext) -> None:
         a = ctx.get(node.inputs[0])

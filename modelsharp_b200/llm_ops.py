@@ -308,7 +308,7 @@ class MatMulNBitsFusedKernel(CudaMatMulNBitsKernel):
         ctx.set(node.outputs[0], out)
 
 
-def create_decoder_registry(device=None, path: int = N.PATH_AUTO) -> KernelRegistry:
+def create_decoder_registry(device=None, path: int = N.PATH_AUTO_SPLIT) -> KernelRegistry:
     """The CUDA registry with MatMulNBits (plain and fused) and the decoder graph's other op
     types. `path` pins the MatMulNBits route (PATH_GEMV: the exact decode GEMV for every M)."""
     reg = KernelRegistry().register(CudaMatMulNBitsKernel(device, path)).register(MatMulNBitsFusedKernel(device, path))

@@ -113,3 +113,40 @@ def test_gemm_bf16_and_unaligned_half(cuda_device):
     refb = oracle.managed(dict(c, a=ab.float().numpy()))
     yb = w.matmul(ab.to(cuda_device), path=N.PATH_GEMM).cpu().numpy()
     assert oracle.rel_l2(yb, refb) <= TOL_TC
+
+
+TOL_SPLIT = 1e-5  # the split-operand GEMM: ~2^-22 products, the fp32-accumulate bar
+
+
+@pytest.mark.parametrize("M,N_,K,bs,zp,adt", [
+    (17, 256, 256, 32, "packed", "f32"),
+    (64, 1000, 4160, 128, "packed", "f32"),   # ragged N tile and last k-stage
+    (130, 512, 1024, 32, "none", "f32"),      # 256-row tiles, ragged M
+    (200, 384, 2048, 64, "float", "f32"),
+    (300, 4096, 4096, 32, "packed", "f16"),   # fp16 A: no lo part (exact), 2 MMAs per step
+    (40, 640, 1000, 32, "packed", "bf16"),    # K % 8 != 0: staged
+    (512, 6144, 4096, 32, "packed", "f32"),   # the 7B prompt's q/k/v shape
+])
+def test_gemm_split_operands_parity(cuda_device, M, N_, K, bs, zp, adt):
+    c = synth.make_case(37, M, N_, K, 4, bs, zp, scale_lo=0.001, scale_hi=0.01)
+    a = c["a"]
+    if adt == "f16":
+        a = a.astype(np.float16)
+    elif adt == "bf16":
+        a = torch.from_numpy(a).to(torch.bfloat16).float().numpy()
+    ref = oracle.managed(dict(c, a=np.asarray(a, np.float32)))
+    w = QuantizedWeights(c["b"], c["scales"], c["zp"], N_, K, 4, bs, device=cuda_device)
+    at = torch.from_numpy(np.ascontiguousarray(a)).to(cuda_device)
+    if adt == "bf16":
+        at = at.to(torch.bfloat16)
+    y = w.matmul(at, path=N.PATH_GEMM_SPLIT)
+    torch.cuda.synchronize()
+    assert N.last_path().startswith("gemm_tc_x3")
+    assert N.lib().msq_device_status(None, None) == N.MSQ_OK, N.last_error()
+    err = oracle.rel_l2(y.cpu().numpy(), ref)
+    assert err <= TOL_SPLIT, err
+    # the fast GEMM on the same inputs is the fp16 one (a bar 500x wider)
+    assert oracle.rel_l2(w.matmul(at, path=N.PATH_GEMM).cpu().numpy(), ref) <= TOL_TC
+    y2 = w.matmul(at, path=N.PATH_AUTO_SPLIT)
+    assert torch.equal(y, y2)
+    w.free()
