@@ -819,10 +819,12 @@ def run_prefill(args, rank: int, world: int, local_rank: int):
     stream = torch.cuda.Stream(dev)
     sptr = stream.cuda_stream
 
+    gpath = N.PATH_GEMM_SPLIT if getattr(args, "split", False) else N.PATH_GEMM
+
     def launch_step(r: int):
         for a, y in zip(a_dev, y_dev):
             rc = lib.msq_matmul_ex(None, sptr, reps[r].handle, a.data_ptr(), N.DT_F16, a.shape[0], y.data_ptr(),
-                                   PREFILL_N, N.PATH_GEMM)
+                                   PREFILL_N, gpath)
             if rc:
                 N.check(rc)
 
@@ -850,7 +852,7 @@ def run_prefill(args, rank: int, world: int, local_rank: int):
         with torch.cuda.graph(g, stream=stream):
             for r in range(reps_n):
                 lib.msq_matmul_ex(None, sptr, reps[r].handle, a.data_ptr(), N.DT_F16, a.shape[0], y.data_ptr(),
-                                  PREFILL_N, N.PATH_GEMM)
+                                  PREFILL_N, gpath)
         with torch.cuda.stream(stream):
             g.replay()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -938,7 +940,8 @@ def run_prefill(args, rank: int, world: int, local_rank: int):
                    "kind": "reference" if oracle.reference_available() else "port",
                    "sample": f"{n} calls of M=64 rows of the M=512 case (fp16 widened to fp32), mean, all host threads"}
         out = {
-            "metric": "MatMulNBits INT4 prefill TFLOPS", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "metric": "MatMulNBits INT4 prefill TFLOPS" + (" (split operands)" if gpath == N.PATH_GEMM_SPLIT else ""),
+            "value": value, "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16 operands, f32 accumulate", "data": "synthetic",
             "config": {"workload": PREFILL_WORKLOAD, "flops_per_step": flops, "parallelism": f"replicas{world}",
@@ -980,7 +983,9 @@ def decode_checks(host_w, cfg, prompt_h, tokens, args):
     from oracle import decoder as od
     t0 = time.perf_counter()
     r = od.greedy_check(host_w, cfg, prompt_h.numpy(), np.asarray(tokens))
-    match = {"tokens_equal": r["matches"], "of": r["steps"], "first_mismatch": r["first_mismatch"],
+    fm = r["first_mismatch"]
+    match = {"tokens_equal": r["matches"], "of": r["steps"], "first_mismatch": fm,
+             "top2_margin_at_first_mismatch": r["margins"][fm] if fm is not None else None,
              "min_top2_margin": r["min_margin"], "min_margin_step": r["min_margin_step"],
              "check": f"teacher-forced CPU pass of oracle/decoder.py over the {len(prompt_h)}-token prompt and the "
                       f"generated tokens ({time.perf_counter() - t0:.0f} s)"}
@@ -1248,6 +1253,8 @@ def main():
                     help="decode7b: decoder layers (32 = the 7B shape; fewer only for small profiling cases)")
     ap.add_argument("--windows", type=int, default=30,
                     help="timed windows of --steps steps each (sweep workloads); value from the median window")
+    ap.add_argument("--split", action="store_true",
+                    help="prefill: the split-operand GEMM (MSQ_PATH_GEMM_SPLIT) instead of the fp16 one")
     ap.add_argument("--no-sub", action="store_true",
                     help="N = 1 sweep only: skip the prefill and 7B decode sub-records")
     ap.add_argument("--shapes", default="",

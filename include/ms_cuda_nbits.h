@@ -65,7 +65,12 @@ extern "C" {
 
 /* ---- msq_pack flags ----------------------------------------------------------------- */
 #define MSQ_PACK_DEFAULT       0
+/* Pack only the decode GEMV's stream records (about 1.0x the reference's bytes on the device
+ * instead of about 2x): the GEMM's layout is derived from them on the device, with an
+ * allocation, by the first call that takes a GEMM path (make it before any stream capture);
+ * msq_matmul_noalloc refuses the handle until then. For weights that decode only.          */
 #define MSQ_PACK_GENERIC_ONLY  1  /* keep only the reference layout (exercise the generic kernel) */
+#define MSQ_PACK_LAZY_GEMM     2
 
 /* ---- capability / info (ms_kernels.h:23-25, NativeCuda.cs:204-206) ------------------ */
 const char* msq_build_info(void);      /* nvcc version, target arch, build date            */
@@ -130,6 +135,18 @@ int msq_matmul(void* cu_ctx, void* stream, msq_weights_t w,
 int msq_matmul_ex(void* cu_ctx, void* stream, msq_weights_t w,
                   const void* d_a, int a_dtype, int64_t M,
                   float* d_y, int64_t ldy, int path);
+
+/* The int8-activation form of the decode GEMV: the GPU counterpart of ms_qgemm_w4a8
+ * (native/ms_kernels.h, native/src/qgemm_w4a8.cpp:247-292), with its arithmetic: per (A row,
+ * K-block) s_a = max|a| / 127 and aq = rint(a / s_a) clamped to [-127, 127], the block's exact
+ * integer dot of aq with (q - zp), and y += (s_a * s_w) * dot over the blocks. APPROXIMATE
+ * against the fp32 op (activation quantization, about 0.5 % rel-L2), like the reference's;
+ * it matches ms_qgemm_w4a8 up to fp32 summation order. Up to 8 A rows share one pass over
+ * the weights (one s8 column per row). bits=4, block_size 32 / 64 / 128, packed or absent
+ * zero points; A finite.                                                                 */
+int msq_matmul_w4a8(void* cu_ctx, void* stream, msq_weights_t w,
+                    const void* d_a, int a_dtype, int64_t M,
+                    float* d_y, int64_t ldy);
 
 /* Host-buffer form (NativeQuant.TryMatMulNBits, NativeQuant.cs:78-115): copies A in,
  * runs, copies Y [M, n_rows] out and synchronizes the stream.                          */

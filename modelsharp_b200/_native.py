@@ -53,7 +53,7 @@ class FusionT(C.Structure):
     _fields_ = [("rms_gamma", C.c_void_p), ("rms_eps", C.c_float), ("swiglu", C.c_int32), ("accumulate", C.c_int32)]
 
 
-PACK_DEFAULT, PACK_GENERIC_ONLY = 0, 1
+PACK_DEFAULT, PACK_GENERIC_ONLY, PACK_LAZY_GEMM = 0, 1, 2
 DIAG_POOL_ALLOCS, DIAG_NOALLOC_LOOKUPS, DIAG_POOL_RESERVED = 1, 2, 3  # MSQ_DIAG_*
 
 LIB_NAME = "libms_cuda_nbits.so"
@@ -82,6 +82,7 @@ SIGNATURES: dict[str, tuple] = {
     "msq_matmul_ex": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp, _i64, _i32]),
     "msq_matmul_host": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp]),
     "msq_matmul_noalloc": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp, _i64]),
+    "msq_matmul_w4a8": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp, _i64]),
     "msq_device_status": (_i32, [_vp, _vp]),
     "msq_set_wait_budget": (_i32, [_vp, _i64]),
     "msq_xbuf_alloc": (_i32, [_vp, _i64, _vp]),

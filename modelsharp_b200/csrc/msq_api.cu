@@ -192,12 +192,15 @@ int pack_impl(cudaStream_t st, const uint8_t* d_b, int64_t b_len, const void* d_
     w->nib_pitch = w->KP / 2;
     w->sc_pitch = (w->nb + 7) / 8 * 8;
     w->zp_pitch = (w->zp_row_bytes + 15) / 16 * 16;
-    rc = dev_alloc(&w->nib, rows * (size_t)w->nib_pitch, &w->device_bytes);
-    if (rc == MSQ_OK) rc = dev_alloc(&w->sc, rows * (size_t)w->sc_pitch, &w->device_bytes);
-    if (rc == MSQ_OK) rc = dev_alloc(&w->sc16, rows * (size_t)w->sc_pitch, &w->device_bytes);
-    if (rc == MSQ_OK && w->zp_kind == ZP_PACKED) rc = dev_alloc(&w->zp4, rows * (size_t)w->zp_pitch, &w->device_bytes);
-    if (rc == MSQ_OK && w->zp_kind == ZP_F32) rc = dev_alloc(&w->zpf, rows * (size_t)w->sc_pitch, &w->device_bytes);
-    if (rc == MSQ_OK) rc = repack_fast4(st, *w, d_b, n_begin, d_scales, scales_dtype, d_zp);
+    if (!(flags & MSQ_PACK_LAZY_GEMM)) {
+      rc = dev_alloc(&w->nib, rows * (size_t)w->nib_pitch, &w->device_bytes);
+      if (rc == MSQ_OK) rc = dev_alloc(&w->sc, rows * (size_t)w->sc_pitch, &w->device_bytes);
+      if (rc == MSQ_OK) rc = dev_alloc(&w->sc16, rows * (size_t)w->sc_pitch, &w->device_bytes);
+      if (rc == MSQ_OK && w->zp_kind == ZP_PACKED) rc = dev_alloc(&w->zp4, rows * (size_t)w->zp_pitch, &w->device_bytes);
+      if (rc == MSQ_OK && w->zp_kind == ZP_F32) rc = dev_alloc(&w->zpf, rows * (size_t)w->sc_pitch, &w->device_bytes);
+      if (rc == MSQ_OK) rc = repack_fast4(st, *w, d_b, n_begin, d_scales, scales_dtype, d_zp);
+      if (rc == MSQ_OK) w->gemm_layout.store(true, std::memory_order_release);
+    }
     plan_stream(*w);
     if (rc == MSQ_OK)
       rc = dev_alloc(&w->strm, (size_t)w->nblk * w->ntiles * w->stage_bytes, &w->device_bytes);
@@ -522,6 +525,28 @@ int msq_matmul_ex(void* cu_ctx, void* stream, msq_weights_t w, const void* d_a, 
   if (g.rc != MSQ_OK) return g.rc;
   return matmul_impl(static_cast<cudaStream_t>(stream), reinterpret_cast<Weights*>(w), d_a, a_dtype, M, d_y, ldy,
                      path);
+}
+
+int msq_matmul_w4a8(void* cu_ctx, void* stream, msq_weights_t h, const void* d_a, int a_dtype, int64_t M, float* d_y,
+                    int64_t ldy) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  Weights* w = reinterpret_cast<Weights*>(h);
+  if (!w) return fail(MSQ_E_INVALID, "msq_matmul_w4a8: NULL weights handle");
+  if (!is_float_act(a_dtype))
+    return fail(MSQ_E_INVALID, "MatMulNBits A must be Float32 or Float16; got %s.", dtype_name(a_dtype));
+  if (M < 0 || ldy < w->n_rows) return fail(MSQ_E_INVALID, "msq_matmul_w4a8: bad M (%lld) or ldy", (long long)M);
+  if (M == 0) return MSQ_OK;
+  if (!d_a || !d_y) return fail(MSQ_E_INVALID, "msq_matmul_w4a8: NULL device pointer");
+  if (!w->fast4 || !w->strm)
+    return fail(MSQ_E_UNSUPPORTED, "msq_matmul_w4a8 needs bits=4 and block_size 32, 64 or 128");
+  int dev;
+  const int rc = current_device(&dev);
+  if (rc != MSQ_OK) return rc;
+  if (dev != w->device)
+    return fail(MSQ_E_INVALID, "weights handle lives on device %d but the current device is %d", w->device, dev);
+  refresh_settled(*w, static_cast<cudaStream_t>(stream));
+  return run_gemv_w4a8(static_cast<cudaStream_t>(stream), *w, d_a, a_dtype, M, d_y, ldy);
 }
 
 int msq_matmul_host(void* cu_ctx, void* stream, msq_weights_t h, const void* a, int a_dtype, int64_t M, float* y) {

@@ -658,6 +658,10 @@ int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t 
   if (!w.fast4) return fail(MSQ_E_UNSUPPORTED, "GEMM path needs bits=4 and a power-of-two block_size >= 32");
   if (M <= 0) return MSQ_OK;
   if (M > 0x7fffffff) return fail(MSQ_E_INVALID, "GEMM: M too large");
+  {
+    const int lrc = ensure_gemm_layout(st, w);
+    if (lrc != MSQ_OK) return lrc;
+  }
   // The tensor maps are built once per handle (under the handle's own lock, so first calls on
   // different handles do not wait for each other) and only read afterwards.
   GemmState* gs = static_cast<GemmState*>(w.gemm_state.load(std::memory_order_acquire));
@@ -705,6 +709,10 @@ size_t gemm_staging_bytes(const Weights& w, const void* d_a, int a_dtype, int64_
 int run_gemm_staged(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M, float* d_y,
                     int64_t ldy, void* staging, size_t staging_bytes) {
   if (!w.fast4) return fail(MSQ_E_UNSUPPORTED, "GEMM path needs bits=4 and a power-of-two block_size >= 32");
+  if (!w.gemm_layout.load(std::memory_order_acquire))
+    return fail(MSQ_E_UNSUPPORTED,
+                "the handle was packed with MSQ_PACK_LAZY_GEMM and has no GEMM layout yet (it is built, with an "
+                "allocation, by the first msq_matmul that takes the GEMM path)");
   if (M <= 0) return MSQ_OK;
   if (M > 0x7fffffff) return fail(MSQ_E_INVALID, "GEMM: M too large");
   WeightMaps m128;

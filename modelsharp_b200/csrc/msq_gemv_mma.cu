@@ -33,6 +33,7 @@ constexpr int kThreads = (kConsumers + 1) * 32;
 constexpr int kMaxSlots = 8;
 constexpr int kSmemMax = 227 * 1024;
 constexpr int kMaxM = 4;  // B columns: 4 per A row (3 digits + 1 zero) -> two n8 tiles for 4 rows
+constexpr int kMaxMA8 = 8;  // the int8-activation form: one B column per A row -> 8 rows in one n8 tile
 constexpr int kUpw = 2;                 // k-units per warp per tile
 constexpr int kYPitch = kConsumers + 1;  // per-warp partial sums of one output, padded against
                                          // bank conflicts in the per-stage update
@@ -241,9 +242,13 @@ __device__ float nonfinite_terms(const Args& p, int m, int64_t row) {
 // XG = the column-split form (outputs to every rank's full-Y buffer, optional wait for a
 // gathered input); FU = the decode-step fusion forms (RMSNorm / SwiGLU input, accumulate). A "unit" is max(BS, 64) k: one or two 64-k chunks (a uint4 of code words
 // per lane each).
-template <int BS, int NT, bool XG, bool FU>
+// A8 = the int8-activation form (ms_qgemm_w4a8's arithmetic, native/src/qgemm_w4a8.cpp:247-292,
+// 622-690): per (A row, block) s_a = max|a| / 127 and aq = rint(a / s_a) in [-127, 127], one s8
+// B column per A row, the block's exact integer dot aq . (q - zp) and y += (s_a s_w) dot.
+template <int BS, int NT, bool XG, bool FU, bool A8 = false>
 __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
   static_assert(!(XG && FU), "the column-split form takes no fusion");
+  static_assert(!A8 || (!XG && !FU && NT == 1), "the int8-activation form is plain, 8 rows per pass");
   constexpr int UNIT = BS > 64 ? BS : 64;
   constexpr int CH = UNIT / 64;     // 64-k chunks per unit
   constexpr int UB = UNIT / BS;     // blocks per unit
@@ -256,7 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
   float* sinv = reinterpret_cast<float*>(sblk + p.mc * (p.kp / BS));  // [mc][kp/BS] 2^-sigma_b
   float* ysum = reinterpret_cast<float*>(smem + p.off_ysum);  // [rows_cta][mc][33]: per warp
   float* rowsq = reinterpret_cast<float*>(smem + 64);         // [kConsumers][kMaxM] sums of x^2
-  volatile int* nonfin = reinterpret_cast<volatile int*>(smem);  // [kMaxM]: A row holds inf / NaN
+  volatile int* nonfin = reinterpret_cast<volatile int*>(smem);  // [kMaxMA8]: A row holds inf / NaN
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.off_bar);
   uint64_t* empty = full + kMaxSlots;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kMaxSlots);
@@ -272,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
       ptx::mbar_init(&empty[s], kConsumers);
     }
     *abort_flag = 0;
-    for (int m = 0; m < kMaxM; ++m) nonfin[m] = 0;
+    for (int m = 0; m < kMaxMA8; ++m) nonfin[m] = 0;
     ptx::fence_mbar_init();
     griddep_launch_dependents();
   }
@@ -386,11 +391,30 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
 #pragma unroll
           for (int off = 1; off < GL; off <<= 1) bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, off));
         }
-        const int sh = max(-120, min(120, 22 - frexp_exponent(bmax)));
+        int sh = 0;
+        float sa = 0.f;  // A8: the block's activation scale
         int bsum = 0;
-        if (f < n4) {
-          const int m = f / n4row;
-          bsum = store_digits(dig, p.kpp, m, 4 * (f - m * n4row), v[u], exp2i(sh));
+        if constexpr (A8) {
+          // the reference's IEEE steps: s = amax / 127, inv = 1 / s, q = lrintf(a inv) clamped
+          sa = bmax / 127.0f;
+          const float inv = sa > 0.f ? 1.0f / sa : 0.f;
+          if (f < n4) {
+            const int m = f / n4row;
+            const int q0 = max(-127, min(127, __float2int_rn(v[u].x * inv)));
+            const int q1 = max(-127, min(127, __float2int_rn(v[u].y * inv)));
+            const int q2 = max(-127, min(127, __float2int_rn(v[u].z * inv)));
+            const int q3 = max(-127, min(127, __float2int_rn(v[u].w * inv)));
+            *reinterpret_cast<uint32_t*>(dig + m * p.kpp + 4 * (f - m * n4row)) =
+                (uint32_t)(q0 & 0xFF) | ((uint32_t)(q1 & 0xFF) << 8) | ((uint32_t)(q2 & 0xFF) << 16) |
+                ((uint32_t)(q3 & 0xFF) << 24);
+            bsum = q0 + q1 + q2 + q3;
+          }
+        } else {
+          sh = max(-120, min(120, 22 - frexp_exponent(bmax)));
+          if (f < n4) {
+            const int m = f / n4row;
+            bsum = store_digits(dig, p.kpp, m, 4 * (f - m * n4row), v[u], exp2i(sh));
+          }
         }
         if constexpr (GL == 32) {
           bsum = (int)__reduce_add_sync(0xffffffffu, (uint32_t)bsum);
@@ -400,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
         }
         if (f < n4 && (lane & (GL - 1)) == 0) {
           sblk[f / GL] = bsum;
-          sinv[f / GL] = exp2i(-sh);
+          sinv[f / GL] = A8 ? sa : exp2i(-sh);
         }
       }
     }
@@ -439,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           const int col = nt * 8 + grp;
-          const bool ok = u < units && col < 4 * mc && (col & 3) != 3;
+          const bool ok = u < units && (A8 ? col < mc : col < 4 * mc && (col & 3) != 3);
           const int8_t* d = dig + col * p.kpp + kk0 + 32 * st + 4 * tq;
           bf[uu][st][nt][0] = ok ? *reinterpret_cast<const uint32_t*>(d) : 0u;
           bf[uu][st][nt][1] = ok ? *reinterpret_cast<const uint32_t*>(d + 16) : 0u;
@@ -448,6 +472,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
       for (int bl = 0; bl < UB; ++bl)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
+          if constexpr (A8) {
+            // this lane's two A rows (B columns 2 tq, 2 tq + 1): block sums S and scales s_a
+            const int m0 = 2 * tq, m1 = m0 + 1;
+            const int bix = kk0 / BS + bl;
+            const bool ok0 = u < units && m0 < mc, ok1 = u < units && m1 < mc;
+            sv[uu][bl][nt] = ok0 ? (float)sblk[m0 * nbp + bix] : 0.f;
+            sv16[uu][bl][nt] = ok1 ? (float)sblk[m1 * nbp + bix] : 0.f;
+            gw0[uu][bl][nt] = ok0 ? sinv[m0 * nbp + bix] : 0.f;
+            gw1[uu][bl][nt] = ok1 ? sinv[m1 * nbp + bix] : 0.f;
+            continue;
+          }
           const int m = nt * 2 + (tq >> 1);
           const bool okb = u < units && m < mc;
           // the zero-point term rides on the lanes of digits 0 and 1 (even tq) only; every
@@ -528,6 +563,37 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
               for (int nt = 0; nt < NT; ++nt)
                 imma(c[uu][bl][q & 1][nt], lo0, hi0, lo1, hi1, bf[uu][st][nt][0], bf[uu][st][nt][1]);
             }
+        if constexpr (A8) {
+          // c[0], c[1]: rows grp (low nibbles) of A rows 2 tq, 2 tq + 1; c[2], c[3]: rows grp + 8
+          // (high nibbles, 16 q). aqwc = dot - zp S is exact (every term < 2^24), and each block
+          // adds (s_a s_w) aqwc as ms_qgemm_w4a8 does.
+          float a00 = 0.f, a01 = 0.f, a10 = 0.f, a11 = 0.f;
+#pragma unroll
+          for (int uu = 0; uu < UPW; ++uu)
+#pragma unroll
+            for (int bl = 0; bl < UB; ++bl) {
+              int cc[4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) cc[j] = c[uu][bl][0][0][j] + c[uu][bl][1][0][j];
+              const float S0 = sv[uu][bl][0], S1 = sv16[uu][bl][0];
+              const float d00 = (float)cc[0] - z0[uu][bl] * S0, d01 = (float)cc[1] - z0[uu][bl] * S1;
+              const float d10 = (float)(cc[2] >> 4) - z1[uu][bl] * S0, d11 = (float)(cc[3] >> 4) - z1[uu][bl] * S1;
+              a00 += (gw0[uu][bl][0] * s0[uu][bl]) * d00;
+              a01 += (gw1[uu][bl][0] * s0[uu][bl]) * d01;
+              a10 += (gw0[uu][bl][0] * s1[uu][bl]) * d10;
+              a11 += (gw1[uu][bl][0] * s1[uu][bl]) * d11;
+            }
+          const int m0 = 2 * tq, m1 = m0 + 1;
+          float* yr = ysum + (i * 16 + grp) * mc * kYPitch + warp;  // row grp + 8 sits 8 mc kYPitch further
+          if (m0 < mc) {
+            yr[m0 * kYPitch] += a00;
+            yr[(8 * mc + m0) * kYPitch] += a10;
+          }
+          if (m1 < mc) {
+            yr[m1 * kYPitch] += a01;
+            yr[(8 * mc + m1) * kYPitch] += a11;
+          }
+        } else {
         float y0[NT], y1[NT];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) y0[nt] = y1[nt] = 0.f;
@@ -561,6 +627,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
             yc[8 * mc * kYPitch] += v1;
           }
         }
+        }  // the digit form
       }
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&empty[rs]);
@@ -594,7 +661,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
       const int b = blockIdx.x + (r >> 4) * grid;
       const int64_t row = (int64_t)b * 16 + (r & 15);
       if (b < p.nblk && row < p.n_rows) {
-        if (nonfin[m]) {
+        if (!A8 && nonfin[m]) {
           // RMSNorm of a row holding inf / NaN is NaN everywhere (inf / inf, 0 * inf)
           if (FU && p.gamma) acc = __int_as_float(0x7FC00000);
           else acc += nonfinite_terms<BS, FU>(p, m, row);
@@ -642,9 +709,9 @@ __global__ void wait_gathered_kernel(const unsigned long long* arr, const unsign
   if (threadIdx.x == 0) wait_arrivals(arr, prod, nranks);
 }
 
-template <int BS, int NT, bool XG, bool FU>
+template <int BS, int NT, bool XG, bool FU, bool A8 = false>
 int launch(cudaStream_t st, const Args& a, int grid, size_t smem) {
-  auto kern = gemv_mma_kernel<BS, NT, XG, FU>;
+  auto kern = gemv_mma_kernel<BS, NT, XG, FU, A8>;
   static ContextOnce configured;
   const int rc = configured.run([&] {
     MSQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax),
@@ -670,10 +737,10 @@ int launch(cudaStream_t st, const Args& a, int grid, size_t smem) {
 inline int align_up(int v, int a) { return (v + a - 1) / a * a; }
 
 // Shared-memory plan for mc rows of A; returns the bytes, or 0 if fewer than 2 stages fit.
-size_t plan_smem(const Weights& w, int mc, int grid, Args& a) {
+size_t plan_smem(const Weights& w, int mc, int grid, Args& a, bool a8 = false) {
   const int kp = w.ntiles * w.kt;
   const int head = 64 + 16 * kMaxM * 4;
-  const int dig = 4 * mc * (kp + 16);
+  const int dig = (a8 ? 1 : 4) * mc * (kp + 16);  // B columns per A row: 3 digits + a zero, or one s8
   const int sb = align_up(8 * mc * (kp / w.block_size), 16);  // block sums + block scales
   a.rows_cta = ((w.nblk + grid - 1) / grid) * 16;
   const int ysum = align_up(a.rows_cta * mc * kYPitch * 4, 16);
@@ -703,8 +770,11 @@ namespace {
 // One decode GEMV call: passes of up to 4 A rows; with `g` (column split) a single pass
 // whose outputs go to every rank's full-Y buffer, after waiting for `wt` (or nothing).
 int gemv_impl(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M, float* d_y,
-              int64_t ldy, const msq_wait_t* wt, const msq_gather_t* g, const Fusion* fu = nullptr) {
+              int64_t ldy, const msq_wait_t* wt, const msq_gather_t* g, const Fusion* fu = nullptr,
+              bool a8 = false) {
   if (!w.strm || (w.block_size != 32 && w.block_size != 64 && w.block_size != 128)) return MSQ_E_UNSUPPORTED;
+  if (a8 && w.zp_kind == ZP_F32)
+    return fail(MSQ_E_UNSUPPORTED, "msq_matmul_w4a8 takes packed or absent zero points (as ms_qgemm_w4a8)");
   const int unit = w.block_size > 64 ? w.block_size : 64;
   if (w.kt / unit > kUpw * kConsumers) return MSQ_E_UNSUPPORTED;
   const int sms = num_sms(w.device);
@@ -760,11 +830,11 @@ int gemv_impl(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, i
       }
     }
     // the widest pass whose digits, row sums and ring fit in shared memory
-    int mc = (int)std::min<int64_t>(kMaxM, M - m0);
+    int mc = (int)std::min<int64_t>(a8 ? kMaxMA8 : kMaxM, M - m0);
     int grid = std::min(w.nblk, sms);
     size_t smem = 0;
     for (;;) {
-      smem = plan_smem(w, mc, grid, a);
+      smem = plan_smem(w, mc, grid, a, a8);
       if (smem) break;
       if (grid < w.nblk) {
         grid = std::min(w.nblk, grid * 2);  // fewer rows per CTA -> smaller row-sum buffer
@@ -778,7 +848,13 @@ int gemv_impl(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, i
     if (g && mc < M) return fail(MSQ_E_UNSUPPORTED, "msq_matmul_gather: %lld A rows do not fit one pass", (long long)M);
     a.mc = mc;
     int rc;
-    if (g) {
+    if (a8) {
+      switch (w.block_size) {
+        case 32: rc = launch<32, 1, false, false, true>(st, a, grid, smem); break;
+        case 64: rc = launch<64, 1, false, false, true>(st, a, grid, smem); break;
+        default: rc = launch<128, 1, false, false, true>(st, a, grid, smem); break;
+      }
+    } else if (g) {
       switch (w.block_size) {
         case 32: rc = launch_nt<32, true>(st, a, grid, smem); break;
         case 64: rc = launch_nt<64, true>(st, a, grid, smem); break;
@@ -800,7 +876,8 @@ int gemv_impl(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, i
     if (rc != MSQ_OK) return rc;
     m0 += mc;
   }
-  note_path(g ? "gemv_imma_gather" : fu ? "gemv_imma_fused" : M <= 4 ? "gemv_imma" : "gemv_imma_multipass");
+  note_path(a8 ? (M <= kMaxMA8 ? "gemv_w4a8" : "gemv_w4a8_multipass")
+                : g ? "gemv_imma_gather" : fu ? "gemv_imma_fused" : M <= 4 ? "gemv_imma" : "gemv_imma_multipass");
   return MSQ_OK;
 }
 
@@ -809,6 +886,11 @@ int gemv_impl(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, i
 int run_gemv_mma(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M, float* d_y,
                  int64_t ldy) {
   return gemv_impl(st, w, d_a, a_dtype, M, d_y, ldy, nullptr, nullptr);
+}
+
+int run_gemv_w4a8(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M, float* d_y,
+                  int64_t ldy) {
+  return gemv_impl(st, w, d_a, a_dtype, M, d_y, ldy, nullptr, nullptr, nullptr, true);
 }
 
 int run_gemv_gather(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M,

@@ -63,6 +63,8 @@ struct Weights {
   int64_t device_bytes = 0;
   std::atomic<void*> gemm_state{nullptr};  // GEMM tensor maps, built by the first GEMM call
   std::mutex state_mu;                     // guards that first build on this handle only
+  std::atomic<bool> gemm_layout{false};    // nib / sc / sc16 / zp planes hold the weights (packed with
+                                           // them, or derived from strm at the first GEMM call)
   cudaEvent_t packed_ev = nullptr;   // recorded on the packing stream after the repack kernels
   std::atomic<bool> settled{false};  // the host has seen packed_ev complete: kernels may read
                                      // the weights before their programmatic-dependency wait
@@ -124,6 +126,9 @@ int repack_fast4(cudaStream_t st, Weights& w, const uint8_t* d_b, int n_begin,
 int repack_stream(cudaStream_t st, Weights& w, const uint8_t* d_b, int n_begin,
                   const void* d_scales, int scales_dtype, const void* d_zp);
 void plan_stream(Weights& w);
+// The GEMM layout (nib, sc, sc16, zp4 / zpf) of a handle packed with MSQ_PACK_LAZY_GEMM, derived
+// from its stream records on the device the first time the GEMM needs it (allocates).
+int ensure_gemm_layout(cudaStream_t st, Weights& w);
 int read_gemv_mma_errors(cudaStream_t st, int* flags);
 int read_gemm_errors(cudaStream_t st, int* flags);
 // Bounded-wait budgets of the decode GEMV's and the GEMM's modules on the current device.
@@ -139,6 +144,9 @@ int run_gemv(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, in
              float* d_y, int64_t ldy);
 int run_gemv_mma(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M,
                  float* d_y, int64_t ldy);
+// The int8-activation decode GEMV (ms_qgemm_w4a8's arithmetic), up to 8 A rows per pass.
+int run_gemv_w4a8(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M,
+                  float* d_y, int64_t ldy);
 // The column-split decode GEMV (outputs to every rank's full-Y buffer) and the wait kernel.
 int run_gemv_gather(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M,
                     const msq_wait_t* wt, const msq_gather_t* g);

@@ -6,6 +6,7 @@
 #include "msq_internal.cuh"
 
 #include <algorithm>
+#include <mutex>
 
 namespace msq {
 namespace {
@@ -215,6 +216,152 @@ int repack_stream(cudaStream_t st, Weights& w, const uint8_t* d_b, int n_begin, 
       reinterpret_cast<uint32_t*>(w.strm), total);
   note_launch();
   MSQ_CUDA_TRY(cudaGetLastError(), "stream repack launch");
+  return MSQ_OK;
+}
+
+namespace {
+
+// The code, scale and zero point of (row r, k) read back from the decode-stream records
+// (layout in msq_internal.cuh); k < K.
+struct StreamGeo {
+  const uint8_t* strm;
+  int kt, ntiles, stage_bytes, off_sc, off_zp, zp_kind, bs;
+};
+
+__device__ __forceinline__ const uint8_t* record_of(const StreamGeo& g, int64_t r, int k, int* kk) {
+  const int t = k / g.kt;
+  *kk = k - t * g.kt;
+  return g.strm + ((r >> 4) * g.ntiles + t) * (int64_t)g.stage_bytes;
+}
+
+__device__ __forceinline__ uint32_t stream_code(const StreamGeo& g, int64_t r, int k) {
+  int kk;
+  const uint8_t* rec = record_of(g, r, k, &kk);
+  const int rr = (int)(r & 15), o = kk & 63;
+  const int word = (o >> 5) * 2 + ((o >> 4) & 1);
+  const int ln = (rr & 7) * 4 + ((o & 15) >> 2);
+  const uint8_t v = rec[(kk >> 6) * 512 + ln * 16 + word * 4 + (o & 3)];
+  return rr < 8 ? (v & 0xFu) : (uint32_t)(v >> 4);
+}
+
+// The GEMM's nibble plane from the stream: one thread per output word (slot order kSlotK).
+__global__ void nib_from_stream_kernel(StreamGeo g, int n_rows, int K, uint32_t* __restrict__ nib,
+                                       int64_t words_per_row) {
+  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)n_rows * words_per_row) return;
+  const int64_t r = idx / words_per_row, wi = idx - r * words_per_row;
+  uint32_t out = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int64_t k = wi * 8 + kSlotK[j];
+    if (k < K) out |= stream_code(g, r, (int)k) << (4 * j);
+  }
+  nib[idx] = out;
+}
+
+// Scale planes (fp32, fp16) and the float zero-point plane from the stream: one thread per
+// (row, padded block).
+__global__ void scales_from_stream_kernel(StreamGeo g, int n_rows, int nb, float* __restrict__ sc,
+                                          __half* __restrict__ sc16, float* __restrict__ zpf, int64_t sc_pitch) {
+  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)n_rows * sc_pitch) return;
+  const int64_t r = idx / sc_pitch;
+  const int bk = (int)(idx - r * sc_pitch);
+  float v = 0.f, z = 0.f;
+  if (bk < nb) {
+    int kk;
+    const uint8_t* rec = record_of(g, r, bk * g.bs, &kk);
+    const int bl = kk / g.bs, rr = (int)(r & 15);
+    v = reinterpret_cast<const float*>(rec + g.off_sc)[bl * 16 + rr];
+    if (zpf) z = reinterpret_cast<const float*>(rec + g.off_zp)[bl * 16 + rr];
+  }
+  sc[idx] = v;
+  sc16[idx] = __float2half_rn(v);
+  if (zpf) zpf[idx] = z;
+}
+
+// The packed zero-point plane from the stream: one thread per byte (blocks 2j and 2j + 1).
+__global__ void zp_from_stream_kernel(StreamGeo g, int n_rows, int nb, uint8_t* __restrict__ zp4, int64_t zp_pitch) {
+  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)n_rows * zp_pitch) return;
+  const int64_t r = idx / zp_pitch;
+  const int j = (int)(idx - r * zp_pitch);
+  const int rr = (int)(r & 15);
+  uint32_t out = 0;
+  for (int h = 0; h < 2; ++h) {
+    const int bk = 2 * j + h;
+    if (bk < nb) {
+      int kk;
+      const uint8_t* rec = record_of(g, r, bk * g.bs, &kk);
+      const unsigned long long zw = reinterpret_cast<const unsigned long long*>(rec + g.off_zp)[kk / g.bs];
+      out |= (uint32_t)((zw >> (4 * rr)) & 0xF) << (4 * h);
+    }
+  }
+  zp4[idx] = (uint8_t)out;
+}
+
+int alloc_plane(void** p, size_t bytes, int64_t* total) {
+  *p = nullptr;
+  if (!bytes) return MSQ_OK;
+  const cudaError_t e = cudaMalloc(p, bytes);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(MSQ_E_OOM, "device allocation of %zu bytes for the GEMM layout failed: %s", bytes,
+                cudaGetErrorString(e));
+  }
+  *total += (int64_t)bytes;
+  return MSQ_OK;
+}
+
+}  // namespace
+
+int ensure_gemm_layout(cudaStream_t st, Weights& w) {
+  if (w.gemm_layout.load(std::memory_order_acquire)) return MSQ_OK;
+  std::lock_guard<std::mutex> lk(w.state_mu);
+  if (w.gemm_layout.load(std::memory_order_relaxed)) return MSQ_OK;
+  if (!w.strm) return fail(MSQ_E_UNSUPPORTED, "GEMM path: the handle holds neither layout");
+  const size_t rows = (size_t)w.n_rows;
+  uint8_t* nib = nullptr;
+  float *sc = nullptr, *zpf = nullptr;
+  __half* sc16 = nullptr;
+  uint8_t* zp4 = nullptr;
+  int64_t bytes = 0;
+  int rc = alloc_plane(reinterpret_cast<void**>(&nib), rows * (size_t)w.nib_pitch, &bytes);
+  if (rc == MSQ_OK) rc = alloc_plane(reinterpret_cast<void**>(&sc), rows * (size_t)w.sc_pitch * 4, &bytes);
+  if (rc == MSQ_OK) rc = alloc_plane(reinterpret_cast<void**>(&sc16), rows * (size_t)w.sc_pitch * 2, &bytes);
+  if (rc == MSQ_OK && w.zp_kind == ZP_PACKED)
+    rc = alloc_plane(reinterpret_cast<void**>(&zp4), rows * (size_t)w.zp_pitch, &bytes);
+  if (rc == MSQ_OK && w.zp_kind == ZP_F32)
+    rc = alloc_plane(reinterpret_cast<void**>(&zpf), rows * (size_t)w.sc_pitch * 4, &bytes);
+  const StreamGeo g{w.strm, w.kt, w.ntiles, w.stage_bytes, w.off_sc, w.off_zp, w.zp_kind, w.block_size};
+  const int T = 256;
+  if (rc == MSQ_OK) {
+    const int64_t words = (int64_t)w.n_rows * (w.nib_pitch / 4);
+    nib_from_stream_kernel<<<grid_for(words, T), T, 0, st>>>(g, w.n_rows, w.K, reinterpret_cast<uint32_t*>(nib),
+                                                             w.nib_pitch / 4);
+    const int64_t sn = (int64_t)w.n_rows * w.sc_pitch;
+    scales_from_stream_kernel<<<grid_for(sn, T), T, 0, st>>>(g, w.n_rows, w.nb, sc, sc16, zpf, w.sc_pitch);
+    note_launch(2);
+    if (zp4) {
+      const int64_t zn = (int64_t)w.n_rows * w.zp_pitch;
+      zp_from_stream_kernel<<<grid_for(zn, T), T, 0, st>>>(g, w.n_rows, w.nb, zp4, w.zp_pitch);
+      note_launch();
+    }
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) rc = cuda_fail(e, "GEMM layout from the stream: launch");
+  }
+  if (rc != MSQ_OK) {
+    for (void* q : {(void*)nib, (void*)sc, (void*)sc16, (void*)zp4, (void*)zpf})
+      if (q) cudaFree(q);
+    return rc;
+  }
+  w.sc = sc;
+  w.sc16 = sc16;
+  w.zp4 = zp4;
+  w.zpf = zpf;
+  w.nib = nib;
+  w.device_bytes += bytes;
+  w.gemm_layout.store(true, std::memory_order_release);
   return MSQ_OK;
 }
 

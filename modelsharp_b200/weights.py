@@ -46,7 +46,7 @@ class QuantizedWeights:
 
     def __init__(self, b, scales, zero_points, N_: int, K: int, bits: int = 4, block_size: int = 32,
                  rows: tuple[int, int] | None = None, device: torch.device | int | str | None = None,
-                 generic_only: bool = False):
+                 generic_only: bool = False, lazy_gemm: bool = False):
         lib = N.lib()
         dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         if dev.type != "cuda":
@@ -54,7 +54,7 @@ class QuantizedWeights:
         n0, n1 = rows if rows is not None else (0, N_)
         b_t, s_t = as_torch(b), as_torch(scales)
         z_t = as_torch(zero_points) if zero_points is not None else None
-        flags = N.PACK_GENERIC_ONLY if generic_only else N.PACK_DEFAULT
+        flags = (N.PACK_GENERIC_ONLY if generic_only else N.PACK_DEFAULT) | (N.PACK_LAZY_GEMM if lazy_gemm else 0)
         h = C.c_void_p()
         with torch.cuda.device(dev):
             on_dev = b_t.is_cuda
@@ -83,6 +83,12 @@ class QuantizedWeights:
         nb_ = C.c_int64()
         lib.msq_weights_query(h, None, None, None, None, C.byref(nb_))
         self.device_bytes = nb_.value
+
+    def query_device_bytes(self) -> int:
+        """Device bytes the handle holds now (a lazy handle grows at its first GEMM call)."""
+        nb_ = C.c_int64()
+        N.check(N.lib().msq_weights_query(self.handle, None, None, None, None, C.byref(nb_)), "msq_weights_query")
+        return nb_.value
 
     @property
     def handle(self) -> C.c_void_p:

@@ -201,3 +201,65 @@ int mnb_dequant(const uint8_t* b, const float* scales, int zp_kind, const void* 
     }
     return 0;
 }
+
+/* ms_qgemm_w4a8, the reference's approximate int8-activation kernel
+ * (native/src/qgemm_w4a8.cpp:247-292, scalar path :622-690): per (row m, K-block)
+ * s_a = amax / 127, inv = 1 / s_a (0 for an all-zero block), aq = lrintf(a * inv) clamped to
+ * [-127, 127]; weight codes centred wc = code - zp (clamped, a no-op at 4 bits); per block the
+ * exact integer dot sum aq * wc, and y accumulates (s_a * s_w) * dot over the blocks in order.
+ * Packed or absent zero points only (zp_kind 0 / 1), as the reference takes. */
+int mnb_ref_w4a8(const float* a, const uint8_t* b, const float* scales, int zp_kind,
+                 const void* zp, float* y, int M, int N, int K, int bits, int block_size,
+                 int nthreads) {
+    if (N <= 0 || K <= 0 || block_size <= 0 || (bits != 4 && bits != 8) || M < 0 || zp_kind == 2) return -1;
+    const int nb = (K + block_size - 1) / block_size;
+    const int blob = (block_size * bits + 7) / 8;
+    const int zp_row_bytes = (nb * bits + 7) / 8;
+    const long b_row_bytes = (long)nb * blob;
+    const int padK = nb * block_size;
+    int8_t* aq = (int8_t*)calloc((size_t)M * padK + 1, 1);
+    float* sa = (float*)malloc(sizeof(float) * ((size_t)M * nb + 1));
+    if (!aq || !sa) { free(aq); free(sa); return -1; }
+#ifdef _OPENMP
+    if (nthreads > 0) omp_set_num_threads(nthreads);
+#else
+    (void)nthreads;
+#endif
+    for (int m = 0; m < M; ++m)
+        for (int bk = 0; bk < nb; ++bk) {
+            const int k0 = bk * block_size, k1 = k0 + block_size < K ? k0 + block_size : K;
+            float amax = 0.0f;
+            for (int k = k0; k < k1; ++k) { float v = fabsf(a[(long)m * K + k]); if (v > amax) amax = v; }
+            const float s = amax / 127.0f;
+            sa[(long)m * nb + bk] = s;
+            const float inv = s > 0.0f ? 1.0f / s : 0.0f;
+            for (int k = k0; k < k1; ++k) {
+                int q = (int)lrintf(a[(long)m * K + k] * inv);
+                if (q > 127) q = 127; else if (q < -127) q = -127;
+                aq[(long)m * padK + k] = (int8_t)q;
+            }
+        }
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < N; ++n) {
+        for (int m = 0; m < M; ++m) {
+            float acc = 0.0f;
+            for (int bk = 0; bk < nb; ++bk) {
+                const int z = zp_kind == 1 ? unpack_nbit((const uint8_t*)zp, (long)n * zp_row_bytes, bk, bits)
+                                           : (1 << (bits - 1));
+                const long blob_base = (long)n * b_row_bytes + (long)bk * blob;
+                const int k0 = bk * block_size, k1 = k0 + block_size < K ? k0 + block_size : K;
+                int32_t dot = 0;
+                for (int k = k0; k < k1; ++k) {
+                    int wc = unpack_nbit(b, blob_base, k - k0, bits) - z;
+                    if (wc > 127) wc = 127; else if (wc < -127) wc = -127;
+                    dot += (int32_t)aq[(long)m * padK + k] * wc;
+                }
+                acc += sa[(long)m * nb + bk] * scales[(long)n * nb + bk] * (float)dot;
+            }
+            y[(long)m * N + n] = acc;
+        }
+    }
+    free(aq);
+    free(sa);
+    return 0;
+}

@@ -60,7 +60,7 @@ def _lib():
         if not ORACLE_SO.exists():
             build()
         L = C.CDLL(str(ORACLE_SO))
-        for name in ("mnb_ref_managed", "mnb_ref_f64"):
+        for name in ("mnb_ref_managed", "mnb_ref_f64", "mnb_ref_w4a8"):
             f = getattr(L, name)
             f.restype = C.c_int
             f.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
@@ -82,6 +82,8 @@ def _ref_lib():
         L = C.CDLL(str(REF_SO))
         L.ms_qgemm_nbits.restype = None
         L.ms_qgemm_nbits.argtypes = [C.c_void_p] * 5 + [C.c_int] * 5
+        L.ms_qgemm_w4a8.restype = None
+        L.ms_qgemm_w4a8.argtypes = [C.c_void_p] * 5 + [C.c_int] * 5
         L.ms_build_info.restype = C.c_char_p
         _ref = L
     return _ref
@@ -115,6 +117,23 @@ def _run(fn_name: str, case: dict, threads: int = 0, rows: slice | None = None) 
 
 def managed(case: dict, threads: int = 0, rows: slice | None = None) -> np.ndarray:
     return _run("mnb_ref_managed", case, threads, rows)
+
+
+def w4a8(case: dict, threads: int = 0, rows: slice | None = None) -> np.ndarray:
+    """The C restatement of ms_qgemm_w4a8 (int8 activations per row and block; approximate)."""
+    return _run("mnb_ref_w4a8", case, threads, rows)
+
+
+def reference_w4a8(case: dict, rows: slice | None = None) -> np.ndarray:
+    """The reference's own ms_qgemm_w4a8 (oracle/_ref, built from native/src/qgemm_w4a8.cpp)."""
+    if case["zp_kind"] == "float":
+        raise ValueError("ms_qgemm_w4a8 takes packed or absent zero points only")
+    a, b, s, kind, z = _inputs(case, rows)
+    M = a.shape[0]
+    y = np.empty((M, case["N"]), dtype=np.float32)
+    _ref_lib().ms_qgemm_w4a8(a.ctypes.data, b.ctypes.data, s.ctypes.data, z.ctypes.data if z is not None else None,
+                             y.ctypes.data, M, case["N"], case["K"], case["bits"], case["block_size"])
+    return y
 
 
 def dequant(case: dict, threads: int = 0) -> np.ndarray:

@@ -16,6 +16,10 @@ QGEMM_GRID = [
     for M in (1, 8) for N in (64, 512) for K in (128, 4096) for bs in (32, 128)
 ] + [(8, 512, 4096, 8, 128, "packed")]
 
+# The 4-bit cases of QGEMM_GRID, for the reference's ms_qgemm_w4a8 (native/test/qgemm_w4a8_test.cpp
+# runs its own grid of the same kind).
+W4A8_CASES = [i for i, g in enumerate(QGEMM_GRID) if g[3] == 4]
+
 # GpuQuantizedLlmOpsTests.cs:326-339 -- (M, K, N, bits, block_size, zp form, seed);
 # A ~ U(-1,1), scales 0.01 + 0.05 U, zero points 2^(bits-1) + U{-2..2} for the float form.
 GPU_PARITY_GRID = [

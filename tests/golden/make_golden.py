@@ -113,10 +113,16 @@ def main() -> None:
                 entry["y"] = "dequant + double dot (qgemm_test.cpp:60-89); ms_qgemm_nbits has no float zp"
             meta.append(entry)
     np.savez_compressed(HERE / "ref_native.npz", **arrays)
+    # the reference's approximate int8-activation kernel on the 4-bit cases of the qgemm grid
+    w4 = {}
+    for i in cases.W4A8_CASES:
+        c = cases.qgemm_case(i)
+        w4[f"qgemm{i}"] = oracle.reference_w4a8(c)
+    np.savez_compressed(HERE / "ref_w4a8.npz", **w4)
     (HERE / "ref_native.json").write_text(json.dumps(
         {"generator": "tests/golden/make_golden.py", "reference_build": oracle._ref_lib().ms_build_info().decode(),
          "cases": meta}, indent=1))
-    print(f"wrote {len(KATS)} KATs and {len(meta)} reference outputs")
+    print(f"wrote {len(KATS)} KATs, {len(meta)} reference outputs and {len(w4)} ms_qgemm_w4a8 outputs")
 
 
 if __name__ == "__main__":

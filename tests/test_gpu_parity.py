@@ -213,3 +213,34 @@ def test_stream_row_blocks_any_height(cuda_device, N_):
     c = synth.make_case(14, 1, N_, 2048, 4, 128, "packed")
     y = run(c, cuda_device, N.PATH_GEMV)
     assert oracle.rel_l2(y, oracle.managed(c)) <= TOL_FP32
+
+
+@pytest.mark.parametrize("N_,K,bs,zp", [(1000, 4160, 128, "packed"), (384, 2048, 32, "float"), (256, 1024, 64, "none"),
+                                        (4096, 4096, 128, "packed")])
+def test_lazy_gemm_layout_holds_one_copy_and_matches(cuda_device, N_, K, bs, zp):
+    """MSQ_PACK_LAZY_GEMM: the handle holds the decode stream only (<= 1.1x the reference's
+    bytes), decodes exactly as before, and the GEMM layout it derives from the stream at its
+    first GEMM call gives the eagerly packed handle's GEMM output bit for bit."""
+    c = synth.make_case(44, 64, N_, K, 4, bs, zp, scale_lo=0.001, scale_hi=0.01)
+    lazy = QuantizedWeights(c["b"], c["scales"], c["zp"], N_, K, 4, bs, device=cuda_device, lazy_gemm=True)
+    eager = pack(c, cuda_device)
+    alg = synth.algorithmic_bytes(N_, K, 4, bs, zp)
+    assert lazy.query_device_bytes() <= 1.1 * alg, (lazy.query_device_bytes(), alg)
+    assert eager.query_device_bytes() > 1.5 * alg
+    a = torch.from_numpy(c["a"]).to(cuda_device)
+    y1 = lazy.matmul(a[:1])
+    assert N.last_path() == "gemv_imma"
+    assert torch.equal(y1, eager.matmul(a[:1]))
+    # the no-allocation entry refuses the handle before its GEMM layout exists
+    yy = torch.empty(64, N_, device=cuda_device)
+    with torch.cuda.device(cuda_device):
+        rc = N.lib().msq_matmul_noalloc(None, torch.cuda.current_stream(cuda_device).cuda_stream, lazy.handle,
+                                        a.data_ptr(), N.DT_F32, 64, yy.data_ptr(), N_)
+    assert rc == N.MSQ_E_UNSUPPORTED and "LAZY_GEMM" in N.last_error()
+    for path in (N.PATH_GEMM, N.PATH_GEMM_SPLIT):
+        assert torch.equal(lazy.matmul(a, path=path), eager.matmul(a, path=path))
+    torch.cuda.synchronize()
+    assert lazy.query_device_bytes() == eager.query_device_bytes()
+    assert oracle.rel_l2(lazy.matmul(a).cpu().numpy(), oracle.managed(c)) <= TOL_TC
+    lazy.free()
+    eager.free()

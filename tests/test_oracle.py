@@ -4,7 +4,10 @@
   tests/golden/kat_matmulnbits.json) within the file's own 1e-4 absolute tolerance;
 * the reference's native ms_qgemm_nbits outputs on seeded cases (tests/golden/ref_native.npz,
   written by tests/golden/make_golden.py) at rel-L2 <= 1e-6;
-* the generator still produces the inputs those outputs were computed from.
+* the generator still produces the inputs those outputs were computed from;
+* the restatement of the reference's int8-activation ms_qgemm_w4a8 against that kernel's own
+  outputs (tests/golden/ref_w4a8.npz) at rel-L2 <= 1e-6 (the integer parts are exact; only the
+  fp32 order of the per-block sum differs from the reference's vectorised loop).
 """
 import json
 from pathlib import Path
@@ -78,3 +81,22 @@ def test_oracle_ignores_codes_past_k():
     c4 = dict(c3)
     c4["zp"] = z
     np.testing.assert_array_equal(oracle.managed(c4), y3)
+
+
+W4A8 = np.load(GOLD / "ref_w4a8.npz")
+
+
+@pytest.mark.parametrize("i", cases.W4A8_CASES)
+def test_w4a8_restatement_matches_reference_outputs(i):
+    c = cases.qgemm_case(i)
+    ref = W4A8[f"qgemm{i}"]
+    got = oracle.w4a8(c)
+    assert oracle.rel_l2(got, ref) <= 1e-6
+    assert oracle.rel_l2(got, oracle.managed(c)) > 1e-4  # approximate: activations quantised to int8
+
+
+@pytest.mark.skipif(not oracle.reference_available(), reason="reference kernel not built here")
+def test_w4a8_reference_live():
+    for i in cases.W4A8_CASES[::5]:
+        c = cases.qgemm_case(i)
+        np.testing.assert_array_equal(oracle.reference_w4a8(c), W4A8[f"qgemm{i}"])
