@@ -57,7 +57,7 @@ WORKLOAD = ("7B decode GEMV sweep (BASELINE configs[1]) at M=1: (K,N) = (4096,40
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (read + write) per algorithmic byte of the decode GEMV, measured by an ncu
 # capture of one K=4096, N=14336 launch of this bench's sweep.
-NCU_DRAM_PER_ALG_BYTE = 31474688 / 31424512
+NCU_DRAM_PER_ALG_BYTE = 31480832 / 31424512
 
 
 def log(*a):
@@ -681,22 +681,9 @@ def run_nsplit(args, rank: int, world: int, local_rank: int):
     stream.synchronize()
     y_chk = outs[0].float().cpu().numpy()
 
-    dist.barrier() if world > 1 else None
-    torch.cuda.synchronize(dev)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clk:
-        ev0.record(stream)
-        with torch.cuda.stream(stream):
-            for i in range(args.steps):
-                graphs[i % reps_n].replay()
-        ev1.record(stream)
-        torch.cuda.synchronize(dev)
-    dist.barrier() if world > 1 else None
-    ms = ev0.elapsed_time(ev1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        wins = timed_windows(args, world, dev, stream, lambda i: graphs[i % reps_n].replay())
+    ms, spread = window_stats(wins)
     value = nbytes * args.steps / (ms * 1e-3) / 1e9
 
     # e2e through the sharded op with host buffers: A in, the down-proj Y out, every step
@@ -767,7 +754,7 @@ def run_nsplit(args, rank: int, world: int, local_rank: int):
                                   "Y over NVLink and signal completion" if gather == "p2p" else
                                   f"one CUDA graph replay per step: {per_step_launches} library launches "
                                   f"({'tensor-core GEMM' if M >= 17 else 'decode GEMV'}) + 2 NCCL all-gathers"),
-                       "gather": gather, "flops_per_step": flops,
+                       "gather": gather, "flops_per_step": flops, "timing": spread,
                        "tflops": flops / (ms / args.steps * 1e-3) / 1e12,
                        "parity_rel_l2": parity},
             "roofline": roof,
