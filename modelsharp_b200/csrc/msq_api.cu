@@ -185,6 +185,7 @@ int pack_impl(cudaStream_t st, const uint8_t* d_b, int64_t b_len, const void* d_
   w->zp_row_bytes = (w->nb * bits + 7) / 8;
   w->zp_kind = zp_dtype == MSQ_DT_U8 ? ZP_PACKED : zp_dtype == MSQ_DT_F32 ? ZP_F32 : ZP_NONE;
   w->fast4 = bits == 4 && bs >= 32 && pow2(bs) && !(flags & MSQ_PACK_GENERIC_ONLY);
+  w->fast8 = bits == 8 && (bs == 32 || bs == 64 || bs == 128) && !(flags & MSQ_PACK_GENERIC_ONLY);
 
   const size_t rows = (size_t)w->n_rows;
   if (w->fast4) {
@@ -204,6 +205,10 @@ int pack_impl(cudaStream_t st, const uint8_t* d_b, int64_t b_len, const void* d_
     plan_stream(*w);
     if (rc == MSQ_OK)
       rc = dev_alloc(&w->strm, (size_t)w->nblk * w->ntiles * w->stage_bytes, &w->device_bytes);
+    if (rc == MSQ_OK) rc = repack_stream(st, *w, d_b, n_begin, d_scales, scales_dtype, d_zp);
+  } else if (w->fast8) {
+    plan_stream(*w);
+    rc = dev_alloc(&w->strm, (size_t)w->nblk * w->ntiles * w->stage_bytes, &w->device_bytes);
     if (rc == MSQ_OK) rc = repack_stream(st, *w, d_b, n_begin, d_scales, scales_dtype, d_zp);
   } else {
     rc = dev_alloc(&w->b_ref, rows * (size_t)w->nb * w->blob, &w->device_bytes);
@@ -263,7 +268,8 @@ int matmul_impl(cudaStream_t st, Weights* w, const void* d_a, int a_dtype, int64
     return fail(MSQ_E_INVALID, "weights handle lives on device %d but the current device is %d", w->device, dev);
   refresh_settled(*w, st);
   if (path == MSQ_PATH_AUTO || path == MSQ_PATH_AUTO_SPLIT) {
-    if (!w->fast4) path = MSQ_PATH_GENERIC;
+    if (!w->fast4 && !w->fast8) path = MSQ_PATH_GENERIC;
+    else if (w->fast8) path = MSQ_PATH_GEMV;
     else if (M >= 17 && w->K >= 64) path = path == MSQ_PATH_AUTO ? MSQ_PATH_GEMM : MSQ_PATH_GEMM_SPLIT;
     else path = MSQ_PATH_GEMV;
   }

@@ -27,6 +27,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 namespace msq {
@@ -51,10 +52,13 @@ struct Plan {
   static constexpr int kTmaWarp = kDeq;
   static constexpr int kMmaWarp = kDeq + 1;
   // what fits in 227 KB (SPLIT: TM <= 2)
-  static constexpr int kStages = SPLIT ? (TM == 1 ? 3 : 2) : (TM == 1 ? 4 : TM == 2 ? 3 : 2);
+  static constexpr int kStages = SPLIT ? (TM == 1 ? 3 : 2) : (TM == 1 ? 4 : TM == 2 || TM == 3 ? 3 : 2);
   static constexpr int kAPart = kRows * BK * 2;       // one fp16 activation tile: 16 / 32 / 64 KB
   static constexpr int kABytes = kAPart * kParts;     // hi tile, then lo tile
-  static constexpr int kABoxes = kRows > 256 ? kRows / 256 : 1;  // activation TMA boxes per part
+  // activation TMA boxes per part: 256-row boxes, or 128-row ones when the tile is not a
+  // multiple of 256 rows (TM = 1, 3)
+  static constexpr int kABoxes = kRows % 256 == 0 ? kRows / 256 : kRows / 128;
+  static constexpr int kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128 : kCols <= 256 ? 256 : 512;
   static constexpr int kBPart = BN * BK * 2;          // one dequantised fp16 weight tile
   static constexpr int kBBytes = kBPart * kParts;
   static constexpr int kPBytes = BN * BK / 2;         // packed int4 weights
@@ -168,7 +172,7 @@ __global__ void __launch_bounds__(Plan<TM, BN, SPLIT>::kThreads, 1)
     ptx::fence_mbar_init();
   }
   if (warp == kMmaWarp) {
-    ptx::tmem_alloc(tmem_slot, PL::kCols);
+    ptx::tmem_alloc(tmem_slot, PL::kTmemCols);
     ptx::tmem_relinquish();
   }
   if (warp == kTmaWarp && lane == 0) {
@@ -373,7 +377,7 @@ __global__ void __launch_bounds__(Plan<TM, BN, SPLIT>::kThreads, 1)
   __syncthreads();
   if (warp == kMmaWarp) {
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem, PL::kCols);
+    ptx::tmem_dealloc(tmem, PL::kTmemCols);
   }
 }
 
@@ -535,11 +539,16 @@ int choose_splits(int ctas, int sms, int ksteps, int64_t M, int64_t ldw) {
 int launch_gemm(cudaStream_t st, const Weights& w, const WeightMaps& m128, const void* a16, int64_t lda,
                 const float* row_scale, int64_t M, float* d_y, int64_t ldy, bool allow_split,
                 bool operand_split = false, bool a_lo = false) {
-  const int tm = M >= 4 * BM && !operand_split ? 4 : M > BM ? 2 : 1;
+  int tm = M >= 4 * BM && !operand_split ? 4 : M > BM ? 2 : 1;
+  static const int tm_env = [] {
+    const char* e = getenv("MSQ_GEMM_TM");
+    return e && *e ? atoi(e) : 0;
+  }();
+  if (tm_env >= 1 && tm_env <= 4 && !operand_split && M > BM) tm = tm_env;
   const int rows = tm * BM;
   CUtensorMap tmA;
   int rc = make_map_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, const_cast<void*>(a16), (uint64_t)w.K,
-                       (uint64_t)M * (a_lo ? 2 : 1), (uint64_t)lda * 2, BK, std::min(rows, 256),
+                       (uint64_t)M * (a_lo ? 2 : 1), (uint64_t)lda * 2, BK, rows % 256 == 0 ? 256 : 128,
                        CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != MSQ_OK) return rc;
   GemmArgs g{};
@@ -573,6 +582,7 @@ int launch_gemm(cudaStream_t st, const Weights& w, const WeightMaps& m128, const
                  : launch_zp<1, 128, true>(st, w.zp_kind, tmA, m128, g, grid);
   else
     rc = tm == 4   ? launch_zp<4, 128>(st, w.zp_kind, tmA, m128, g, grid)
+         : tm == 3 ? launch_zp<3, 128>(st, w.zp_kind, tmA, m128, g, grid)
          : tm == 2 ? launch_zp<2, 128>(st, w.zp_kind, tmA, m128, g, grid)
                    : launch_zp<1, 128>(st, w.zp_kind, tmA, m128, g, grid);
   if (rc == MSQ_OK && splits > 1) {
@@ -586,12 +596,14 @@ int launch_gemm(cudaStream_t st, const Weights& w, const WeightMaps& m128, const
   }
   scratch_free(ws, st);
   if (rc == MSQ_OK) {
-    static const char* names[2][2][3] = {
-        {{"gemm_tc_m128_n128", "gemm_tc_m256_n128", "gemm_tc_m512_n128"},
-         {"gemm_tc_m128_n128_splitk", "gemm_tc_m256_n128_splitk", "gemm_tc_m512_n128_splitk"}},
-        {{"gemm_tc_x3_m128_n128", "gemm_tc_x3_m256_n128", "gemm_tc_x3_m512_n128"},
-         {"gemm_tc_x3_m128_n128_splitk", "gemm_tc_x3_m256_n128_splitk", "gemm_tc_x3_m512_n128_splitk"}}};
-    note_path(names[operand_split ? 1 : 0][splits > 1 ? 1 : 0][tm == 4 ? 2 : tm == 2 ? 1 : 0]);
+    static const char* names[2][2][4] = {
+        {{"gemm_tc_m128_n128", "gemm_tc_m256_n128", "gemm_tc_m384_n128", "gemm_tc_m512_n128"},
+         {"gemm_tc_m128_n128_splitk", "gemm_tc_m256_n128_splitk", "gemm_tc_m384_n128_splitk",
+          "gemm_tc_m512_n128_splitk"}},
+        {{"gemm_tc_x3_m128_n128", "gemm_tc_x3_m256_n128", "gemm_tc_x3_m384_n128", "gemm_tc_x3_m512_n128"},
+         {"gemm_tc_x3_m128_n128_splitk", "gemm_tc_x3_m256_n128_splitk", "gemm_tc_x3_m384_n128_splitk",
+          "gemm_tc_x3_m512_n128_splitk"}}};
+    note_path(names[operand_split ? 1 : 0][splits > 1 ? 1 : 0][tm - 1]);
   }
   return rc;
 }

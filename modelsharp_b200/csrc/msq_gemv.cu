@@ -264,7 +264,13 @@ inline int rows_per_warp(int mr) { return mr <= 2 ? 4 : (mr == 4 ? 2 : 1); }
 
 int run_gemv(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M,
              float* d_y, int64_t ldy) {
-  if (!w.fast4) return fail(MSQ_E_UNSUPPORTED, "GEMV path needs bits=4 and a power-of-two block_size >= 32");
+  if (w.fast8) {
+    if (M <= 0) return MSQ_OK;
+    const int rc = run_gemv_mma(st, w, d_a, a_dtype, M, d_y, ldy);
+    if (rc == MSQ_E_UNSUPPORTED) return fail(rc, "bits=8 decode GEMV: shape not supported");
+    return rc;
+  }
+  if (!w.fast4) return fail(MSQ_E_UNSUPPORTED, "GEMV path needs bits=4 (or bits=8) and a power-of-two block_size >= 32");
   if (M <= 0) return MSQ_OK;
   const int sms = num_sms(w.device);
   const int mr = M == 1 ? 1 : M == 2 ? 2 : M <= 4 ? 4 : 8;

@@ -202,21 +202,29 @@ __device__ __forceinline__ float exp2i(int s) { return __int_as_float((s + 127) 
 
 // W[row, k] = (q - zp) * s in fp32, read back from the stream records in global memory
 // (layout in msq_internal.cuh): the slow path of rows of A that hold inf or NaN.
-template <int BS>
+template <int BS, bool B8>
 __device__ float stream_weight(const Args& p, int64_t row, int k) {
   const int64_t b = row >> 4;
   const int r = (int)(row & 15);
   const int t = k / p.kt, kk = k - t * p.kt;
   const uint8_t* rec = p.strm + (b * p.ntiles + t) * (int64_t)p.stage_bytes;
   const int o = kk & 63;
-  const int word = (o >> 5) * 2 + ((o >> 4) & 1);
   const int ln = (r & 7) * 4 + ((o & 15) >> 2);
-  const uint8_t v = rec[(kk >> 6) * 512 + ln * 16 + word * 4 + (o & 3)];
-  const int q = r < 8 ? (v & 0xF) : (v >> 4);
+  int q;
+  if constexpr (B8) {  // word (step, k half, row half) of 8 per lane, one byte per code
+    const int word = (o >> 5) * 4 + ((o >> 4) & 1) * 2 + (r >> 3);
+    q = rec[(kk >> 6) * 1024 + ln * 32 + word * 4 + (o & 3)];
+  } else {
+    const int word = (o >> 5) * 2 + ((o >> 4) & 1);
+    const uint8_t v = rec[(kk >> 6) * 512 + ln * 16 + word * 4 + (o & 3)];
+    q = r < 8 ? (v & 0xF) : (v >> 4);
+  }
   const int bl = kk / BS;
   const float sc = reinterpret_cast<const float*>(rec + p.off_sc)[bl * 16 + r];
-  float z = 8.f;
-  if (p.zp_kind == ZP_PACKED)
+  float z = B8 ? 128.f : 8.f;
+  if (p.zp_kind == ZP_PACKED && B8)
+    z = (float)rec[p.off_zp + bl * 16 + r];
+  else if (p.zp_kind == ZP_PACKED)
     z = (float)((reinterpret_cast<const unsigned long long*>(rec + p.off_zp)[bl] >> (4 * r)) & 0xF);
   else if (p.zp_kind == ZP_F32)
     z = reinterpret_cast<const float*>(rec + p.off_zp)[bl * 16 + r];
@@ -226,14 +234,14 @@ __device__ float stream_weight(const Args& p, int64_t row, int k) {
 // Sum over the k where A row m is inf or NaN of a[m, k] * W[row, k] in fp32: inf, -inf or NaN
 // exactly as the reference's fp32 sum gets them (a NaN term, inf * 0 or inf - inf give NaN),
 // which is what the row's output then is.
-template <int BS, bool FU>
+template <int BS, bool FU, bool B8>
 __device__ float nonfinite_terms(const Args& p, int m, int64_t row) {
   const int64_t base = (p.m0 + m) * (FU ? p.lda : (int64_t)p.K);
   float t = 0.f;
   for (int k = 0; k < p.K; ++k) {
     float a = load_act(p.a, p.a_dtype, base + k);
     if (FU && p.swiglu) a = silu_mul(a, load_act(p.a, p.a_dtype, base + p.K + k));
-    if (!(fabsf(a) <= 3.402823466e38f)) t += a * stream_weight<BS>(p, row, k);
+    if (!(fabsf(a) <= 3.402823466e38f)) t += a * stream_weight<BS, B8>(p, row, k);
   }
   return t;
 }
@@ -245,9 +253,12 @@ __device__ float nonfinite_terms(const Args& p, int m, int64_t row) {
 // A8 = the int8-activation form (ms_qgemm_w4a8's arithmetic, native/src/qgemm_w4a8.cpp:247-292,
 // 622-690): per (A row, block) s_a = max|a| / 127 and aq = rint(a / s_a) in [-127, 127], one s8
 // B column per A row, the block's exact integer dot aq . (q - zp) and y += (s_a s_w) dot.
-template <int BS, int NT, bool XG, bool FU, bool A8 = false>
+// B8 = 8-bit weight codes (MatMulNBits bits=8): the record's code words are the u8 A-fragment
+// registers themselves (no nibble split, no 16x high-nibble rows), default zero point 128.
+template <int BS, int NT, bool XG, bool FU, bool A8 = false, bool B8 = false>
 __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
   static_assert(!(XG && FU), "the column-split form takes no fusion");
+  static_assert(!B8 || (!XG && !FU && !A8), "8-bit codes take the plain form");
   static_assert(!A8 || (!XG && !FU && NT == 1), "the int8-activation form is plain, 8 rows per pass");
   constexpr int UNIT = BS > 64 ? BS : 64;
   constexpr int CH = UNIT / 64;     // 64-k chunks per unit
@@ -488,10 +499,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
           // the zero-point term rides on the lanes of digits 0 and 1 (even tq) only; every
           // factor below is the block scale times a power of two, so the products are exact
           sv[uu][bl][nt] = okb && (tq & 1) == 0 ? (float)sblk[m * nbp + kk0 / BS + bl] : 0.f;
-          sv16[uu][bl][nt] = 16.f * sv[uu][bl][nt];
+          sv16[uu][bl][nt] = (B8 ? 1.f : 16.f) * sv[uu][bl][nt];
           const float g = okb ? sinv[m * nbp + kk0 / BS + bl] : 0.f;
           gw0[uu][bl][nt] = g * wdig;
-          gw1[uu][bl][nt] = g * wdig * 0.0625f;
+          gw1[uu][bl][nt] = B8 ? g * wdig : g * wdig * 0.0625f;
         }
     }
 
@@ -504,20 +515,36 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
         // Both units of this warp as independent chains, each block's k32 steps split over
         // two accumulators, so the tensor-core latency overlaps; a missing second unit
         // (kt < 32 units) reads unit 0's words and contributes nothing (its gw0 and gw1 are 0).
-        uint32_t wv[UPW][4 * CH];
+        uint32_t wv[UPW][(B8 ? 8 : 4) * CH];
         float s0[UPW][UB], s1[UPW][UB], z0[UPW][UB], z1[UPW][UB];
 #pragma unroll
         for (int uu = 0; uu < UPW; ++uu) {
           const int u = warp + uu * kConsumers;
           const int ul = u < units ? u : 0;  // unit 0 always exists in a stage
-          const uint4* nib = reinterpret_cast<const uint4*>(base) + ul * CH * 32 + lane;
+          if constexpr (B8) {
+            const uint4* cw = reinterpret_cast<const uint4*>(base) + ul * CH * 64 + 2 * lane;
 #pragma unroll
-          for (int c = 0; c < CH; ++c) {
-            const uint4 q4 = nib[c * 32];
-            wv[uu][4 * c + 0] = q4.x;
-            wv[uu][4 * c + 1] = q4.y;
-            wv[uu][4 * c + 2] = q4.z;
-            wv[uu][4 * c + 3] = q4.w;
+            for (int c = 0; c < CH; ++c) {
+              const uint4 q0 = cw[c * 64], q1 = cw[c * 64 + 1];
+              wv[uu][8 * c + 0] = q0.x;
+              wv[uu][8 * c + 1] = q0.y;
+              wv[uu][8 * c + 2] = q0.z;
+              wv[uu][8 * c + 3] = q0.w;
+              wv[uu][8 * c + 4] = q1.x;
+              wv[uu][8 * c + 5] = q1.y;
+              wv[uu][8 * c + 6] = q1.z;
+              wv[uu][8 * c + 7] = q1.w;
+            }
+          } else {
+            const uint4* nib = reinterpret_cast<const uint4*>(base) + ul * CH * 32 + lane;
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+              const uint4 q4 = nib[c * 32];
+              wv[uu][4 * c + 0] = q4.x;
+              wv[uu][4 * c + 1] = q4.y;
+              wv[uu][4 * c + 2] = q4.z;
+              wv[uu][4 * c + 3] = q4.w;
+            }
           }
 #pragma unroll
           for (int bl = 0; bl < UB; ++bl) {
@@ -525,7 +552,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
             s0[uu][bl] = scp[blk_local * 16 + grp];
             s1[uu][bl] = scp[blk_local * 16 + grp + 8];
             // z1 is for the high-nibble rows, whose products come out 16x (sv16 carries the 16)
-            if (p.zp_kind == ZP_PACKED) {
+            if (B8 && p.zp_kind == ZP_PACKED) {
+              const uint8_t* zb = base + p.off_zp + blk_local * 16;
+              z0[uu][bl] = (float)zb[grp];
+              z1[uu][bl] = (float)zb[grp + 8];
+            } else if (p.zp_kind == ZP_PACKED) {
               const uint2 zw = reinterpret_cast<const uint2*>(base + p.off_zp)[blk_local];
               z0[uu][bl] = (float)((zw.x >> (4 * grp)) & 0xF);
               z1[uu][bl] = (float)((zw.y >> (4 * grp)) & 0xF);
@@ -534,8 +565,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
               z0[uu][bl] = zf[blk_local * 16 + grp];
               z1[uu][bl] = zf[blk_local * 16 + grp + 8];
             } else {
-              z0[uu][bl] = 8.f;
-              z1[uu][bl] = 8.f;
+              z0[uu][bl] = B8 ? 128.f : 8.f;
+              z1[uu][bl] = B8 ? 128.f : 8.f;
             }
           }
         }
@@ -555,10 +586,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
 #pragma unroll
             for (int uu = 0; uu < UPW; ++uu) {
               const int st = bl * BSTEPS + q;
-              // rows r+8 keep their codes in the high nibble: 16 q as a u8, exact
-              const uint32_t x0 = wv[uu][2 * st], x1 = wv[uu][2 * st + 1];
-              const uint32_t lo0 = x0 & 0x0F0F0F0Fu, hi0 = x0 & 0xF0F0F0F0u;
-              const uint32_t lo1 = x1 & 0x0F0F0F0Fu, hi1 = x1 & 0xF0F0F0F0u;
+              uint32_t lo0, hi0, lo1, hi1;
+              if constexpr (B8) {  // the record words are the fragment registers
+                lo0 = wv[uu][4 * st];
+                hi0 = wv[uu][4 * st + 1];
+                lo1 = wv[uu][4 * st + 2];
+                hi1 = wv[uu][4 * st + 3];
+              } else {
+                // rows r+8 keep their codes in the high nibble: 16 q as a u8, exact
+                const uint32_t x0 = wv[uu][2 * st], x1 = wv[uu][2 * st + 1];
+                lo0 = x0 & 0x0F0F0F0Fu;
+                hi0 = x0 & 0xF0F0F0F0u;
+                lo1 = x1 & 0x0F0F0F0Fu;
+                hi1 = x1 & 0xF0F0F0F0u;
+              }
 #pragma unroll
               for (int nt = 0; nt < NT; ++nt)
                 imma(c[uu][bl][q & 1][nt], lo0, hi0, lo1, hi1, bf[uu][st][nt][0], bf[uu][st][nt][1]);
@@ -664,7 +705,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
         if (!A8 && nonfin[m]) {
           // RMSNorm of a row holding inf / NaN is NaN everywhere (inf / inf, 0 * inf)
           if (FU && p.gamma) acc = __int_as_float(0x7FC00000);
-          else acc += nonfinite_terms<BS, FU>(p, m, row);
+          else acc += nonfinite_terms<BS, FU, B8>(p, m, row);
         }
         if constexpr (XG) {
           for (int r = 0; r < p.nranks; ++r) p.gy[r][(p.m0 + m) * p.gldy + p.gcol0 + row] = acc;
@@ -709,9 +750,9 @@ __global__ void wait_gathered_kernel(const unsigned long long* arr, const unsign
   if (threadIdx.x == 0) wait_arrivals(arr, prod, nranks);
 }
 
-template <int BS, int NT, bool XG, bool FU, bool A8 = false>
+template <int BS, int NT, bool XG, bool FU, bool A8 = false, bool B8 = false>
 int launch(cudaStream_t st, const Args& a, int grid, size_t smem) {
-  auto kern = gemv_mma_kernel<BS, NT, XG, FU, A8>;
+  auto kern = gemv_mma_kernel<BS, NT, XG, FU, A8, B8>;
   static ContextOnce configured;
   const int rc = configured.run([&] {
     MSQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax),
@@ -848,7 +889,17 @@ int gemv_impl(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, i
     if (g && mc < M) return fail(MSQ_E_UNSUPPORTED, "msq_matmul_gather: %lld A rows do not fit one pass", (long long)M);
     a.mc = mc;
     int rc;
-    if (a8) {
+    if (w.bits == 8) {
+      if (g || fu || a8) return fail(MSQ_E_UNSUPPORTED, "bits=8 weights take the plain decode GEMV only");
+      switch (w.block_size) {
+        case 32: rc = a.mc <= 2 ? launch<32, 1, false, false, false, true>(st, a, grid, smem)
+                                : launch<32, 2, false, false, false, true>(st, a, grid, smem); break;
+        case 64: rc = a.mc <= 2 ? launch<64, 1, false, false, false, true>(st, a, grid, smem)
+                                : launch<64, 2, false, false, false, true>(st, a, grid, smem); break;
+        default: rc = a.mc <= 2 ? launch<128, 1, false, false, false, true>(st, a, grid, smem)
+                                : launch<128, 2, false, false, false, true>(st, a, grid, smem); break;
+      }
+    } else if (a8) {
       switch (w.block_size) {
         case 32: rc = launch<32, 1, false, false, true>(st, a, grid, smem); break;
         case 64: rc = launch<64, 1, false, false, true>(st, a, grid, smem); break;
@@ -875,6 +926,10 @@ int gemv_impl(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, i
     }
     if (rc != MSQ_OK) return rc;
     m0 += mc;
+  }
+  if (w.bits == 8) {
+    note_path(M <= 4 ? "gemv_imma_b8" : "gemv_imma_b8_multipass");
+    return MSQ_OK;
   }
   note_path(a8 ? (M <= kMaxMA8 ? "gemv_w4a8" : "gemv_w4a8_multipass")
                 : g ? "gemv_imma_gather" : fu ? "gemv_imma_fused" : M <= 4 ? "gemv_imma" : "gemv_imma_multipass");

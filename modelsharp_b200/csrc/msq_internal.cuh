@@ -40,6 +40,9 @@ struct Weights {
   int n_rows = 0, K = 0, bits = 4, block_size = 0, nb = 0, blob = 0, zp_row_bytes = 0;
   int zp_kind = ZP_NONE;
   bool fast4 = false;
+  bool fast8 = false;  // bits = 8, block_size 32 / 64 / 128: the decode stream only, codes one byte
+                       // each in the same fragment order (see strm), zero points one byte per
+                       // (block, row); every M takes the decode GEMV
   int KP = 0;
   uint8_t* nib = nullptr;
   int64_t nib_pitch = 0;

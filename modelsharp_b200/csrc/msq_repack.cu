@@ -87,7 +87,7 @@ __global__ void repack_stream_kernel(const uint8_t* __restrict__ b, const void* 
                                      const void* __restrict__ zp, int zp_kind, int64_t row0, int n_rows, int K,
                                      int bs, int nb, int blob, int zp_row_bytes, int kt, int ntiles,
                                      int stage_words, int off_sc_w, int off_zp_w, uint32_t* __restrict__ out,
-                                     int64_t total_words) {
+                                     int64_t total_words, int bits) {
   const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (idx >= total_words) return;
   const int64_t stage = idx / stage_words;
@@ -97,7 +97,24 @@ __global__ void repack_stream_kernel(const uint8_t* __restrict__ b, const void* 
   const int nbt = kt / bs;
   const int64_t r0 = blk * 16;
   uint32_t val = 0;
-  if (wi < off_sc_w) {
+  if (wi < off_sc_w && bits == 8) {
+    // 8-bit code words: [chunk][lane][8 words] = per 32-k step: (row r, k), (row r+8, k),
+    // (row r, k+16), (row r+8, k+16), byte j = k offset j: the u8 A-fragment registers
+    const int word = wi & 7;
+    const int lane = (wi >> 3) & 31;
+    const int chunk = wi >> 8;
+    const int sub = word & 3;
+    const int64_t rr = r0 + (lane >> 2) + (sub & 1) * 8;
+    const int64_t kb = (int64_t)tile * kt + chunk * 64 + (word >> 2) * 32 + (sub >> 1) * 16 + 4 * (lane & 3);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t k = kb + j;
+      if (k < K && rr < n_rows) {
+        const int64_t bk = k / bs;
+        val |= (uint32_t)b[((row0 + rr) * nb + bk) * (int64_t)blob + (k - bk * bs)] << (8 * j);
+      }
+    }
+  } else if (wi < off_sc_w) {
     // code words: [chunk][lane][4 words] = [32-k step 0: k, k+16][step 1: k, k+16]
     const int word = wi & 3;
     const int lane = (wi >> 2) & 31;
@@ -121,6 +138,18 @@ __global__ void repack_stream_kernel(const uint8_t* __restrict__ b, const void* 
     const int64_t rr = r0 + row;
     const int64_t bl = (int64_t)tile * nbt + j;
     if (rr < n_rows && bl < nb) val = __float_as_uint(load_scale(scales, sdt, (row0 + rr) * nb + bl));
+  } else if (zp_kind == ZP_PACKED && bits == 8) {
+    // 8-bit packed: [block][16 bytes, byte = row]
+    const int r = wi - off_zp_w;
+    const int j = r >> 2, q0 = (r & 3) * 4;
+    if (j < nbt) {
+      const int64_t bl = (int64_t)tile * nbt + j;
+      for (int q = 0; q < 4; ++q) {
+        const int64_t rr = r0 + q0 + q;
+        if (rr < n_rows && bl < nb)
+          val |= (uint32_t)static_cast<const uint8_t*>(zp)[(row0 + rr) * zp_row_bytes + bl] << (8 * q);
+      }
+    }
   } else if (zp_kind == ZP_PACKED) {
     // packed: [block][2 words of 8 nibbles, nibble = row]
     const int r = wi - off_zp_w;
@@ -186,7 +215,8 @@ int repack_fast4(cudaStream_t st, Weights& w, const uint8_t* d_b, int n_begin,
 void plan_stream(Weights& w) {
   const int K = w.K, bs = w.block_size;
   const int unit = bs > 64 ? bs : 64;
-  const int kt_max = std::max(unit, (unit == 64 ? 2048 : 4096) / unit * unit);
+  // stages of 16-35 KB: half the k per tile for 8-bit codes
+  const int kt_max = std::max(unit, (unit == 64 ? 2048 : 4096) / (w.bits == 8 ? 2 : 1) / unit * unit);
   const int units = (K + unit - 1) / unit;
   int best = 1;
   for (int d = 1; d * unit <= kt_max; ++d)
@@ -197,9 +227,9 @@ void plan_stream(Weights& w) {
   w.ntiles = (K + kt - 1) / kt;
   w.nblk = (w.n_rows + 15) / 16;
   const int nbt = kt / bs;
-  const int nib = 16 * kt / 2;
+  const int nib = 16 * kt * w.bits / 8;
   const int sc = nbt * 16 * 4;
-  const int zpb = w.zp_kind == ZP_PACKED ? nbt * 8 : w.zp_kind == ZP_F32 ? nbt * 64 : 0;
+  const int zpb = w.zp_kind == ZP_PACKED ? nbt * 2 * w.bits : w.zp_kind == ZP_F32 ? nbt * 64 : 0;
   w.off_sc = nib;
   w.off_zp = nib + sc;
   w.stage_bytes = (nib + sc + zpb + 15) / 16 * 16;
@@ -213,7 +243,7 @@ int repack_stream(cudaStream_t st, Weights& w, const uint8_t* d_b, int n_begin, 
   repack_stream_kernel<<<grid_for(total, T), T, 0, st>>>(
       d_b, d_scales, scales_dtype, d_zp, w.zp_kind, n_begin, w.n_rows, w.K, w.block_size, w.nb, w.blob,
       w.zp_row_bytes, w.kt, w.ntiles, stage_words, w.off_sc / 4, w.off_zp / 4,
-      reinterpret_cast<uint32_t*>(w.strm), total);
+      reinterpret_cast<uint32_t*>(w.strm), total, w.bits);
   note_launch();
   MSQ_CUDA_TRY(cudaGetLastError(), "stream repack launch");
   return MSQ_OK;
