@@ -245,42 +245,3 @@ def test_lazy_gemm_layout_holds_one_copy_and_matches(cuda_device, N_, K, bs, zp)
     lazy.free()
     eager.free()
 
-
-@pytest.mark.parametrize("e", [e for e in META["cases"] if e["bits"] == 8 and e["block_size"] in (32, 64, 128)],
-                         ids=lambda e: e["key"])
-def test_golden_gemv_bits8(cuda_device, e):
-    """bits=8 weights on the decode GEMV's 8-bit form against the reference's own ms_qgemm_nbits."""
-    c = golden_case(e["key"])
-    ref = np.load(GOLD / "ref_native.npz")[e["key"]]
-    y = run(c, cuda_device)  # the default route: every M of a bits=8 handle takes the GEMV
-    assert N.last_path().startswith("gemv_imma_b8")
-    assert oracle.rel_l2(y, ref) <= TOL_FP32
-    assert oracle.rel_l2(y, oracle.managed(c)) <= TOL_FP32
-
-
-@pytest.mark.parametrize("M", [1, 3, 4, 7, 16, 40])
-@pytest.mark.parametrize("K,bs,zp_kind", [(4096, 128, "packed"), (1000, 32, "none"), (2048, 64, "float"),
-                                          (4160, 128, "none"), (896, 32, "packed")])
-def test_gemv_bits8(cuda_device, M, K, bs, zp_kind):
-    c = synth.make_case(88, M, 700, K, 8, bs, zp_kind, scale_lo=0.0001, scale_hi=0.001)
-    w = pack(c, cuda_device)
-    assert w.query_device_bytes() <= 1.1 * synth.algorithmic_bytes(700, K, 8, bs, zp_kind)  # one layout
-    y = w.matmul(torch.from_numpy(c["a"]).to(cuda_device)).cpu().numpy()
-    assert N.last_path().startswith("gemv_imma_b8")
-    assert oracle.rel_l2(y, oracle.managed(c)) <= TOL_FP32
-    w.free()
-
-
-def test_gemv_bits8_half_activations_and_nonfinite(cuda_device):
-    c = synth.make_case(89, 3, 512, 2048, 8, 64, "packed", a_dtype="f16", scale_lo=0.0001, scale_hi=0.001)
-    assert oracle.rel_l2(run(c, cuda_device), oracle.managed(c)) <= TOL_FP32
-    a = np.asarray(c["a"], np.float32).copy()
-    a[0, 9] = np.inf
-    a[2, 100] = np.nan
-    cn = dict(c, a=a)
-    y = run(cn, cuda_device)
-    ref = oracle.managed(cn)
-    for f in (np.isnan, np.isposinf, np.isneginf):
-        assert np.array_equal(f(y), f(ref)), f.__name__
-    fin = np.isfinite(ref)
-    assert oracle.rel_l2(y[fin], ref[fin]) <= TOL_FP32
