@@ -27,6 +27,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 namespace msq {
@@ -538,7 +539,12 @@ int choose_splits(int ctas, int sms, int ksteps, int64_t M, int64_t ldw) {
 int launch_gemm(cudaStream_t st, const Weights& w, const WeightMaps& m128, const void* a16, int64_t lda,
                 const float* row_scale, int64_t M, float* d_y, int64_t ldy, bool allow_split,
                 bool operand_split = false, bool a_lo = false) {
-  const int tm = M >= 4 * BM && !operand_split ? 4 : M > BM ? 2 : 1;
+  int tm = M >= 4 * BM && !operand_split ? 4 : M > BM ? 2 : 1;
+  static const int tm_env = [] {
+    const char* e = getenv("MSQ_GEMM_TM");
+    return e && *e ? atoi(e) : 0;
+  }();
+  if (tm_env >= 1 && tm_env <= 4 && !operand_split && M > BM) tm = tm_env;
   const int rows = tm * BM;
   CUtensorMap tmA;
   int rc = make_map_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, const_cast<void*>(a16), (uint64_t)w.K,
@@ -576,6 +582,7 @@ int launch_gemm(cudaStream_t st, const Weights& w, const WeightMaps& m128, const
                  : launch_zp<1, 128, true>(st, w.zp_kind, tmA, m128, g, grid);
   else
     rc = tm == 4   ? launch_zp<4, 128>(st, w.zp_kind, tmA, m128, g, grid)
+         : tm == 3 ? launch_zp<3, 128>(st, w.zp_kind, tmA, m128, g, grid)
          : tm == 2 ? launch_zp<2, 128>(st, w.zp_kind, tmA, m128, g, grid)
                    : launch_zp<1, 128>(st, w.zp_kind, tmA, m128, g, grid);
   if (rc == MSQ_OK && splits > 1) {
