@@ -4,8 +4,8 @@
 //
 // One CTA computes a (128 TM) x BN tile of Y over k-stages of 64: TM accumulators of 128
 // activation rows (TMEM lanes) x BN weight rows (TMEM columns) that share one dequantised
-// weight tile, so each dequantised weight feeds 128 TM rows (BN = 128; TM = 4 for M >= 512,
-// 2 for M > 128, 1 below):
+// weight tile, so each dequantised weight feeds 128 TM rows (BN = 128; TM = 3 or 4 for
+// M >= 512, by whole waves of tiles, 2 for M > 128, 1 below):
 //   TMA warp    per stage: the fp16 activation tile (128 x 64, 128-byte swizzle), the packed
 //               int4 weight tile (BN rows x 32 bytes) and a 16-byte column of scales and of
 //               zero points per weight row covering the stage's blocks, no multicast;
@@ -27,7 +27,6 @@
 #include <cuda.h>
 
 #include <algorithm>
-#include <cstdlib>
 #include <mutex>
 
 namespace msq {
@@ -539,12 +538,18 @@ int choose_splits(int ctas, int sms, int ksteps, int64_t M, int64_t ldw) {
 int launch_gemm(cudaStream_t st, const Weights& w, const WeightMaps& m128, const void* a16, int64_t lda,
                 const float* row_scale, int64_t M, float* d_y, int64_t ldy, bool allow_split,
                 bool operand_split = false, bool a_lo = false) {
-  int tm = M >= 4 * BM && !operand_split ? 4 : M > BM ? 2 : 1;
-  static const int tm_env = [] {
-    const char* e = getenv("MSQ_GEMM_TM");
-    return e && *e ? atoi(e) : 0;
-  }();
-  if (tm_env >= 1 && tm_env <= 4 && !operand_split && M > BM) tm = tm_env;
+  int tm = M > BM ? 2 : 1;
+  if (!operand_split && M >= 4 * BM) {
+    // Three or four accumulators per dequantised weight tile, chosen by whole waves of tiles:
+    // four share each tile over more rows, three fit a 3-deep stage ring instead of 2. Measured
+    // on configs[2] (N = 14336), a three-accumulator tile costs 0.71-0.74 of a four-accumulator
+    // one (M = 2048: 834 against 736 TFLOP/s; M = 8192: 936 against 911; M = 512, one wave of
+    // four against 1.5 of three: 720 against 535).
+    const int64_t gxt = (w.n_rows + 127) / 128, sms = num_sms(w.device);
+    const int64_t waves4 = (gxt * ((M + 4 * BM - 1) / (4 * BM)) + sms - 1) / sms;
+    const int64_t waves3 = (gxt * ((M + 3 * BM - 1) / (3 * BM)) + sms - 1) / sms;
+    tm = 0.72 * (double)waves3 < (double)waves4 ? 3 : 4;
+  }
   const int rows = tm * BM;
   CUtensorMap tmA;
   int rc = make_map_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, const_cast<void*>(a16), (uint64_t)w.K,
