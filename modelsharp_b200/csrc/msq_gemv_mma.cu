@@ -300,6 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
     // and overlaps the previous kernel's tail.
     if (lane == 0) {
       if (!p.prefetch) griddep_wait();
+      const uint64_t pol = ptx::policy_evict_first();  // each record is read once per launch
       int issued = 0, s = 0;
       uint32_t wrap = 0;
       bool ok = true;
@@ -311,8 +312,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
           }
           const int b = blockIdx.x + i * grid;
           ptx::mbar_arrive_expect_tx(&full[s], p.stage_bytes);
-          ptx::bulk_g2s(ring + (size_t)s * p.stage_bytes,
-                        p.strm + ((int64_t)b * T + t) * (int64_t)p.stage_bytes, p.stage_bytes, &full[s]);
+          ptx::bulk_g2s_hint(ring + (size_t)s * p.stage_bytes,
+                             p.strm + ((int64_t)b * T + t) * (int64_t)p.stage_bytes, p.stage_bytes, &full[s], pol);
           ++issued;
           if (++s == p.nslots) {
             s = 0;
