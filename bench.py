@@ -853,22 +853,11 @@ def run_prefill(args, rank: int, world: int, local_rank: int):
         per_m.append({"M": PREFILL_MS[mi], "us": us, "TFLOP/s": 2.0 * PREFILL_MS[mi] * PREFILL_N * PREFILL_K / us / 1e6})
         del g
 
-    dist.barrier() if world > 1 else None
-    torch.cuda.synchronize(dev)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # timed like the sweep: windows of exactly --steps graph replays, the median window
     with ClockSampler(local_rank) as clk:
-        ev0.record(stream)
-        with torch.cuda.stream(stream):
-            for i in range(args.steps):
-                graphs[i % reps_n].replay()
-        ev1.record(stream)
-        torch.cuda.synchronize(dev)
-    dist.barrier() if world > 1 else None
-    ms = ev0.elapsed_time(ev1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        wins = timed_windows(argparse.Namespace(windows=getattr(args, "windows", 30), steps=args.steps), world, dev,
+                             stream, lambda i: graphs[i % reps_n].replay())
+    ms, spread = window_stats(wins)
     value = world * flops * args.steps / (ms * 1e-3) / 1e12
 
     # e2e: host A in (fp16), Y out (fp32) through msq_matmul_host, every step
@@ -934,7 +923,7 @@ def run_prefill(args, rank: int, world: int, local_rank: int):
             "config": {"workload": PREFILL_WORKLOAD, "flops_per_step": flops, "parallelism": f"replicas{world}",
                        "l2": f"{reps_n} weight replicas rotate; A up to {8192 * PREFILL_K * 2 / 1e6:.0f} MB",
                        "launch": "one CUDA graph replay per step", "kernel_path": path,
-                       "parity_rel_l2_sampled_rows": max(par)},
+                       "parity_rel_l2_sampled_rows": max(par), "timing": spread},
             "roofline": {"bound": "tensor", "achieved": value / world, "peak": peak, "unit": "TFLOP/s",
                          "frac": value / world / peak, "traffic": None,
                          "peak_source": peak_src, "per_M": per_m},

@@ -69,7 +69,7 @@ struct Plan {
   static constexpr int kOffS = kOffP + kStages * kPBytes;
   static constexpr int kOffZ = kOffS + kStages * kSBytes;
   static constexpr int kOffBar = kOffZ + kStages * kZBytes;
-  static constexpr int kBarBytes = (3 * kStages + 1) * 8 + 16;
+  static constexpr int kBarBytes = (4 * kStages + 1) * 8 + 16;
   static constexpr int kSmem = kOffBar + kBarBytes + 1024;  // + alignment slack
 };
 
@@ -147,8 +147,11 @@ __global__ void __launch_bounds__(Plan<TM, BN, SPLIT>::kThreads, 1)
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + PL::kOffBar);
-  uint64_t* wready = full + S;
+  // afull: the stage's activation tile landed (the MMA waits for it); pfull: its codes, scales
+  // and zero points landed (the dequant warps wait only for these, not for the larger A tile)
+  uint64_t* afull = reinterpret_cast<uint64_t*>(smem + PL::kOffBar);
+  uint64_t* pfull = afull + S;
+  uint64_t* wready = pfull + S;
   uint64_t* empty = wready + S;
   uint64_t* accum = empty + S;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
@@ -162,7 +165,8 @@ __global__ void __launch_bounds__(Plan<TM, BN, SPLIT>::kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&afull[s], 1);
+      ptx::mbar_init(&pfull[s], 1);
       ptx::mbar_init(&wready[s], kDeqWarps);
       ptx::mbar_init(&empty[s], 1);
     }
@@ -195,35 +199,38 @@ __global__ void __launch_bounds__(Plan<TM, BN, SPLIT>::kThreads, 1)
         // scales / zero points: the 16-byte-aligned column holding the stage's block(s)
         const int blk0 = (kt * BK) >> p.bs_shift;
         const bool lo = SPLIT && p.a_lo_row > 0;
-        ptx::mbar_arrive_expect_tx(&full[s], PL::kAPart * (lo ? 2 : 1) + PL::kPBytes + PL::kSBytes +
-                                                 (ZPK != ZP_NONE ? PL::kZBytes : 0));
+        // the weight side first: it feeds the dequant warps, which the MMA then waits for
+        ptx::mbar_arrive_expect_tx(&pfull[s], PL::kPBytes + PL::kSBytes + (ZPK != ZP_NONE ? PL::kZBytes : 0));
+        ptx::tma_load_2d(smem + PL::kOffP + s * PL::kPBytes, &tmP, &pfull[s], kt * (BK / 2), n0);
+        ptx::tma_load_2d(smem + PL::kOffS + s * PL::kSBytes, &tmS, &pfull[s], SPLIT ? (blk0 & ~3) : (blk0 & ~7), n0);
+        if (ZPK == ZP_PACKED)
+          ptx::tma_load_2d(smem + PL::kOffZ + s * PL::kZBytes, &tmZ, &pfull[s], (blk0 >> 1) & ~15, n0);
+        else if (ZPK == ZP_F32)
+          ptx::tma_load_2d(smem + PL::kOffZ + s * PL::kZBytes, &tmZ, &pfull[s], blk0 & ~3, n0);
+        ptx::mbar_arrive_expect_tx(&afull[s], PL::kAPart * (lo ? 2 : 1));
 #pragma unroll
         for (int h = 0; h < PL::kABoxes; ++h)  // a box is at most 256 rows
-          ptx::tma_load_2d(smem + PL::kOffA + s * PL::kABytes + h * (PL::kAPart / PL::kABoxes), &tmA, &full[s],
+          ptx::tma_load_2d(smem + PL::kOffA + s * PL::kABytes + h * (PL::kAPart / PL::kABoxes), &tmA, &afull[s],
                            kt * BK, m0 + h * (PL::kRows / PL::kABoxes));
         if (lo) {
 #pragma unroll
           for (int h = 0; h < PL::kABoxes; ++h)
             ptx::tma_load_2d(smem + PL::kOffA + s * PL::kABytes + PL::kAPart + h * (PL::kAPart / PL::kABoxes), &tmA,
-                             &full[s], kt * BK, p.a_lo_row + m0 + h * (PL::kRows / PL::kABoxes));
+                             &afull[s], kt * BK, p.a_lo_row + m0 + h * (PL::kRows / PL::kABoxes));
         }
-        ptx::tma_load_2d(smem + PL::kOffP + s * PL::kPBytes, &tmP, &full[s], kt * (BK / 2), n0);
-        ptx::tma_load_2d(smem + PL::kOffS + s * PL::kSBytes, &tmS, &full[s], SPLIT ? (blk0 & ~3) : (blk0 & ~7), n0);
-        if (ZPK == ZP_PACKED)
-          ptx::tma_load_2d(smem + PL::kOffZ + s * PL::kZBytes, &tmZ, &full[s], (blk0 >> 1) & ~15, n0);
-        else if (ZPK == ZP_F32)
-          ptx::tma_load_2d(smem + PL::kOffZ + s * PL::kZBytes, &tmZ, &full[s], blk0 & ~3, n0);
         ++issued;
       }
       for (int s = 0; s < S && s < issued; ++s) {  // drain copies in flight
         const int last = s + (issued - 1 - s) / S * S;
         const unsigned long long t0 = ptx::globaltimer(), budget = ptx::wait_budget_ns();
-        while (!ptx::mbar_try_wait(&full[s], (last / S) & 1)) {
-          if (ptx::globaltimer() - t0 > budget) {
-            atomicCAS(&g_gemm_err, 0, ptx::kErrTimeoutDrain);
-            break;
+        bool timed_out = false;
+        for (uint64_t* bar : {&afull[s], &pfull[s]})
+          while (!timed_out && !ptx::mbar_try_wait(bar, (last / S) & 1)) {
+            if (ptx::globaltimer() - t0 > budget) {
+              atomicCAS(&g_gemm_err, 0, ptx::kErrTimeoutDrain);
+              timed_out = true;
+            }
           }
-        }
       }
     }
   } else if (warp == kMmaWarp) {
@@ -233,7 +240,7 @@ __global__ void __launch_bounds__(Plan<TM, BN, SPLIT>::kThreads, 1)
       for (int i = 0; i < nk && ok; ++i) {
         const int s = i % S;
         const uint32_t u = i / S;
-        ok = wait_abort(&full[s], u & 1, abort_flag, ptx::kErrTimeoutFull) &&
+        ok = wait_abort(&afull[s], u & 1, abort_flag, ptx::kErrTimeoutFull) &&
              wait_abort(&wready[s], u & 1, abort_flag, ptx::kErrTimeoutFull);
         if (!ok) break;
         ptx::tc_fence_after();
@@ -280,7 +287,7 @@ __global__ void __launch_bounds__(Plan<TM, BN, SPLIT>::kThreads, 1)
     for (int i = 0; i < nk; ++i) {
       const int kt = kb + i, s = i % S;
       const uint32_t u = i / S;
-      const bool ok = wait_abort(&full[s], u & 1, abort_flag, ptx::kErrTimeoutFull);
+      const bool ok = wait_abort(&pfull[s], u & 1, abort_flag, ptx::kErrTimeoutFull);
       if (ok) {
         const uint4 w4 = *reinterpret_cast<const uint4*>(smem + PL::kOffP + s * PL::kPBytes + tid * 16);
         const int blk0 = (kt * BK) >> p.bs_shift;

@@ -452,7 +452,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
   }
   ptx::named_bar_sync(1, kConsumers * 32);
 
-  // ---- main loop: tile t outer, this CTA's row blocks inner; warp w takes units w, w+16
+  // ---- main loop: tile t outer, this CTA's row blocks inner. Warp w takes the units whose
+  // index along the whole row is w mod kConsumers: units w0, w0 + 16 of tile t with
+  // w0 = (w - t units) mod 16, so every warp gets the same count over the row even when a tile
+  // holds fewer than 32 units (K = 14336 at block_size 128: 28 per tile, 7 per warp in all).
   const int grp = lane >> 2, tq = lane & 3;
   const float wdig = (tq & 1) ? 65536.f : 1.f;  // weight of this lane's first digit column
   const int units = p.kt / UNIT;
@@ -460,6 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
   int rs = 0;
   uint32_t rph = 0;
   for (int t = 0; t < T; ++t) {
+    const int w0 = ((warp - t * units) % kConsumers + kConsumers) % kConsumers;
     // B fragments of this warp's units (digits of columns grp + 8j), held across row blocks
     uint32_t bf[UPW][STEPS][NT][2];
     float sv[UPW][UB][NT];    // block sums of a_int for this lane's A row(s), 0 on odd lanes
@@ -468,7 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
     float gw1[UPW][UB][NT];   // the same / 16: undoes the 16 q of the high-nibble rows
 #pragma unroll
     for (int uu = 0; uu < UPW; ++uu) {
-      const int u = warp + uu * kConsumers;
+      const int u = w0 + uu * kConsumers;
       const int kk0 = t * p.kt + u * UNIT;
 #pragma unroll
       for (int st = 0; st < STEPS; ++st)
@@ -520,7 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
         float s0[UPW][UB], s1[UPW][UB], z0[UPW][UB], z1[UPW][UB];
 #pragma unroll
         for (int uu = 0; uu < UPW; ++uu) {
-          const int u = warp + uu * kConsumers;
+          const int u = w0 + uu * kConsumers;
           const int ul = u < units ? u : 0;  // unit 0 always exists in a stage
           if constexpr (B8) {
             const uint4* cw = reinterpret_cast<const uint4*>(base) + ul * CH * 64 + 2 * lane;

@@ -78,6 +78,26 @@ def test_prefill_config_m8192_sampled_rows(cuda_device):
     w.free()
 
 
+@pytest.mark.parametrize("M,N_,K,bs", [(1, 4096, 14336, 128), (3, 4096, 14336, 128), (1, 1000, 8960, 32),
+                                        (4, 700, 8960, 64), (6, 300, 8960, 32)])
+def test_gemv_tiles_of_fewer_than_32_units(cuda_device, M, N_, K, bs):
+    """Stream tiles of 28 k-units (K = 14336 at block_size 128, 8960 at 32 / 64), whose units
+    each warp takes by its index along the whole row (w mod 16), so the count per warp differs
+    from tile to tile: the plain and fused decode GEMV against the checker."""
+    c = synth.make_case(75, M, N_, K, 4, bs, "packed", scale_lo=0.001, scale_hi=0.01)
+    w = _weights(c, cuda_device)
+    y = _mm(w, c["a"], cuda_device, path=N.PATH_GEMV)
+    assert oracle.rel_l2(y, oracle.managed(c)) <= TOL_FP32
+    gamma = np.random.default_rng(5).uniform(0.8, 1.2, K).astype(np.float32)
+    yf = torch.zeros(M, N_, device=cuda_device)
+    w.matmul_fused(torch.from_numpy(c["a"]).to(cuda_device), yf, rms_gamma=torch.from_numpy(gamma).to(cuda_device),
+                   rms_eps=1e-5)
+    torch.cuda.synchronize(cuda_device)
+    ref = oracle.managed(dict(c, a=od.rms_norm(c["a"], gamma, 1e-5)))
+    assert oracle.rel_l2(yf.cpu().numpy(), ref) <= TOL_FP32
+    w.free()
+
+
 def _classes_match(y, ref):
     for f in (np.isnan, np.isposinf, np.isneginf):
         assert np.array_equal(f(y), f(ref)), f.__name__

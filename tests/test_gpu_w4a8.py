@@ -40,6 +40,7 @@ def w4a8(w, a, dev):
     (8, 512, 1024, 64, "packed"),     # a full pass of 8 rows
     (13, 300, 2048, 32, "packed"),    # two passes
     (4, 14336, 4096, 128, "packed"),
+    (8, 700, 14336, 128, "packed"),   # 28 k-units per stream tile, 4 tiles
 ])
 def test_w4a8_matches_reference_arithmetic(cuda_device, M, N_, K, bs, zp):
     c = synth.make_case(95, M, N_, K, 4, bs, zp, scale_lo=0.001, scale_hi=0.01)
