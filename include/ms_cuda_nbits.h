@@ -324,6 +324,29 @@ int msq_rope_gqa_decode(void* cu_ctx, void* stream, const float* qkv, int heads,
 /* gate_up = [gate (n) | up (n)]: out = gate / (1 + exp(-gate)) * up.                     */
 int msq_swiglu(void* cu_ctx, void* stream, const float* gate_up, float* out, int64_t n);
 
+/* ---- prompt forms of the glue: S tokens at positions pos0 .. pos0 + S - 1 at once --------
+ * msq_rope_append_rows: qkv [S][(heads + 2 kv_heads) d], unrotated and left unchanged; the
+ * half-split rotary of every token's q heads goes to q_out [S][heads d], of its k heads to cache
+ * rows pos0 + s, and its v heads to the same rows of the value cache (RotaryEmbeddingKernel.cs:
+ * 96-114 per token). pos0 + S <= max_seq.                                                      */
+int msq_rope_append_rows(void* cu_ctx, void* stream, const float* qkv, int64_t S, int64_t pos0,
+                         int heads, int kv_heads, int d, const float* cos_t, const float* sin_t,
+                         float* q_out, float* kcache, float* vcache, int64_t max_seq);
+
+/* Causal attention of a prompt: q [S][heads d] (rotated), keys and values of positions
+ * 0 .. pos0 + S - 1 already in the caches [kv_heads][max_seq][d]; out [S][heads d] with
+ * out[s][h] = softmax over cache rows 0 .. pos0 + s of q[s][h] . k / sqrt(d), times v, head h
+ * reading kv head h / (heads / kv_heads) (GroupQueryAttentionKernel.cs:194-195, 275-312 for
+ * every query token), fp32 throughout. MSQ_E_UNSUPPORTED unless heads / kv_heads <= 8, d is 64
+ * or 128, and q, out and the caches are 16-byte aligned.                                      */
+int msq_gqa_prefill(void* cu_ctx, void* stream, const float* q, const float* kcache,
+                    const float* vcache, int64_t S, int64_t pos0, float* out, int heads,
+                    int kv_heads, int d, int64_t max_seq);
+
+/* Rows of gate_up [rows][2n] = [gate | up]: out [rows][n] = gate / (1 + exp(-gate)) * up.    */
+int msq_swiglu_rows(void* cu_ctx, void* stream, const float* gate_up, float* out, int64_t rows,
+                    int64_t n);
+
 /* *d_idx = the first index of the maximum of x[0..n); *d_pos += 1 when d_pos is not NULL.  */
 int msq_argmax(void* cu_ctx, void* stream, const float* x, int64_t n, int64_t* d_idx, int64_t* d_pos);
 

@@ -98,6 +98,9 @@ SIGNATURES: dict[str, tuple] = {
     "msq_rope_gqa_decode": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i64]),
     "msq_swiglu": (_i32, [_vp, _vp, _vp, _vp, _i64]),
     "msq_argmax": (_i32, [_vp, _vp, _vp, _i64, _vp, _vp]),
+    "msq_rope_append_rows": (_i32, [_vp, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _i64]),
+    "msq_gqa_prefill": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _i32, _i32, _i32, _i64]),
+    "msq_swiglu_rows": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64]),
     "msq_matmul_fused": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, C.POINTER(FusionT)]),
     "msq_qgemm_nbits": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32]),
 }

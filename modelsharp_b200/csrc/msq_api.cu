@@ -852,6 +852,52 @@ int msq_swiglu(void* cu_ctx, void* stream, const float* gate_up, float* out, int
   return run_swiglu(static_cast<cudaStream_t>(stream), gate_up, out, n);
 }
 
+int msq_swiglu_rows(void* cu_ctx, void* stream, const float* gate_up, float* out, int64_t rows, int64_t n) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  if (!gate_up || !out || rows < 1 || n < 1) return fail(MSQ_E_INVALID, "msq_swiglu_rows: NULL pointer or empty");
+  return run_swiglu_rows(static_cast<cudaStream_t>(stream), gate_up, out, rows, n);
+}
+
+int msq_rope_append_rows(void* cu_ctx, void* stream, const float* qkv, int64_t S, int64_t pos0, int heads,
+                         int kv_heads, int d, const float* cos_t, const float* sin_t, float* q_out, float* kcache,
+                         float* vcache, int64_t max_seq) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  if (!qkv || !cos_t || !sin_t || !q_out || !kcache || !vcache)
+    return fail(MSQ_E_INVALID, "msq_rope_append_rows: NULL pointer");
+  if (heads < 1 || kv_heads < 1 || heads % kv_heads || d < 2 || (d & 1) || max_seq < 1 ||
+      ((int64_t)heads + 2 * (int64_t)kv_heads) * d > 0x7fffffff)
+    return fail(MSQ_E_INVALID, "msq_rope_append_rows: heads %d, kv_heads %d, d %d, max_seq %lld", heads, kv_heads, d,
+                (long long)max_seq);
+  if (S < 1 || pos0 < 0 || pos0 + S > max_seq)
+    return fail(MSQ_E_INVALID, "msq_rope_append_rows: %lld tokens from position %lld do not fit a cache of %lld",
+                (long long)S, (long long)pos0, (long long)max_seq);
+  return run_rope_append_rows(static_cast<cudaStream_t>(stream), qkv, S, pos0, heads, kv_heads, d, cos_t, sin_t, q_out,
+                              kcache, vcache, max_seq);
+}
+
+int msq_gqa_prefill(void* cu_ctx, void* stream, const float* q, const float* kcache, const float* vcache, int64_t S,
+                    int64_t pos0, float* out, int heads, int kv_heads, int d, int64_t max_seq) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  if (!q || !kcache || !vcache || !out) return fail(MSQ_E_INVALID, "msq_gqa_prefill: NULL pointer");
+  if (heads < 1 || kv_heads < 1 || heads % kv_heads || d < 1 || max_seq < 1)
+    return fail(MSQ_E_INVALID, "msq_gqa_prefill: heads %d, kv_heads %d, d %d, max_seq %lld", heads, kv_heads, d,
+                (long long)max_seq);
+  if (S < 1 || pos0 < 0 || pos0 + S > max_seq)
+    return fail(MSQ_E_INVALID, "msq_gqa_prefill: %lld tokens from position %lld do not fit a cache of %lld",
+                (long long)S, (long long)pos0, (long long)max_seq);
+  if (heads / kv_heads > 8 || (d != 64 && d != 128) ||
+      ((uintptr_t)q | (uintptr_t)kcache | (uintptr_t)vcache | (uintptr_t)out) & 15)
+    return fail(MSQ_E_UNSUPPORTED,
+                "msq_gqa_prefill: needs heads / kv_heads <= 8, d 64 or 128, and 16-byte aligned q, out and caches "
+                "(heads %d, kv_heads %d, d %d)",
+                heads, kv_heads, d);
+  return run_gqa_prefill(static_cast<cudaStream_t>(stream), q, kcache, vcache, out, S, pos0, heads, kv_heads, d,
+                         max_seq);
+}
+
 int msq_argmax(void* cu_ctx, void* stream, const float* x, int64_t n, int64_t* d_idx, int64_t* d_pos) {
   CtxGuard g(cu_ctx);
   if (g.rc != MSQ_OK) return g.rc;

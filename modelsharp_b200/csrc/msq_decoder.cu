@@ -10,6 +10,9 @@
 //                 rope_append's work for the current token
 //   swiglu        silu(gate) * up
 //   argmax        first index of the maximum; also advances the device-side position
+// and the prompt forms for S tokens at once: rope_append_rows (rotary of S tokens at their
+// positions, k and v to the cache), gqa_prefill (causal grouped-query attention of S queries
+// over the cache), swiglu_rows.
 // Positions are read from device memory so a decode step can be replayed from a CUDA graph.
 // Every launch uses programmatic dependent launch: a kernel waits for its predecessor before
 // reading, and lets the next kernel (typically a MatMulNBits GEMV that prefetches its
@@ -405,6 +408,201 @@ __global__ void swiglu_kernel(const float* __restrict__ gu, float* __restrict__ 
   }
 }
 
+// Rows of gu [rows][2n] = [gate | up] -> out [rows][n] = silu(gate) * up.
+__global__ void swiglu_rows_kernel(const float* __restrict__ gu, float* __restrict__ out, int64_t rows, int64_t n) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t total = rows * n;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / n, c = i - r * n;
+    const float gt = gu[2 * r * n + c];
+    out[i] = gt / (1.0f + expf(-gt)) * gu[2 * r * n + n + c];
+  }
+}
+
+// S tokens of qkv [S][(heads + 2 kv) d] (read only) at positions pos0 + s: the rotated q heads
+// to q_out [S][heads d], the rotated k heads and the v heads to cache rows pos0 + s.
+__global__ void rope_append_rows_kernel(const float* __restrict__ qkv, int64_t S, int64_t pos0, int heads, int kv,
+                                        int d, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                        float* __restrict__ q_out, float* __restrict__ kc, float* __restrict__ vc,
+                                        int64_t max_seq) {
+  pdl_wait();
+  pdl_trigger();
+  const int half = d / 2;
+  const int pairs = (heads + kv) * half;
+  const int per = pairs + kv * d;  // work items of one token
+  const int64_t width = (int64_t)(heads + 2 * kv) * d;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < S * per; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t s = i / per;
+    const int e = (int)(i - s * per);
+    const int64_t pos = pos0 + s;
+    const float* row = qkv + s * width;
+    if (e < pairs) {
+      const int hh = e / half, j = e - hh * half;
+      const float c = cos_t[pos * half + j], sn = sin_t[pos * half + j];
+      const float a = row[(int64_t)hh * d + j], b = row[(int64_t)hh * d + j + half];
+      const float ra = a * c - b * sn, rb = b * c + a * sn;
+      float* dst = hh < heads ? q_out + s * (int64_t)heads * d + (int64_t)hh * d
+                              : kc + ((int64_t)(hh - heads) * max_seq + pos) * d;
+      dst[j] = ra;
+      dst[j + half] = rb;
+    } else {
+      const int v = e - pairs, g = v / d, c = v - g * d;
+      vc[((int64_t)g * max_seq + pos) * d + c] = row[(int64_t)(heads + kv) * d + v];
+    }
+  }
+}
+
+// Causal grouped-query attention of S query tokens (positions pos0 .. pos0 + S - 1) over
+// cache rows 0 .. pos0 + S - 1, fp32 throughout (the reference's softmax attention,
+// GroupQueryAttentionKernel.cs:275-312, applied to every query token of a prompt).
+// Block (x: 16 query tokens, y: kv head g) takes the R = 16 G rows (G query heads of the group
+// x 16 tokens), so each K / V tile of 64 cache rows, staged in shared memory, serves all of them.
+// Thread (rb = tid / 16, cg = tid % 16) owns rows rb G .. rb G + G - 1: their scores against keys
+// cg + 16 j (j < 4) of the tile and their output elements 4 cg + 64 i .. + 3 (i < D / 64), with
+// an online softmax per row (running max m, running sum l, output rescaled by e^(m_old - m_new));
+// the 16 threads of a row group combine maxima and sums by shuffles. Row pitches of D + 4 floats
+// keep the key reads of a quarter warp on distinct banks.
+constexpr int kPfTok = 16;  // query tokens per block
+constexpr int kPfKeys = 64;  // cache rows per tile
+
+template <int G, int D>
+__global__ void __launch_bounds__(256, 1) gqa_prefill_kernel(const float* __restrict__ q, const float* __restrict__ kc,
+                                                          const float* __restrict__ vc, float* __restrict__ out,
+                                                          int64_t S, int64_t pos0, int heads, int64_t max_seq,
+                                                          float scale) {
+  constexpr int R = kPfTok * G, DP = D + 4, PP = kPfKeys + 4, DV = D / 64;
+  extern __shared__ __align__(16) float sm[];
+  float* Qs = sm;                   // [R][DP]
+  float* Ks = Qs + R * DP;          // [kPfKeys][DP]
+  float* Vs = Ks + kPfKeys * DP;    // [kPfKeys][DP]
+  float* Ps = Vs + kPfKeys * DP;    // [R][PP]
+  pdl_wait();
+  pdl_trigger();
+  const int g = blockIdx.y;
+  const int64_t s0 = (int64_t)blockIdx.x * kPfTok;
+  const int tid = threadIdx.x, rb = tid >> 4, cg = tid & 15;
+  const int64_t ldq = (int64_t)heads * D;
+  // row r: query head g G + r / 16 of token s0 + r % 16 (rows past S are zeros, never stored)
+  for (int i = tid; i < R * (D / 4); i += 256) {
+    const int r = i / (D / 4), c4 = i - r * (D / 4);
+    const int64_t s = s0 + (r & 15);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (s < S) v = *reinterpret_cast<const float4*>(q + s * ldq + (int64_t)(g * G + (r >> 4)) * D + 4 * c4);
+    *reinterpret_cast<float4*>(Qs + r * DP + 4 * c4) = v;
+  }
+  float m[G], l[G];
+  float4 o[G][DV];
+#pragma unroll
+  for (int i = 0; i < G; ++i) {
+    m[i] = -INFINITY;
+    l[i] = 0.f;
+#pragma unroll
+    for (int v = 0; v < DV; ++v) o[i][v] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const int64_t pmax = pos0 + min(s0 + kPfTok, S) - 1;  // the last position a row of this block sees
+  const int ntile = (int)(pmax / kPfKeys) + 1;
+  const float* kg = kc + (int64_t)g * max_seq * D;
+  const float* vg = vc + (int64_t)g * max_seq * D;
+  for (int t = 0; t < ntile; ++t) {
+    const int64_t k0 = (int64_t)t * kPfKeys;
+    __syncthreads();  // the previous tile's K, V and P are no longer read (and Q is in place)
+    for (int i = tid; i < kPfKeys * (D / 4); i += 256) {
+      const int kr = i / (D / 4), c4 = i - kr * (D / 4);
+      float4 kv4 = make_float4(0.f, 0.f, 0.f, 0.f), vv4 = kv4;
+      if (k0 + kr <= pmax) {
+        kv4 = *reinterpret_cast<const float4*>(kg + (k0 + kr) * D + 4 * c4);
+        vv4 = *reinterpret_cast<const float4*>(vg + (k0 + kr) * D + 4 * c4);
+      }
+      *reinterpret_cast<float4*>(Ks + kr * DP + 4 * c4) = kv4;
+      *reinterpret_cast<float4*>(Vs + kr * DP + 4 * c4) = vv4;
+    }
+    __syncthreads();
+    float sc[G][4];
+#pragma unroll
+    for (int i = 0; i < G; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sc[i][j] = 0.f;
+#pragma unroll 4
+    for (int c = 0; c < D; c += 4) {
+      float4 kv[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) kv[j] = *reinterpret_cast<const float4*>(Ks + (cg + 16 * j) * DP + c);
+#pragma unroll
+      for (int i = 0; i < G; ++i) {
+        const float4 qv = *reinterpret_cast<const float4*>(Qs + (rb * G + i) * DP + c);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          sc[i][j] = fmaf(qv.w, kv[j].w, fmaf(qv.z, kv[j].z, fmaf(qv.y, kv[j].y, fmaf(qv.x, kv[j].x, sc[i][j]))));
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < G; ++i) {
+      const int r = rb * G + i;
+      const int64_t pr = pos0 + s0 + (r & 15);  // this row's position: keys 0 .. pr are visible
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float v = k0 + cg + 16 * j <= pr ? sc[i][j] * scale : -INFINITY;
+        sc[i][j] = v;
+        mx = fmaxf(mx, v);
+      }
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float mn = fmaxf(m[i], mx);  // finite: key 0 is visible to every row in tile 0
+      const float alpha = expf(m[i] - mn);  // 0 on the first tile (m = -inf)
+      float ps = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float pj = expf(sc[i][j] - mn);
+        Ps[r * PP + cg + 16 * j] = pj;
+        ps += pj;
+      }
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+      l[i] = fmaf(l[i], alpha, ps);
+      m[i] = mn;
+#pragma unroll
+      for (int v = 0; v < DV; ++v) {
+        o[i][v].x *= alpha;
+        o[i][v].y *= alpha;
+        o[i][v].z *= alpha;
+        o[i][v].w *= alpha;
+      }
+    }
+    __syncthreads();  // P of every row is in shared memory
+    const int kn = (int)min((int64_t)kPfKeys, pmax - k0 + 1);
+    for (int key = 0; key < kn; ++key) {
+      float4 vv[DV];
+#pragma unroll
+      for (int v = 0; v < DV; ++v) vv[v] = *reinterpret_cast<const float4*>(Vs + key * DP + 4 * cg + 64 * v);
+#pragma unroll
+      for (int i = 0; i < G; ++i) {
+        const float pk = Ps[(rb * G + i) * PP + key];
+#pragma unroll
+        for (int v = 0; v < DV; ++v) {
+          o[i][v].x = fmaf(pk, vv[v].x, o[i][v].x);
+          o[i][v].y = fmaf(pk, vv[v].y, o[i][v].y);
+          o[i][v].z = fmaf(pk, vv[v].z, o[i][v].z);
+          o[i][v].w = fmaf(pk, vv[v].w, o[i][v].w);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < G; ++i) {
+    const int r = rb * G + i;
+    const int64_t s = s0 + (r & 15);
+    if (s >= S) continue;
+    const float inv = 1.0f / l[i];
+    float* dst = out + s * ldq + (int64_t)(g * G + (r >> 4)) * D + 4 * cg;
+#pragma unroll
+    for (int v = 0; v < DV; ++v)
+      *reinterpret_cast<float4*>(dst + 64 * v) =
+          make_float4(o[i][v].x * inv, o[i][v].y * inv, o[i][v].z * inv, o[i][v].w * inv);
+  }
+}
+
 // One block (1024 threads): first index of the maximum into *idx (NaNs never win; with no
 // element above -FLT_MAX the index is 0); *pos += 1 when pos is given.
 __global__ void argmax_kernel(const float* __restrict__ x, int64_t n, int64_t* __restrict__ idx,
@@ -549,6 +747,72 @@ int run_swiglu(cudaStream_t st, const float* gu, float* out, int64_t n) {
 
 int run_argmax(cudaStream_t st, const float* x, int64_t n, int64_t* idx, int64_t* pos) {
   return launch_pdl(st, dim3(1), dim3(1024), argmax_kernel, "argmax launch", x, n, idx, pos);
+}
+
+int run_swiglu_rows(cudaStream_t st, const float* gu, float* out, int64_t rows, int64_t n) {
+  const int64_t blocks = std::min<int64_t>((rows * n + 255) / 256, 8 * (int64_t)sms_now());
+  return launch_pdl(st, dim3((unsigned)blocks), dim3(256), swiglu_rows_kernel, "swiglu_rows launch", gu, out, rows, n);
+}
+
+int run_rope_append_rows(cudaStream_t st, const float* qkv, int64_t S, int64_t pos0, int heads, int kv, int d,
+                         const float* cos_t, const float* sin_t, float* q_out, float* kc, float* vc, int64_t max_seq) {
+  const int64_t work = S * ((int64_t)(heads + kv) * (d / 2) + (int64_t)kv * d);
+  const int64_t blocks = std::min<int64_t>((work + 255) / 256, 8 * (int64_t)sms_now());
+  return launch_pdl(st, dim3((unsigned)blocks), dim3(256), rope_append_rows_kernel, "rope_append_rows launch", qkv, S,
+                    pos0, heads, kv, d, cos_t, sin_t, q_out, kc, vc, max_seq);
+}
+
+namespace {
+template <int G, int D>
+int launch_prefill(cudaStream_t st, const float* q, const float* kc, const float* vc, float* out, int64_t S,
+                   int64_t pos0, int heads, int kv, int64_t max_seq) {
+  constexpr size_t smem = sizeof(float) * ((size_t)(kPfTok * G + 2 * kPfKeys) * (D + 4) + (size_t)kPfTok * G * (kPfKeys + 4));
+  static_assert(smem <= 227 * 1024, "prefill attention tile exceeds shared memory");
+  auto kern = gqa_prefill_kernel<G, D>;
+  static ContextOnce configured;
+  const int rc = configured.run([&] {
+    MSQ_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                 "gqa_prefill smem attribute");
+    return MSQ_OK;
+  });
+  if (rc != MSQ_OK) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((S + kPfTok - 1) / kPfTok), (unsigned)kv);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  MSQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, q, kc, vc, out, S, pos0, heads, max_seq, 1.0f / sqrtf((float)D)),
+               "gqa_prefill launch");
+  note_launch();
+  return MSQ_OK;
+}
+
+template <int D>
+int prefill_g(cudaStream_t st, int G, const float* q, const float* kc, const float* vc, float* out, int64_t S,
+              int64_t pos0, int heads, int kv, int64_t max_seq) {
+  switch (G) {
+    case 1: return launch_prefill<1, D>(st, q, kc, vc, out, S, pos0, heads, kv, max_seq);
+    case 2: return launch_prefill<2, D>(st, q, kc, vc, out, S, pos0, heads, kv, max_seq);
+    case 3: return launch_prefill<3, D>(st, q, kc, vc, out, S, pos0, heads, kv, max_seq);
+    case 4: return launch_prefill<4, D>(st, q, kc, vc, out, S, pos0, heads, kv, max_seq);
+    case 5: return launch_prefill<5, D>(st, q, kc, vc, out, S, pos0, heads, kv, max_seq);
+    case 6: return launch_prefill<6, D>(st, q, kc, vc, out, S, pos0, heads, kv, max_seq);
+    case 7: return launch_prefill<7, D>(st, q, kc, vc, out, S, pos0, heads, kv, max_seq);
+    default: return launch_prefill<8, D>(st, q, kc, vc, out, S, pos0, heads, kv, max_seq);
+  }
+}
+}  // namespace
+
+int run_gqa_prefill(cudaStream_t st, const float* q, const float* kc, const float* vc, float* out, int64_t S,
+                    int64_t pos0, int heads, int kv, int d, int64_t max_seq) {
+  const int G = heads / kv;
+  return d == 64 ? prefill_g<64>(st, G, q, kc, vc, out, S, pos0, heads, kv, max_seq)
+                 : prefill_g<128>(st, G, q, kc, vc, out, S, pos0, heads, kv, max_seq);
 }
 
 }  // namespace msq

@@ -191,6 +191,11 @@ int run_rope_gqa_decode(cudaStream_t st, const float* qkv, float* kc, float* vc,
 size_t gqa_decode_smem(int heads, int kv, int d);
 int run_swiglu(cudaStream_t st, const float* gu, float* out, int64_t n);
 int run_argmax(cudaStream_t st, const float* x, int64_t n, int64_t* idx, int64_t* pos);
+int run_swiglu_rows(cudaStream_t st, const float* gu, float* out, int64_t rows, int64_t n);
+int run_rope_append_rows(cudaStream_t st, const float* qkv, int64_t S, int64_t pos0, int heads, int kv, int d,
+                         const float* cos_t, const float* sin_t, float* q_out, float* kc, float* vc, int64_t max_seq);
+int run_gqa_prefill(cudaStream_t st, const float* q, const float* kc, const float* vc, float* out, int64_t S,
+                    int64_t pos0, int heads, int kv, int d, int64_t max_seq);
 
 // Loads element idx of an activation tensor of dtype dt (f32 / f16 / bf16) as fp32.
 __device__ __forceinline__ float load_act(const void* a, int dt, int64_t idx) {

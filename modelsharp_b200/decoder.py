@@ -101,7 +101,8 @@ class CudaDecoder:
     """Greedy decoding with the projections on libms_cuda_nbits.
 
     q/k/v are packed into one weight (N = (H + 2 Hkv) d) and gate/up into another (N = 2 I), as
-    packed-QKV exports do, so a layer runs four MatMulNBits. The prompt pass uses torch glue;
+    packed-QKV exports do, so a layer runs four MatMulNBits. The prompt pass uses the library's
+    row forms of the glue (causal prompt attention included; torch only gathers embedding rows);
     a decode step folds RMSNorm, SwiGLU and the residual adds into its GEMVs and uses the
     library's fused rotary + KV append + GQA decode and argmax kernels, every launch chained
     with programmatic dependent launch."""
@@ -134,7 +135,6 @@ class CudaDecoder:
         shape = (cfg.layers, cfg.kv_heads, cfg.max_seq, cfg.head_dim)
         self.kc = torch.zeros(shape, device=dev)
         self.vc = torch.zeros(shape, device=dev)
-        self.keys = torch.arange(cfg.max_seq, device=dev)
         # decode-step buffers (fixed addresses, so a captured step can be replayed)
         f = dict(device=dev, dtype=torch.float32)
         self.bx = torch.empty(1, cfg.hidden, **f)
@@ -142,53 +142,55 @@ class CudaDecoder:
         self.battn = torch.empty(1, self.n_q, **f)
         self.bgu, self.blogits = torch.empty(1, 2 * cfg.inter, **f), torch.empty(1, cfg.vocab, **f)
 
-    # ---- torch glue (prompt pass)
-    def _norm(self, x, gamma):
-        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.cfg.eps) * gamma
-
-    def _rope(self, x, heads, cos, sin):
-        s, d = x.shape[0], self.cfg.head_dim
-        v = x.contiguous().view(s, heads, d)
-        a, b = v[..., : d // 2], v[..., d // 2:]
-        c, sn = cos[:, None, :], sin[:, None, :]
-        return torch.cat((a * c - b * sn, b * c + a * sn), dim=-1).reshape(s, heads * d)
-
-    def _attend(self, q, li, mask):
-        """q [S, H*d] against the layer's cache; mask [S, max_seq] True where a key is visible."""
-        cfg = self.cfg
-        s, d, hkv = q.shape[0], cfg.head_dim, cfg.kv_heads
-        qv = q.reshape(s, hkv, cfg.heads // hkv, d).permute(1, 2, 0, 3)         # [Hkv, G, S, d]
-        sc = torch.matmul(qv, self.kc[li].unsqueeze(1).transpose(-1, -2)) / float(np.sqrt(d))  # [Hkv, G, S, T]
-        sc = sc.masked_fill(~mask, float("-inf"))
-        p = torch.softmax(sc, dim=-1)
-        out = torch.matmul(p, self.vc[li].unsqueeze(1))                          # [Hkv, G, S, d]
-        return out.permute(2, 0, 1, 3).reshape(s, cfg.heads * d)
-
+    # ---- prompt pass
     def prefill(self, tokens: torch.Tensor, path: int = N.PATH_AUTO_SPLIT) -> torch.Tensor:
         """Runs the prompt from position 0; returns the last position's logits [vocab]. The
         default route puts the prompt's projections on the split-operand tcgen05 GEMM (products
         good to ~2^-22): the greedy tokens that follow must be the fp32 reference's, and this
         decoder amplifies a projection's error about a hundredfold through its 32 layers, which
-        the fp16 GEMM's 2^-11 operands (PATH_AUTO) do not survive."""
-        cfg = self.cfg
+        the fp16 GEMM's 2^-11 operands (PATH_AUTO) do not survive.
+
+        Every step is a library launch: add + RMSNorm (the residual add of the previous block
+        folded in), the projections, rotary of the S tokens with k and v appended to the cache
+        (msq_rope_append_rows), causal attention over the cache (msq_gqa_prefill) and SwiGLU
+        (msq_swiglu_rows); torch only gathers the embedding rows."""
+        cfg, lib = self.cfg, N.lib()
+        st = torch.cuda.current_stream(self.device).cuda_stream
         s = tokens.shape[0]
-        cos, sin = self.cos[:s], self.sin[:s]
-        mask = self.keys[None, :] <= torch.arange(s, device=self.device)[:, None]
-        x = self.embed[tokens]
+        if s < 1 or s > cfg.max_seq:
+            raise ModelSharpException(f"prompt of {s} tokens does not fit max_seq {cfg.max_seq}")
+
+        def ok(rc, what):
+            if rc:
+                N.check(rc, what)
+
+        f = dict(device=self.device, dtype=torch.float32)
+        x = torch.index_select(self.embed, 0, tokens).contiguous()  # [S, hidden]: the residual stream
+        h = torch.empty_like(x)
+        q = torch.empty(s, self.n_q, **f)
+        attn = torch.empty(s, self.n_q, **f)
+        act = torch.empty(s, cfg.inter, **f)
+
+        def add_norm(delta, gamma):  # x += delta (if any); h = RMSNorm(x) * gamma
+            ok(lib.msq_add_rmsnorm(None, st, x.data_ptr(), None if delta is None else delta.data_ptr(),
+                                   gamma.data_ptr(), h.data_ptr(), s, cfg.hidden, cfg.eps), "msq_add_rmsnorm")
+
+        delta = None
         for li, lw in enumerate(self.layers):
-            h = self._norm(x, lw["norm_attn"])
+            add_norm(delta, lw["norm_attn"])
             qkv = lw["qkv"].matmul(h, path=path)
-            q = self._rope(qkv[:, :self.n_q], cfg.heads, cos, sin)
-            k = self._rope(qkv[:, self.n_q:self.n_q + self.n_kv], cfg.kv_heads, cos, sin)
-            v = qkv[:, self.n_q + self.n_kv:]
-            self.kc[li][:, :s].copy_(k.reshape(s, cfg.kv_heads, cfg.head_dim).transpose(0, 1))
-            self.vc[li][:, :s].copy_(v.reshape(s, cfg.kv_heads, cfg.head_dim).transpose(0, 1))
-            x = x + lw["o"].matmul(self._attend(q, li, mask), path=path)
-            h = self._norm(x, lw["norm_mlp"])
+            ok(lib.msq_rope_append_rows(None, st, qkv.data_ptr(), s, 0, cfg.heads, cfg.kv_heads, cfg.head_dim,
+                                        self.cos.data_ptr(), self.sin.data_ptr(), q.data_ptr(), self.kc[li].data_ptr(),
+                                        self.vc[li].data_ptr(), cfg.max_seq), "msq_rope_append_rows")
+            ok(lib.msq_gqa_prefill(None, st, q.data_ptr(), self.kc[li].data_ptr(), self.vc[li].data_ptr(), s, 0,
+                                   attn.data_ptr(), cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.max_seq),
+               "msq_gqa_prefill")
+            add_norm(lw["o"].matmul(attn, path=path), lw["norm_mlp"])
             gu = lw["gate_up"].matmul(h, path=path)
-            act = torch.nn.functional.silu(gu[:, :cfg.inter]) * gu[:, cfg.inter:]
-            x = x + lw["down"].matmul(act, path=path)
-        return self.lm_head.matmul(self._norm(x[-1:], self.norm_final), path=path)[0]
+            ok(lib.msq_swiglu_rows(None, st, gu.data_ptr(), act.data_ptr(), s, cfg.inter), "msq_swiglu_rows")
+            delta = lw["down"].matmul(act, path=path)
+        add_norm(delta, self.norm_final)
+        return self.lm_head.matmul(h[-1:], path=path)[0]
 
     # ---- fused decode step
     def decode_step(self, tok: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:

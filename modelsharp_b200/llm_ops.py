@@ -13,7 +13,8 @@ CPU kernels:
                                   [output, mean, inv_std_var, input_skip_bias_sum]; beta and
                                   bias inputs are not supported here): msq_add_rmsnorm
 * GroupQueryAttention             GroupQueryAttentionKernel.cs:55-202 (packed QKV, do_rotary,
-                                  cos_cache / sin_cache, seqlens_k): msq_rope_gqa_decode
+                                  cos_cache / sin_cache, seqlens_k): msq_rope_gqa_decode, and
+                                  for a prompt msq_rope_append_rows + msq_gqa_prefill
 * Sigmoid, Mul                    SigmoidKernel.cs:11, MulKernel.cs:8 (same-shape operands)
 * ArgMax                          ArgReduceKernels.cs:77 (last axis): msq_argmax
 
@@ -21,8 +22,8 @@ GroupQueryAttention takes batch 1, packed QKV, rotary in the op, and past_key / 
 preallocated to [1, kv_num_heads, max_seq, head_dim] and shared with present_key /
 present_value: the tokens' rotated k and v are written into the past buffers (rows up to
 seqlens_k) and the present outputs are those buffers. One query token runs as one
-msq_rope_gqa_decode launch; several (a prompt ending at seqlens_k) run as batched torch
-matmuls and a softmax over the cache. (The reference
+msq_rope_gqa_decode launch; several (a prompt ending at seqlens_k) as msq_rope_append_rows and
+msq_gqa_prefill. (The reference
 returns a fresh concatenated present each step; sharing the buffer keeps a decode step free
 of per-token copies of the cache.) Inputs outside these forms raise ModelSharpException.
 """
@@ -177,34 +178,24 @@ class GroupQueryAttentionKernel:
     @staticmethod
     def _prompt(qkv, pos, pk, pv, cos, sin, heads, kvh, d, max_seq):
         """S > 1 query tokens ending at position seqlens_k (a prompt): half-split rotary of q and k
-        at positions p0..p0+S-1, k and v appended to the cache, causal attention of each query
-        over cache rows 0..its position, 1/sqrt(d) scale. Batched torch matmuls and softmax over
-        the cache on the device; reads seqlens_k on the host."""
+        at positions p0..p0+S-1 with k and v appended to the cache (msq_rope_append_rows, qkv left
+        unchanged), then causal attention of each query over cache rows 0..its position with the
+        1/sqrt(d) scale (msq_gqa_prefill). Reads seqlens_k on the host."""
         S = qkv.shape[1]
         last = int(pos.reshape(-1)[0])
         p0 = last - S + 1
         if p0 < 0 or last >= max_seq:
             raise ModelSharpException(f"GroupQueryAttention: {S} query tokens ending at position {last} do not fit "
                                       f"a cache of {max_seq}.")
-        half = d // 2
-        x = qkv.reshape(S, heads + 2 * kvh, d)
-        c, sn = cos[p0:last + 1][:, None, :], sin[p0:last + 1][:, None, :]
-
-        def rot(t):
-            a, b = t[..., :half], t[..., half:]
-            return torch.cat((a * c - b * sn, b * c + a * sn), dim=-1)
-
-        q, k, v = rot(x[:, :heads]), rot(x[:, heads:heads + kvh]), x[:, heads + kvh:]
-        pk[0, :, p0:last + 1].copy_(k.transpose(0, 1))
-        pv[0, :, p0:last + 1].copy_(v.transpose(0, 1))
-        T = last + 1
-        qv = q.reshape(S, kvh, heads // kvh, d).permute(1, 2, 0, 3)                     # [kvh, G, S, d]
-        sc = torch.matmul(qv, pk[0, :, :T].unsqueeze(1).transpose(-1, -2)) / math.sqrt(d)  # [kvh, G, S, T]
-        keys = torch.arange(T, device=qkv.device)
-        mask = keys[None, :] <= (p0 + torch.arange(S, device=qkv.device))[:, None]
-        p = torch.softmax(sc.masked_fill(~mask, float("-inf")), dim=-1)
-        o = torch.matmul(p, pv[0, :, :T].unsqueeze(1))                                   # [kvh, G, S, d]
-        return o.permute(2, 0, 1, 3).reshape(1, S, heads * d).contiguous()
+        st = _stream(qkv)
+        q = torch.empty(S, heads * d, dtype=torch.float32, device=qkv.device)
+        _ok(N.lib().msq_rope_append_rows(None, st, qkv.data_ptr(), S, p0, heads, kvh, d, cos.data_ptr(),
+                                         sin.data_ptr(), q.data_ptr(), pk.data_ptr(), pv.data_ptr(), max_seq),
+            "GroupQueryAttention")
+        out = torch.empty(1, S, heads * d, dtype=torch.float32, device=qkv.device)
+        _ok(N.lib().msq_gqa_prefill(None, st, q.data_ptr(), pk.data_ptr(), pv.data_ptr(), S, p0, out.data_ptr(), heads,
+                                    kvh, d, max_seq), "GroupQueryAttention")
+        return out
 
 
 class SigmoidKernel:
@@ -258,7 +249,8 @@ class MatMulNBitsFusedKernel(CudaMatMulNBitsKernel):
     silu(gate) * up; with residual, the product is added into that tensor in place (the fusion
     pass proves no later node reads its old value) and the node's output is that tensor. Up to
     16 rows of fp32 A run as one msq_matmul_fused launch; larger M (a prompt) runs the same steps
-    unfused (msq_add_rmsnorm or a torch SwiGLU, the MatMulNBits path of the registry, an add)."""
+    unfused (msq_add_rmsnorm or msq_swiglu_rows, the MatMulNBits path of the registry, a torch
+    add into the residual)."""
 
     op_type = "MatMulNBitsFused"
 
@@ -298,8 +290,8 @@ class MatMulNBitsFusedKernel(CudaMatMulNBitsKernel):
                 _ok(N.lib().msq_add_rmsnorm(None, _stream(a), a2.data_ptr(), None, gamma.data_ptr(), x.data_ptr(),
                                             m, k, eps), self.op_type)
             elif swiglu:
-                gt, up = a2[:, :k], a2[:, k:]
-                x = (gt / (1.0 + torch.exp(-gt)) * up).contiguous()
+                x = torch.empty(m, k, dtype=torch.float32, device=a.device)
+                _ok(N.lib().msq_swiglu_rows(None, _stream(a), a2.data_ptr(), x.data_ptr(), m, k), self.op_type)
             y = w.matmul(x, path=self.path)
             if ins[5]:
                 o2.add_(y)

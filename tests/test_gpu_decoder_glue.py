@@ -88,10 +88,9 @@ def test_rope_append_position_past_cache_writes_nothing(cuda_device):
     kc = torch.zeros(kv, max_seq, d, device=cuda_device)
     vc = torch.zeros_like(kc)
     dpos = torch.tensor([max_seq], dtype=torch.int64, device=cuda_device)
-    _ok(N.lib().msq_rope_append(None, _stream(cuda_device), qkv.data_ptr(), heads, kv, d,
-                                torch.from_numpy(cos).to(cuda_device).data_ptr(),
-                                torch.from_numpy(sin).to(cuda_device).data_ptr(), dpos.data_ptr(), kc.data_ptr(),
-                                vc.data_ptr(), max_seq))
+    dcos, dsin = torch.from_numpy(cos).to(cuda_device), torch.from_numpy(sin).to(cuda_device)
+    _ok(N.lib().msq_rope_append(None, _stream(cuda_device), qkv.data_ptr(), heads, kv, d, dcos.data_ptr(),
+                                dsin.data_ptr(), dpos.data_ptr(), kc.data_ptr(), vc.data_ptr(), max_seq))
     torch.cuda.synchronize(cuda_device)
     assert torch.equal(qkv, before) and not kc.any() and not vc.any()
 
@@ -196,10 +195,10 @@ def test_rope_gqa_decode_position_past_cache(cuda_device):
     dqkv, dkc, dvc = (torch.from_numpy(v.copy()).to(cuda_device) for v in (qkv, kc, vc))
     dpos = torch.tensor([max_seq + 3], dtype=torch.int64, device=cuda_device)
     out = torch.empty(1, heads * d, device=cuda_device)
-    _ok(N.lib().msq_rope_gqa_decode(None, _stream(cuda_device), dqkv.data_ptr(), heads, kv, d,
-                                    torch.from_numpy(cos).to(cuda_device).data_ptr(),
-                                    torch.from_numpy(sin).to(cuda_device).data_ptr(), dpos.data_ptr(),
-                                    dkc.data_ptr(), dvc.data_ptr(), out.data_ptr(), max_seq))
+    dcos, dsin = torch.from_numpy(cos).to(cuda_device), torch.from_numpy(sin).to(cuda_device)
+    _ok(N.lib().msq_rope_gqa_decode(None, _stream(cuda_device), dqkv.data_ptr(), heads, kv, d, dcos.data_ptr(),
+                                    dsin.data_ptr(), dpos.data_ptr(), dkc.data_ptr(), dvc.data_ptr(), out.data_ptr(),
+                                    max_seq))
     ref = od.attention(qkv[:, :heads * d], kc, vc, max_seq - 1, cfg)
     assert oracle.rel_l2(out.cpu().numpy(), ref) <= TOL
     np.testing.assert_array_equal(dkc.cpu().numpy(), kc)
