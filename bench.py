@@ -715,8 +715,10 @@ def run_nsplit(args, rank: int, world: int, local_rank: int):
     peak, peak_kind = peaks()
     per_rank_achieved = shard_bytes / (ms / args.steps * 1e-3) / 1e9
     flops = 2.0 * M * sum(n * k for k, n in NSPLIT_LAYERS)  # whole step, all ranks
-    if M >= 17:  # the tensor-core GEMM: a contraction, bounded by the tensor pipe
-        tc_peak = tensor_peak()
+    tc_peak = tensor_peak()
+    # the bound by arithmetic intensity: FLOPs per weight byte against the ridge of the measured
+    # peaks (about 210 FLOP/B; M = 32 does about 120, so it is HBM-bound even on the tensor cores)
+    if flops / nbytes > tc_peak[0] * 1e12 / (peak * 1e9):
         tflops_rank = flops / world / (ms / args.steps * 1e-3) / 1e12
         roof = {"bound": "tensor", "achieved": tflops_rank, "peak": tc_peak[0], "unit": "TFLOP/s",
                 "frac": tflops_rank / tc_peak[0], "traffic": None, "peak_source": tc_peak[1],
@@ -724,7 +726,8 @@ def run_nsplit(args, rank: int, world: int, local_rank: int):
     else:
         roof = {"bound": "hbm", "achieved": per_rank_achieved, "peak": peak, "unit": "GB/s",
                 "frac": per_rank_achieved / peak, "traffic": None, "peak_source": f"{peak_kind} HBM copy bandwidth",
-                "note": "per-rank shard bytes over the whole step time (all-gathers included)"}
+                "note": "per-rank shard bytes over the whole step time (all-gathers included)",
+                "tflops_per_rank": flops / world / (ms / args.steps * 1e-3) / 1e12}
     if rank == 0:
         from oracle import oracle
         # parity of the assembled output against the checker chain (up-proj output fed to the down-proj)
@@ -753,7 +756,8 @@ def run_nsplit(args, rank: int, world: int, local_rank: int):
                        "launch": ("one CUDA graph replay per step: 2 GEMV launches that store into every rank's "
                                   "Y over NVLink and signal completion" if gather == "p2p" else
                                   f"one CUDA graph replay per step: {per_step_launches} library launches "
-                                  f"({'tensor-core GEMM' if M >= 17 else 'decode GEMV'}) + 2 NCCL all-gathers"),
+                                  f"({'tensor-core GEMM' if M >= 17 else 'decode GEMV'})"
+                                  + (" + 2 NCCL all-gathers" if world > 1 else " (one GPU: nothing to gather)")),
                        "gather": gather, "flops_per_step": flops, "timing": spread,
                        "tflops": flops / (ms / args.steps * 1e-3) / 1e12,
                        "parity_rel_l2": parity},
@@ -1279,8 +1283,11 @@ def main():
                 pre = run_prefill(args, rank, world, local_rank)
                 log("sub-record: 7B decode (configs[4])")
                 dec = run_decode(args, rank, world, local_rank)
+                log("sub-record: 70B layers at M = 32 (configs[3], one GPU)")
+                l70 = run_nsplit(argparse.Namespace(**{**vars(args), "m": 32, "gather": "nccl"}), rank, world,
+                                 local_rank)
                 if out is not None:
-                    out["sub"] = {"prefill": pre, "decode7b": dec}
+                    out["sub"] = {"prefill": pre, "decode7b": dec, "layers70b_m32": l70}
         if rank == 0 and out is not None:
             print(json.dumps(out), flush=True)
     finally:

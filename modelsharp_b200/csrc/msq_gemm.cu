@@ -387,39 +387,51 @@ __global__ void __launch_bounds__(Plan<TM, BN, SPLIT>::kThreads, 1)
   }
 }
 
-// fp32 / bf16 / unaligned fp16 activations -> fp16 [M][lda] (k < K only), one warp per row.
-// fp16 holds magnitudes up to 65504 and keeps full precision only above 2^-14, while the
-// reference computes in fp32; so each row is scaled by a power of two 2^e chosen from its
-// largest finite magnitude (that maximum lands in [2^14, 2^15)) before the rounding, and
-// row_scale[m] = 2^-e undoes it exactly in the GEMM's epilogue. Infinities and NaNs pass
-// through unchanged, so they propagate through the tensor core as in the fp32 reference.
-// With out_lo (the split GEMM), also the fp16 remainder lo = fp16(a 2^e - hi) of every element.
-__global__ void to_half_rows_kernel(const void* __restrict__ a, int dt, int64_t M, int K, __half* __restrict__ out,
-                                    int64_t lda, float* __restrict__ row_scale, __half* __restrict__ out_lo) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t m = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); m < M; m += warps) {
+// fp32 / bf16 / unaligned fp16 activations -> fp16 [M][lda] (k < K only), one block of 256
+// threads per row (a warp per row left 32 warps to stage the 28672-k rows of a 32-row down
+// projection, hundreds of microseconds of dependent loads). fp16 holds magnitudes up to 65504
+// and keeps full precision only above 2^-14, while the reference computes in fp32; so each row
+// is scaled by a power of two 2^e chosen from its largest finite magnitude (that maximum lands
+// in [2^14, 2^15)) before the rounding, and row_scale[m] = 2^-e undoes it exactly in the GEMM's
+// epilogue. Infinities and NaNs pass through unchanged, so they propagate through the tensor
+// core as in the fp32 reference. With out_lo (the split GEMM), also the fp16 remainder
+// lo = fp16(a 2^e - hi) of every element.
+constexpr int kStageThreads = 256;
+
+__global__ void __launch_bounds__(kStageThreads) to_half_rows_kernel(const void* __restrict__ a, int dt, int64_t M,
+                                                                     int K, __half* __restrict__ out, int64_t lda,
+                                                                     float* __restrict__ row_scale,
+                                                                     __half* __restrict__ out_lo) {
+  __shared__ uint32_t red[kStageThreads / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int64_t m = blockIdx.x; m < M; m += gridDim.x) {
     const int64_t base = m * (int64_t)K;
     float mx = 0.f;
-    for (int k = lane; k < K; k += 32) {
+    for (int k = tid; k < K; k += kStageThreads) {
       const float v = fabsf(load_act(a, dt, base + k));
       if (v <= 3.402823466e38f) mx = fmaxf(mx, v);  // finite only (false for NaN and inf)
     }
-    mx = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(mx)));
+    // non-negative floats order as their bits
+    uint32_t u = __reduce_max_sync(0xffffffffu, __float_as_uint(mx));
+    if (lane == 0) red[warp] = u;
+    __syncthreads();
+    u = __reduce_max_sync(0xffffffffu, red[lane % (kStageThreads / 32)]);
+    __syncthreads();  // red is reused by the next row
+    mx = __uint_as_float(u);
     int e = 0;
     if (mx > 0.f) {
       int ex;
-      frexpf(mx, &ex);               // mx = f 2^ex, f in [0.5, 1)
+      frexpf(mx, &ex);                   // mx = f 2^ex, f in [0.5, 1)
       e = max(-120, min(120, 15 - ex));  // mx 2^e in [2^14, 2^15)
     }
     const float up = ldexpf(1.f, e);
-    for (int k = lane; k < K; k += 32) {
+    for (int k = tid; k < K; k += kStageThreads) {
       const float v = load_act(a, dt, base + k) * up;
       const __half h = __float2half_rn(v);
       out[m * lda + k] = h;
       if (out_lo) out_lo[m * lda + k] = __float2half_rn(v - __half2float(h));
     }
-    if (lane == 0) row_scale[m] = ldexpf(1.f, -e);
+    if (tid == 0) row_scale[m] = ldexpf(1.f, -e);
   }
 }
 
@@ -665,10 +677,10 @@ size_t staging_bytes(const Weights& w, const void* d_a, int a_dtype, int64_t M, 
 int stage_rows(cudaStream_t st, const Weights& w, const void* d_a, int a_dtype, int64_t M, void* staging,
                const float** row_scale, int parts = 1) {
   float* rs = reinterpret_cast<float*>(static_cast<uint8_t*>(staging) + staged_scale_offset(w, M, parts));
-  const int64_t blocks = std::min<int64_t>((M + 7) / 8, 16 * (int64_t)num_sms(w.device));
+  const int64_t blocks = std::min<int64_t>(M, 16 * (int64_t)num_sms(w.device));
   __half* hi = static_cast<__half*>(staging);
-  to_half_rows_kernel<<<(unsigned)blocks, 256, 0, st>>>(d_a, a_dtype, M, w.K, hi, staged_lda(w), rs,
-                                                        parts == 2 ? hi + M * staged_lda(w) : nullptr);
+  to_half_rows_kernel<<<(unsigned)blocks, kStageThreads, 0, st>>>(d_a, a_dtype, M, w.K, hi, staged_lda(w), rs,
+                                                                  parts == 2 ? hi + M * staged_lda(w) : nullptr);
   note_launch();
   MSQ_CUDA_TRY(cudaGetLastError(), "staging launch");
   *row_scale = rs;

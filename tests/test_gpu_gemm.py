@@ -82,6 +82,38 @@ def test_gemm_full_grid_does_not_split(cuda_device):
     assert N.last_path() in ("gemm_tc_m384_n128", "gemm_tc_m512_n128")  # a full grid: no k split
 
 
+@pytest.mark.parametrize("M,N_,K,bs,zp,a_dtype", [
+    (17, 300, 256, 32, "packed", "f32"),     # ragged N, K-split (3 weight tiles), staged A
+    (24, 1000, 4160, 128, "none", "f16"),    # ragged last k-stage
+    (32, 8192, 2048, 64, "float", "f32"),
+    (33, 4096, 4096, 128, "packed", "f16"),
+    (48, 256, 8192, 32, "packed", "f16"),    # two weight tiles, many K-splits
+    (64, 2000, 1024, 128, "packed", "f32"),
+])
+def test_gemm_small_m(cuda_device, M, N_, K, bs, zp, a_dtype):
+    """17 <= M <= 64 (one 128-row activation tile, K split across CTAs where the weight tiles
+    leave SMs idle; staged fp32 rows scaled by a power of two), against the checker at the
+    GEMM's bar."""
+    c = synth.make_case(37, M, N_, K, 4, bs, zp, a_dtype=a_dtype, scale_lo=0.001, scale_hi=0.01)
+    y = gemm(c, cuda_device)
+    assert N.last_path().startswith("gemm_tc_m128_n128"), N.last_path()
+    assert oracle.rel_l2(y, oracle.managed(c)) <= TOL_TC
+
+
+def test_gemm_small_m_writes_only_its_shard(cuda_device):
+    c = synth.make_case(39, 20, 600, 1024, 4, 64, "packed", scale_lo=0.001, scale_hi=0.01)
+    w = QuantizedWeights(c["b"], c["scales"], c["zp"], 600, 1024, 4, 64, rows=(200, 600), device=cuda_device)
+    y = torch.full((20, 640), float("nan"), device=cuda_device)
+    w.matmul(torch.from_numpy(c["a"]).to(cuda_device), out=y[:, 200:600], ldy=640, path=N.PATH_GEMM)
+    torch.cuda.synchronize()
+    assert N.last_path().startswith("gemm_tc_m128_n128")
+    out = y.cpu().numpy()
+    assert np.isnan(out[:, :200]).all() and np.isnan(out[:, 600:]).all()
+    ref = oracle.managed(c)[:, 200:600]
+    assert oracle.rel_l2(out[:, 200:600], ref) <= TOL_TC
+    w.free()
+
+
 def test_gemm_auto_routes_prefill(cuda_device):
     c = synth.make_case(32, 40, 640, 1024, 4, 128, "packed")
     w = QuantizedWeights(c["b"], c["scales"], c["zp"], 640, 1024, 4, 128, device=cuda_device)
