@@ -21,7 +21,8 @@ stores them). value = algorithmic GB/s of the whole job.
             clocks, parity, roofline, CPU baseline, e2e): "prefill" (configs[2], TFLOP/s of the
             tcgen05 GEMM at M = 512 / 2048 / 8192) and "decode7b" (configs[4], tok/s of the
             synthetic 7B decoder, 128 greedy tokens after a 512-token prompt, every token checked
-            against the CPU checker). --no-sub skips them.
+            against the CPU checker); and "layers70b_m32" (configs[3] at M = 32 on one GPU: the
+            up and down projections of the 70B MLP, GB/s). --no-sub skips them.
 
 Multi-GPU (torchrun, N > 1): the sweep column-split over the ranks: every shape's rows are
 sharded, each shard's GEMV stores its outputs into every rank's full Y over NVLink, and each op
@@ -1240,7 +1241,7 @@ def main():
     ap.add_argument("--split", action="store_true",
                     help="prefill: the split-operand GEMM (MSQ_PATH_GEMM_SPLIT) instead of the fp16 one")
     ap.add_argument("--no-sub", action="store_true",
-                    help="N = 1 sweep only: skip the prefill and 7B decode sub-records")
+                    help="N = 1 sweep only: skip the prefill, 7B decode and 70B M = 32 sub-records")
     ap.add_argument("--shapes", default="",
                     help="restrict the step to these KxN shapes (comma separated), for profiling one shape")
     args = ap.parse_args()
