@@ -18,8 +18,10 @@
 // preparation is one pass of loads and warp shuffles.
 //
 // Decode: a lane's 32-bit word holds, byte j, the codes of (row r, k 4t+j) (low nibble)
-// and (row r+8, k 4t+j) (high nibble), so (x & 0x0F0F0F0F) and ((x >> 4) & 0x0F0F0F0F) are
-// directly the u8 A-fragment registers of rows r and r+8: three integer ops per 8 weights.
+// and (row r+8, k 4t+j) (high nibble), so (x & 0x0F0F0F0F) is directly the u8 A-fragment
+// register of rows r, and x itself that of rows r+8 as 16 q' + q: their dot comes out as
+// 16 D' + D, and D, row r's own dot, sits in the same lane's accumulator, so the epilogue
+// subtracts it once per block (exact in s32). One integer op per 8 weights.
 #include "msq_internal.cuh"
 #include "msq_ptx.cuh"
 
@@ -598,12 +600,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
                 lo1 = wv[uu][4 * st + 2];
                 hi1 = wv[uu][4 * st + 3];
               } else {
-                // rows r+8 keep their codes in the high nibble: 16 q as a u8, exact
+                // rows r take the low nibbles; rows r+8 take the whole bytes, 16 q' + q as a
+                // u8, whose dot is 16 D' + D with D row r's own dot from the same MMA (the
+                // epilogue subtracts it: exact in s32)
                 const uint32_t x0 = wv[uu][2 * st], x1 = wv[uu][2 * st + 1];
                 lo0 = x0 & 0x0F0F0F0Fu;
-                hi0 = x0 & 0xF0F0F0F0u;
+                hi0 = x0;
                 lo1 = x1 & 0x0F0F0F0Fu;
-                hi1 = x1 & 0xF0F0F0F0u;
+                hi1 = x1;
               }
 #pragma unroll
               for (int nt = 0; nt < NT; ++nt)
@@ -621,6 +625,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
               int cc[4];
 #pragma unroll
               for (int j = 0; j < 4; ++j) cc[j] = c[uu][bl][0][0][j] + c[uu][bl][1][0][j];
+              cc[2] -= cc[0];  // rows grp + 8: 16 D' (their MMA rows carried the low nibbles too)
+              cc[3] -= cc[1];
               const float S0 = sv[uu][bl][0], S1 = sv16[uu][bl][0];
               const float d00 = (float)cc[0] - z0[uu][bl] * S0, d01 = (float)cc[1] - z0[uu][bl] * S1;
               const float d10 = (float)(cc[2] >> 4) - z1[uu][bl] * S0, d11 = (float)(cc[3] >> 4) - z1[uu][bl] * S1;
@@ -652,6 +658,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_mma_kernel(const Args p) {
               int cc[4];
 #pragma unroll
               for (int j = 0; j < 4; ++j) cc[j] = c[uu][bl][0][nt][j] + c[uu][bl][1][nt][j];
+              if constexpr (!B8) {  // rows grp + 8: 16 D' (their MMA rows carried the low nibbles too)
+                cc[2] -= cc[0];
+                cc[3] -= cc[1];
+              }
               // even lanes hold digits 0 and 1 (and the zero-point term), odd lanes digit 2
               // and the always-zero fourth column: y += s 2^-sigma wdig (c_a + 256 c_b - z S / wdig)
               // with S = 0 on odd lanes, the integer combination exact in s32 (|c| < 2^22 even

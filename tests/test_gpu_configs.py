@@ -131,6 +131,31 @@ def test_gemv_nonfinite_activations_propagate(cuda_device, M, bs, zp):
     w.free()
 
 
+@pytest.mark.parametrize("M,bs,K", [(1, 32, 8960), (3, 128, 14336)])
+def test_gemv_rows_over_several_stream_tiles(cuda_device, M, bs, K):
+    """Rows of A that span several stream tiles (K = 8960 at block_size 32 is five k-tiles,
+    14336 at 128 four), with magnitudes that differ by 1e6 from one part of the row to the
+    next and inf / NaN only in the last tiles: each block's fixed-point exponent is its own,
+    and the outputs have the checker's finite values and IEEE classes."""
+    c = synth.make_case(77, M, 500, K, 4, bs, "packed", scale_lo=0.001, scale_hi=0.01)
+    a = c["a"].copy()
+    a[:, : K // 3] *= 1e-3
+    a[:, 2 * K // 3:] *= 1e3
+    w = _weights(dict(c, a=a), cuda_device)
+    y = _mm(w, a, cuda_device, path=N.PATH_GEMV)
+    assert oracle.rel_l2(y, oracle.managed(dict(c, a=a))) <= TOL_FP32
+    b = a.copy()
+    b[0, K - 7] = np.inf
+    if M > 1:
+        b[1, K - 200] = np.nan
+    y = _mm(w, b, cuda_device, path=N.PATH_GEMV)
+    ref = oracle.managed(dict(c, a=b))
+    _classes_match(y, ref)
+    fin = np.isfinite(ref)
+    assert oracle.rel_l2(y[fin], ref[fin]) <= TOL_FP32
+    w.free()
+
+
 def test_gemm_nonfinite_activations_propagate(cuda_device):
     c = _nonfinite_case(40, 256, 1024, 32, "packed", 72)
     w = _weights(c, cuda_device)
