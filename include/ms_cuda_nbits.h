@@ -51,7 +51,10 @@ extern "C" {
 #define MSQ_DT_BF16    16  /* not an ElementType: the loader widens bf16 (OnnxModelLoader.cs:410) */
 
 /* ---- kernel path selection (msq_matmul_ex) -------------------------------------- */
-#define MSQ_PATH_AUTO     0  /* M<=16 -> decode GEMV, M>=17 -> tcgen05 GEMM, else generic */
+/* MSQ_PATH_AUTO: bits=4 with a power-of-two block_size >= 32 takes M <= 4 -> decode GEMV;
+ * 5 <= M <= 32 at block_size 128 -> MSQ_PATH_GEMV_TC; other M <= 16 -> decode GEMV; M >= 17 ->
+ * tcgen05 GEMM. bits=8 (block_size 32 / 64 / 128) -> decode GEMV. Everything else -> generic. */
+#define MSQ_PATH_AUTO     0
 #define MSQ_PATH_GENERIC  1  /* any bits / block size / zero-point form, reference layout  */
 #define MSQ_PATH_GEMV     2  /* bits=4, block_size a power of two >= 32                   */
 #define MSQ_PATH_GEMM     3  /* bits=4, block_size a power of two >= 32, tcgen05 + TMEM   */
@@ -62,6 +65,10 @@ extern "C" {
  * reference; about a third of MSQ_PATH_GEMM's throughput.                                */
 #define MSQ_PATH_GEMM_SPLIT 4
 #define MSQ_PATH_AUTO_SPLIT 5  /* as MSQ_PATH_AUTO, with MSQ_PATH_GEMM_SPLIT for M >= 17       */
+/* The batched decode GEMV on tcgen05 kind::i8 (bits=4, block_size 128, 1..32 rows of A): the
+ * decode GEMV's exact integer arithmetic with every weight read once for all rows; the same
+ * parity bar as MSQ_PATH_GEMV (rel-L2 <= 1e-5).                                          */
+#define MSQ_PATH_GEMV_TC  6
 
 /* ---- msq_pack flags ----------------------------------------------------------------- */
 #define MSQ_PACK_DEFAULT       0

@@ -24,7 +24,7 @@ MSQ_E_TIMEOUT = -6
 # ElementType codes (src/ModelSharp/Tensors/ElementType.cs:4-15) plus bf16.
 DT_ABSENT, DT_F32, DT_F64, DT_F16, DT_I32, DT_I64, DT_I8, DT_U8, DT_BOOL, DT_BF16 = -1, 1, 2, 3, 4, 5, 6, 7, 8, 16
 
-PATH_AUTO, PATH_GENERIC, PATH_GEMV, PATH_GEMM, PATH_GEMM_SPLIT, PATH_AUTO_SPLIT = 0, 1, 2, 3, 4, 5
+PATH_AUTO, PATH_GENERIC, PATH_GEMV, PATH_GEMM, PATH_GEMM_SPLIT, PATH_AUTO_SPLIT, PATH_GEMV_TC = 0, 1, 2, 3, 4, 5, 6
 NOALLOC_SCRATCH_BYTES = 16 << 20  # MSQ_NOALLOC_SCRATCH_BYTES
 
 

@@ -14,7 +14,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libms_cuda_nbits.so"
 SOURCES = ["msq_api.cu", "msq_repack.cu", "msq_generic.cu", "msq_gemv.cu", "msq_gemv_mma.cu", "msq_gemm.cu",
-           "msq_noalloc.cu", "msq_decoder.cu"]
+           "msq_noalloc.cu", "msq_decoder.cu", "msq_gemv_tc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

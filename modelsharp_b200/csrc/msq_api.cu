@@ -270,6 +270,7 @@ int matmul_impl(cudaStream_t st, Weights* w, const void* d_a, int a_dtype, int64
   if (path == MSQ_PATH_AUTO || path == MSQ_PATH_AUTO_SPLIT) {
     if (!w->fast4 && !w->fast8) path = MSQ_PATH_GENERIC;
     else if (w->fast8) path = MSQ_PATH_GEMV;
+    else if (M >= 5 && M <= 32 && w->block_size == 128) path = MSQ_PATH_GEMV_TC;  // exact, weights read once
     else if (M >= 17 && w->K >= 64) path = path == MSQ_PATH_AUTO ? MSQ_PATH_GEMM : MSQ_PATH_GEMM_SPLIT;
     else path = MSQ_PATH_GEMV;
   }
@@ -278,6 +279,7 @@ int matmul_impl(cudaStream_t st, Weights* w, const void* d_a, int a_dtype, int64
     case MSQ_PATH_GEMV: return run_gemv(st, *w, d_a, a_dtype, M, d_y, ldy);
     case MSQ_PATH_GEMM: return run_gemm(st, *w, d_a, a_dtype, M, d_y, ldy);
     case MSQ_PATH_GEMM_SPLIT: return run_gemm(st, *w, d_a, a_dtype, M, d_y, ldy, true);
+    case MSQ_PATH_GEMV_TC: return run_gemv_tc(st, *w, d_a, a_dtype, M, d_y, ldy);
     default: return fail(MSQ_E_INVALID, "msq_matmul_ex: unknown path %d", path);
   }
 }
@@ -622,6 +624,7 @@ int msq_set_wait_budget(void* cu_ctx, int64_t ns) {
   const unsigned long long v = ns > 0 ? (unsigned long long)ns : 2000000000ull;
   int rc = set_wait_budget_gemv(v);
   if (rc == MSQ_OK) rc = set_wait_budget_gemm(v);
+  if (rc == MSQ_OK) rc = set_wait_budget_tc(v);
   return rc;
 }
 
@@ -629,15 +632,17 @@ int msq_device_status(void* cu_ctx, void* stream) {
   CtxGuard g(cu_ctx);
   if (g.rc != MSQ_OK) return g.rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  int fv = 0, fm = 0;
+  int fv = 0, fm = 0, ft = 0;
   int rc = read_gemv_mma_errors(st, &fv);
   if (rc == MSQ_OK) rc = read_gemm_errors(st, &fm);
+  if (rc == MSQ_OK) rc = read_gemv_tc_errors(st, &ft);
   if (rc != MSQ_OK) return rc;
   static const char* what[] = {"", "waiting for a stage to arrive", "waiting for a free stage",
                                "waiting for the tensor core", "draining in-flight copies",
                                "waiting for other ranks' shards of a gathered input"};
   if (fv) return fail(MSQ_E_TIMEOUT, "decode GEMV kernel gave up %s", what[fv > 0 && fv < 6 ? fv : 0]);
   if (fm) return fail(MSQ_E_TIMEOUT, "GEMM kernel gave up %s", what[fm > 0 && fm < 6 ? fm : 0]);
+  if (ft) return fail(MSQ_E_TIMEOUT, "tensor-core decode GEMV kernel gave up %s", what[ft > 0 && ft < 6 ? ft : 0]);
   return MSQ_OK;
 }
 

@@ -163,6 +163,10 @@ struct Fusion {
 };
 int run_gemv_fused(cudaStream_t st, const Weights& w, const float* d_a, int64_t M, float* d_y, int64_t ldy,
                    const Fusion& f);
+// The batched decode GEMV on tcgen05 kind::i8 (exact, 1..32 rows of A, block_size 128).
+int run_gemv_tc(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t M, float* d_y, int64_t ldy);
+int read_gemv_tc_errors(cudaStream_t st, int* flags);
+int set_wait_budget_tc(unsigned long long ns);
 // operand_split: the split-operand (three fp16 MMAs per step) form of the GEMM.
 int run_gemm(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64_t M,
              float* d_y, int64_t ldy, bool operand_split = false);

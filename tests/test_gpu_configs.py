@@ -1,8 +1,9 @@
 """Parity at the north_star's own shapes, and A values outside the usual range (needs a B200).
 
 * the 70B-shaped MLP layers (K=8192, N=28672) and (K=28672, N=8192), block_size 128,
-  fp16 A and scales, packed zero points, at M = 1 (decode GEMV, rel-L2 <= 1e-5), 32 and 1024
-  (tensor-core GEMM, rel-L2 <= 5e-3; M = 1024 on sampled rows, rows being independent).
+  fp16 A and scales, packed zero points, at M = 1 (decode GEMV, rel-L2 <= 1e-5), 32 (the
+  tensor-core decode GEMV, rel-L2 <= 1e-5, and the GEMM) and 1024 (tensor-core GEMM, rel-L2 <=
+  5e-3; M = 1024 on sampled rows, rows being independent).
 * configs[2] at M = 8192 on sampled rows.
 * Infinity and NaN in A propagate as in the reference's fp32 sum (MatMulNBitsKernel.cs:236-261):
   an output is NaN, +inf or -inf exactly where the checker's is, on the GEMV and the GEMM;
@@ -53,11 +54,16 @@ def test_70b_layers_at_configs3_row_counts(cuda_device, K, N_):
     y1 = _mm(w, a[:1], cuda_device)
     assert N.last_path() == "gemv_imma"
     assert oracle.rel_l2(y1, oracle.managed(c1)) <= TOL_FP32
-    # M = 32: the GEMM (k split across CTAs at this size)
+    # M = 32: the tensor-core decode GEMV (exact; k split across CTAs at this size), and the
+    # fp16 GEMM when asked for it
     c32 = dict(c, a=a[:32], M=32)
+    ref32 = oracle.managed(c32)
     y32 = _mm(w, a[:32], cuda_device)
+    assert N.last_path().startswith("gemv_tc_i8")
+    assert oracle.rel_l2(y32, ref32) <= TOL_FP32
+    y32 = _mm(w, a[:32], cuda_device, path=N.PATH_GEMM)
     assert N.last_path().startswith("gemm_tc")
-    assert oracle.rel_l2(y32, oracle.managed(c32)) <= TOL_TC
+    assert oracle.rel_l2(y32, ref32) <= TOL_TC
     # M = 1024: the GEMM, sampled rows
     y = _mm(w, a, cuda_device)
     assert N.last_path().startswith("gemm_tc")
