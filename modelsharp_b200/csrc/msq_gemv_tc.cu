@@ -150,6 +150,8 @@ __global__ void __launch_bounds__(MP * 32) tc_digits_kernel(const void* __restri
                                                             int64_t kpd, int8_t* __restrict__ dig,
                                                             float* __restrict__ meta) {
   __shared__ uint32_t mask;
+  // the GEMV (launched with programmatic serialization) may start its prologue and weight loads
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int m = threadIdx.x >> 5, lane = threadIdx.x & 31, b = blockIdx.x;
   if (threadIdx.x == 0) mask = 0u;
   __syncthreads();
@@ -243,6 +245,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   const int nk = min(p.nblk, kb + p.kper) - kb;
 
   if (threadIdx.x == 0) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the split-K sum may launch
     for (int s = 0; s < S; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
@@ -276,21 +279,35 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
 
   if (warp == kTmaWarpTc) {
     if (lane == 0) {
-      int issued = 0;
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % S, j = i % MS;
-        if (i >= S && !tc_wait(&empty[s], ((i / S) - 1) & 1, abort_flag, ptx::kErrTimeoutEmpty)) break;
-        if (i >= MS && !tc_wait(&mempty[j], ((i / MS) - 1) & 1, abort_flag, ptx::kErrTimeoutEmpty)) break;
-        const int b = kb + i;
+      // The weights are settled before the call; the digits and meta rows come from the digits
+      // kernel just before this one. So the first stages' weight side is loaded before the
+      // programmatic-dependency wait, and everything the digits kernel wrote after it.
+      auto load_weights = [&](int i) {
+        const int s = i % S, b = kb + i;
         uint8_t* st = smem + s * PL::kStage;
         ptx::mbar_arrive_expect_tx(&full[s], PL::kCodes + PL::kSc + (ZPK != ZP_NONE ? PL::kZp : 0) + PL::kDig);
         ptx::tma_load_2d(st + PL::kOffCodes, &tmC, &full[s], b * (TBK / 2), n0);
         ptx::tma_load_2d(st + PL::kOffSc, &tmS, &full[s], b & ~3, n0);
         if (ZPK == ZP_PACKED) ptx::tma_load_2d(st + PL::kOffZp, &tmZ, &full[s], (b >> 1) & ~15, n0);
         else if (ZPK == ZP_F32) ptx::tma_load_2d(st + PL::kOffZp, &tmZ, &full[s], b & ~3, n0);
-        ptx::tma_load_2d(st + PL::kOffDig, &tmD, &full[s], b * TBK, 0);
+      };
+      auto load_digits = [&](int i) {
+        const int s = i % S, j = i % MS, b = kb + i;
+        ptx::tma_load_2d(smem + s * PL::kStage + PL::kOffDig, &tmD, &full[s], b * TBK, 0);
         ptx::mbar_arrive_expect_tx(&mfull[j], PL::kMeta);
         ptx::bulk_g2s(smem + PL::kOffMeta + j * PL::kMeta, p.meta + (int64_t)b * PL::kMetaW, PL::kMeta, &mfull[j]);
+      };
+      const int pre = min(nk, S);
+      for (int i = 0; i < pre; ++i) load_weights(i);
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      for (int i = 0; i < pre; ++i) load_digits(i);
+      int issued = pre;
+      for (int i = pre; i < nk; ++i) {
+        const int s = i % S, j = i % MS;
+        if (!tc_wait(&empty[s], ((i / S) - 1) & 1, abort_flag, ptx::kErrTimeoutEmpty)) break;
+        if (i >= MS && !tc_wait(&mempty[j], ((i / MS) - 1) & 1, abort_flag, ptx::kErrTimeoutEmpty)) break;
+        load_weights(i);
+        load_digits(i);
         ++issued;
       }
       // copies in flight must land before exit
@@ -481,6 +498,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
 // y[m][n] = sum over splits z (in order) of ws[z][m][n].
 __global__ void tc_reduce_kernel(const float* __restrict__ ws, int splits, int64_t stride, int M, int N,
                                  float* __restrict__ y, int64_t ldy) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // launched early: the partials must be complete
   const int64_t total = (int64_t)M * N;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t m = i / N, n = i - m * N;
@@ -531,7 +549,19 @@ int launch_tc(cudaStream_t st, const CUtensorMap& c, const CUtensorMap& s, const
     return MSQ_OK;
   });
   if (rc != MSQ_OK) return rc;
-  kern<<<grid, kThreadsTc, PL::kSmem, st>>>(c, s, z, d, a);
+  // programmatic serialization: the prologue and the first stages' weight loads overlap the
+  // digits kernel, which releases this grid early (the producer waits before reading digits)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreadsTc);
+  cfg.dynamicSmemBytes = PL::kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  MSQ_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, c, s, z, d, a), "tc gemv launch");
   note_launch();
   MSQ_CUDA_TRY(cudaGetLastError(), "tc gemv launch");
   return MSQ_OK;
@@ -657,9 +687,18 @@ int run_gemv_tc(cudaStream_t st, Weights& w, const void* d_a, int a_dtype, int64
   if (splits > 1) {
     const int64_t outs = M * (int64_t)w.n_rows;
     const int blocks = (int)std::min<int64_t>((outs + 255) / 256, 4 * (int64_t)sms);
-    tc_reduce_kernel<<<blocks, 256, 0, st>>>(ws, splits, split_stride, (int)M, w.n_rows, d_y, ldy);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(blocks);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, tc_reduce_kernel, (const float*)ws, splits, split_stride, (int)M,
+                                             w.n_rows, d_y, ldy);
     note_launch();
-    const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return done(cuda_fail(e, "tc reduce launch"));
   }
   note_path(splits > 1 ? "gemv_tc_i8_ksplit" : "gemv_tc_i8");
