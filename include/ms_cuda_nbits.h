@@ -160,6 +160,15 @@ int msq_matmul_w4a8(void* cu_ctx, void* stream, msq_weights_t w,
 int msq_matmul_host(void* cu_ctx, void* stream, msq_weights_t w,
                     const void* a, int a_dtype, int64_t M, float* y);
 
+/* The same without the final synchronize: the upload, the op and the download of Y are
+ * enqueued on `stream` and the call returns. A and Y must stay valid until the stream has
+ * passed the download (pinned host memory keeps the copies asynchronous); the caller
+ * synchronizes the stream, or an event recorded after the call, before reading Y. No
+ * counterpart in the reference, whose host-buffer entry (NativeQuant.cs:78-115) is
+ * synchronous: a host loop over several ops pays one round trip per batch of ops. */
+int msq_matmul_host_async(void* cu_ctx, void* stream, msq_weights_t w,
+                          const void* a, int a_dtype, int64_t M, float* y);
+
 /* ---- no-allocation GEMM -------------------------------------------------------------
  * No counterpart in the reference. For callers that cannot allocate device memory while a
  * node runs (an engine that owns all device memory through its own arena, a plugin called

@@ -81,6 +81,7 @@ SIGNATURES: dict[str, tuple] = {
     "msq_matmul": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp, _i64]),
     "msq_matmul_ex": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp, _i64, _i32]),
     "msq_matmul_host": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp]),
+    "msq_matmul_host_async": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp]),
     "msq_matmul_noalloc": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp, _i64]),
     "msq_matmul_w4a8": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _vp, _i64]),
     "msq_device_status": (_i32, [_vp, _vp]),

@@ -557,41 +557,56 @@ int msq_matmul_w4a8(void* cu_ctx, void* stream, msq_weights_t h, const void* d_a
   return run_gemv_w4a8(static_cast<cudaStream_t>(stream), *w, d_a, a_dtype, M, d_y, ldy);
 }
 
-int msq_matmul_host(void* cu_ctx, void* stream, msq_weights_t h, const void* a, int a_dtype, int64_t M, float* y) {
-  CtxGuard g(cu_ctx);
-  if (g.rc != MSQ_OK) return g.rc;
-  Weights* w = reinterpret_cast<Weights*>(h);
-  if (!w) return fail(MSQ_E_INVALID, "msq_matmul_host: NULL weights handle");
+namespace {
+
+// Enqueues the host-buffer form on `st`: pool scratch for A and Y, the upload, the op, the
+// download and the scratch's stream-ordered release. Nothing waits for the GPU here.
+int host_enqueue(cudaStream_t st, Weights* w, const void* a, int a_dtype, int64_t M, float* y, const char* who) {
+  if (!w) return fail(MSQ_E_INVALID, "%s: NULL weights handle", who);
   if (!is_float_act(a_dtype))
     return fail(MSQ_E_INVALID, "MatMulNBits A must be Float32 or Float16; got %s.", dtype_name(a_dtype));
-  if (M <= 0) return M == 0 ? MSQ_OK : fail(MSQ_E_INVALID, "msq_matmul_host: negative M");
-  if (!a || !y) return fail(MSQ_E_INVALID, "msq_matmul_host: NULL host pointer");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (M <= 0) return M == 0 ? MSQ_OK : fail(MSQ_E_INVALID, "%s: negative M", who);
+  if (!a || !y) return fail(MSQ_E_INVALID, "%s: NULL host pointer", who);
   const size_t abytes = (size_t)M * w->K * act_elem_size(a_dtype);
   const size_t ybytes = (size_t)M * w->n_rows * sizeof(float);
+  // one pool block: A, then Y at the next 256-byte boundary
+  const size_t yoff = (abytes + 255) / 256 * 256;
   void* da = nullptr;
-  void* dyv = nullptr;
-  int arc = scratch_alloc(&da, abytes, st);
-  if (arc == MSQ_OK) arc = scratch_alloc(&dyv, ybytes, st);
-  if (arc != MSQ_OK) {
-    scratch_free(da, st);
-    return arc;
-  }
-  float* dy = static_cast<float*>(dyv);
+  const int arc = scratch_alloc(&da, yoff + ybytes, st);
+  if (arc != MSQ_OK) return arc;
+  float* dy = reinterpret_cast<float*>(static_cast<uint8_t*>(da) + yoff);
   cudaError_t e;
   int rc = MSQ_OK;
   e = cudaMemcpyAsync(da, a, abytes, cudaMemcpyHostToDevice, st);
-  if (e != cudaSuccess) rc = cuda_fail(e, "msq_matmul_host upload");
+  if (e != cudaSuccess) rc = cuda_fail(e, "host-buffer upload");
   if (rc == MSQ_OK) rc = matmul_impl(st, w, da, a_dtype, M, dy, w->n_rows, MSQ_PATH_AUTO);
   if (rc == MSQ_OK) {
     e = cudaMemcpyAsync(y, dy, ybytes, cudaMemcpyDeviceToHost, st);
-    if (e != cudaSuccess) rc = cuda_fail(e, "msq_matmul_host download");
+    if (e != cudaSuccess) rc = cuda_fail(e, "host-buffer download");
   }
   scratch_free(da, st);
-  scratch_free(dy, st);
-  e = cudaStreamSynchronize(st);
+  return rc;
+}
+
+}  // namespace
+
+int msq_matmul_host(void* cu_ctx, void* stream, msq_weights_t h, const void* a, int a_dtype, int64_t M, float* y) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc = host_enqueue(st, reinterpret_cast<Weights*>(h), a, a_dtype, M, y, "msq_matmul_host");
+  if (!h || !is_float_act(a_dtype) || M <= 0 || !a || !y) return rc;  // rejected before anything was enqueued
+  const cudaError_t e = cudaStreamSynchronize(st);
   if (rc == MSQ_OK && e != cudaSuccess) rc = cuda_fail(e, "msq_matmul_host synchronize");
   return rc;
+}
+
+int msq_matmul_host_async(void* cu_ctx, void* stream, msq_weights_t h, const void* a, int a_dtype, int64_t M,
+                          float* y) {
+  CtxGuard g(cu_ctx);
+  if (g.rc != MSQ_OK) return g.rc;
+  return host_enqueue(static_cast<cudaStream_t>(stream), reinterpret_cast<Weights*>(h), a, a_dtype, M, y,
+                      "msq_matmul_host_async");
 }
 
 int msq_matmul_noalloc(void* cu_ctx, void* stream, msq_weights_t h, const void* d_a, int a_dtype, int64_t M,

@@ -154,6 +154,32 @@ def test_output_canaries(cuda_device):
     assert not torch.isnan(buf[:1500]).any()
 
 
+def test_host_buffer_async_entry_matches_the_synchronous_one(cuda_device):
+    """msq_matmul_host_async enqueues upload, op and download without waiting: three ops on one
+    stream, one synchronize, the same bits as msq_matmul_host gives op by op (fp32 and fp16 A,
+    the decode GEMV, the tensor-core batched GEMV and the GEMM)."""
+    cs = [synth.make_case(12, 1, 640, 1024, 4, 32, "packed"),
+          synth.make_case(13, 8, 300, 1024, 4, 128, "packed", a_dtype="f16", scale_dtype="f16"),
+          synth.make_case(14, 40, 256, 512, 4, 64, "float")]
+    ws = [pack(c, cuda_device) for c in cs]
+    want = [w.matmul_host(c["a"]) for w, c in zip(ws, cs)]
+    a_h = [torch.from_numpy(np.ascontiguousarray(c["a"])).pin_memory() for c in cs]
+    y_h = [torch.full((c["M"], c["N"]), float("nan")).pin_memory() for c in cs]
+    st = torch.cuda.Stream(cuda_device)
+    for w, a, y in zip(ws, a_h, y_h):
+        rc = N.lib().msq_matmul_host_async(None, st.cuda_stream, w.handle, a.data_ptr(),
+                                           N.DT_F16 if a.dtype == torch.float16 else N.DT_F32, a.shape[0], y.data_ptr())
+        assert rc == N.MSQ_OK, N.last_error()
+    st.synchronize()
+    assert N.lib().msq_device_status(None, None) == N.MSQ_OK
+    for y, yw, c in zip(y_h, want, cs):
+        assert np.array_equal(y.numpy(), yw)
+    rc = N.lib().msq_matmul_host_async(None, st.cuda_stream, ws[0].handle, None, N.DT_F32, 1, y_h[0].data_ptr())
+    assert rc == N.MSQ_E_INVALID and "NULL host pointer" in N.last_error()
+    for w in ws:
+        w.free()
+
+
 def test_host_buffer_entry_and_one_shot(cuda_device):
     c = synth.make_case(10, 2, 640, 1024, 4, 32, "packed")
     ref = oracle.managed(c)
