@@ -83,3 +83,19 @@ def test_tc_gemv_nonfinite_activations(cuda_device):
         assert np.array_equal(f(y), f(ref)), f.__name__
     fin = np.isfinite(ref)
     assert oracle.rel_l2(y[fin], ref[fin]) <= TOL_FP32
+
+
+@pytest.mark.parametrize("K", [1024, 28672])  # one CTA per tile, and the k split
+def test_tc_gemv_writes_only_its_columns(cuda_device, K):
+    """A shard's Y written into a wider row (ldy > N, as the column split does): the columns
+    outside [200, 200 + N) keep their contents, on the direct store and the split sum."""
+    c = synth.make_case(94, 12, 300, K, 4, 128, "packed", scale_lo=0.001, scale_hi=0.01)
+    w = QuantizedWeights(c["b"], c["scales"], c["zp"], c["N"], c["K"], 4, 128, device=cuda_device)
+    buf = torch.full((12, 640), float("nan"), device=cuda_device)
+    w.matmul(torch.from_numpy(c["a"]).to(cuda_device), out=buf[:, 200:500], ldy=640, path=N.PATH_GEMV_TC)
+    torch.cuda.synchronize(cuda_device)
+    assert N.lib().msq_device_status(None, None) == N.MSQ_OK, N.last_error()
+    y = buf.cpu().numpy()
+    assert np.isnan(y[:, :200]).all() and np.isnan(y[:, 500:]).all()
+    assert oracle.rel_l2(y[:, 200:500], oracle.managed(c)) <= TOL_FP32
+    w.free()
