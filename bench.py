@@ -11,8 +11,9 @@ stores them). value = algorithmic GB/s of the whole job.
             --windows windows of exactly --steps steps (each bracketed by a barrier and a
             synchronize); value from the median window, the spread in config.timing.
 * per_M     the same sweep at M = 4 and M = 16 (configs[1]'s batched rows; same weight bytes).
-* e2e       the same ops through the C-ABI host-buffer entry (msq_matmul_host_async per op and one
-            stream synchronize per step; msq_matmul_host, synchronous per op, beside it): pinned host
+* e2e       the same ops through the C-ABI host-buffer entry (msq_matmul_host_async per op, the ops
+            alternating over two streams, both synchronized per step; beside it one stream, and
+            msq_matmul_host, synchronous per op): pinned host
             A copied in and Y copied out inside the timed region, every step.
 * roofline  the decode GEMV kernel: algorithmic bytes / its CUDA-event launch duration vs
             the measured HBM copy bandwidth (MEASURED_PEAKS.json).
@@ -413,31 +414,36 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     d2h = sum(y.numel() * 4 for y in y_host)
     e2e_steps = max(1, min(args.steps, 2000))
 
-    def e2e_step(r: int, asynchronous: bool):
-        # asynchronous: every op's upload, GEMV and download enqueued through
-        # msq_matmul_host_async, then one stream synchronize before the host has the step's Y;
-        # otherwise msq_matmul_host, which synchronizes after every op
-        fn = lib.msq_matmul_host_async if asynchronous else lib.msq_matmul_host
-        for w, a, y in zip(reps[r], a_host, y_host):
-            rc = fn(None, sptr, w.handle, a.data_ptr(), N.DT_F32, 1, y.data_ptr())
+    stream2 = torch.cuda.Stream(dev)
+
+    def e2e_step(r: int, mode: str):
+        # "sync": msq_matmul_host, which synchronizes after every op; "one": every op's upload,
+        # GEMV and download enqueued through msq_matmul_host_async on one stream, then one
+        # synchronize before the host has the step's Y; "two": the same with the ops alternating
+        # over two streams (one op's copies overlap the other stream's GEMV), both synchronized
+        fn = lib.msq_matmul_host if mode == "sync" else lib.msq_matmul_host_async
+        streams = (stream, stream2) if mode == "two" else (stream,)
+        for i, (w, a, y) in enumerate(zip(reps[r], a_host, y_host)):
+            rc = fn(None, streams[i % len(streams)].cuda_stream, w.handle, a.data_ptr(), N.DT_F32, 1, y.data_ptr())
             if rc:
                 N.check(rc)
-        if asynchronous:
-            stream.synchronize()
+        if mode != "sync":
+            for s_ in streams:
+                s_.synchronize()
 
-    def time_e2e(asynchronous: bool) -> tuple[float, bool]:
+    def time_e2e(mode: str) -> tuple[float, bool]:
         for y in y_host:
             y.fill_(float("nan"))
         for i in range(max(args.warmup, 3)):
-            e2e_step(i % REPLICAS, asynchronous)
+            e2e_step(i % REPLICAS, mode)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for i in range(e2e_steps):
-            e2e_step(i % REPLICAS, asynchronous)
-        e1.record(stream)
+            e2e_step(i % REPLICAS, mode)
+        e1.record(stream)  # every step ended with the host waiting for both streams
         torch.cuda.synchronize(dev)
         t_ms = e0.elapsed_time(e1)
         if world > 1:
@@ -447,8 +453,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         ok = all(np.array_equal(y.numpy(), yc) for y, yc in zip(y_host, y_chk))
         return world * nbytes * e2e_steps / (t_ms * 1e-3) / 1e9, ok
 
-    e2e_value, e2e_ok = time_e2e(True)
-    e2e_sync_value, e2e_sync_ok = time_e2e(False)
+    e2e_value, e2e_ok = time_e2e("two")
+    e2e_one_value, e2e_one_ok = time_e2e("one")
+    e2e_sync_value, e2e_sync_ok = time_e2e("sync")
 
     # ---- parity spot check + CPU baseline (rank 0, N = 1)
     cpu = None
@@ -481,8 +488,12 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "steps": e2e_steps, "entry": "msq_matmul_host_async per op, one stream synchronize per step",
+                    "steps": e2e_steps,
+                    "entry": "msq_matmul_host_async per op, ops alternating over two streams, both synchronized "
+                             "per step",
                     "matches_device_run": e2e_ok,
+                    "one_stream": {"value": e2e_one_value, "entry": "msq_matmul_host_async per op, one stream "
+                                   "synchronize per step", "matches_device_run": e2e_one_ok},
                     "synchronous_entry": {"value": e2e_sync_value, "entry": "msq_matmul_host (synchronize per op)",
                                           "matches_device_run": e2e_sync_ok}},
             "gpu_launches": launches_per_step * args.steps,
